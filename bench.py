@@ -1,0 +1,543 @@
+"""Benchmark of the decode-step RoPE + KV-cache append path on B200.
+
+Default workload (N=1 and per GPU for N>1): `llama3_8b_decode32` -- a 32-layer Llama-3-8B-shaped
+decode step (batch 64 per GPU, 32 Q / 8 KV heads, head_dim 128, theta 5e5, bf16, per-layer
+caches [64, 8192, 8, 128] prefilled N(0, 1), int32 ragged positions including 0 and 8191),
+captured as one CUDA graph of 32 fused launches chained with programmatic dependent launch.
+A step is one replay. Inputs rotate over enough distinct input sets (q/k/v/positions/q_out)
+that their total exceeds 3x L2, so no step is served from L2.
+
+metric: achieved HBM GB/s per decode step = algorithmic bytes (reads of q, k, v and the rotary
+half-rows of cos/sin, writes of q_out and the K and V cache slots) / device time; value is the
+whole job's total over all ranks. us_per_step and us_per_call (per layer launch) are reported
+beside it.
+
+Launch: python bench.py [--gpus N --steps K --warmup W]; for N > 1 under torchrun, one rank per
+GPU, each owning its own batch shard and caches (weak scaling, no collective on the data path;
+NCCL only for the barrier and the max-over-ranks time).
+`--impl reference` times the reference's CPU algorithm (the CPU oracle port, all host threads)
+on the same workload and prints the same JSON line with impl=reference.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from decode_llm_kernel_b200.harness.configs import WORKLOADS, make_positions  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "achieved HBM GB/s per decode step (algorithmic bytes / device time), with us/call"
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", default="llama3_8b_decode32", choices=sorted(WORKLOADS))
+    p.add_argument("--no-pdl", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-bw-probe", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--seed", type=int, default=1234)
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------- distributed setup
+
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------- peaks and clocks
+
+def measured_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.samples = []
+        self._proc = None
+        self._thread = None
+
+    def start(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._proc = None
+            return self
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+        return self
+
+    def _read(self):
+        for line in self._proc.stdout:
+            self.samples.append((time.perf_counter(), line.strip()))
+
+    def stop(self):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self, t0, t1):
+        rows = [s for t, s in self.samples if t0 <= t <= t1] or [s for _, s in self.samples]
+        sm, sm_max, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for row in rows:
+            parts = [x.strip() for x in row.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": sm_max,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------- GPU state
+
+def build_tables(w, device):
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    return build_rope_tables(w.cache_alloc_len, w.rotary_dim or w.head_dim, w.theta,
+                             device=device)
+
+
+def normal_(t, g):
+    flat = t.view(-1)
+    step = 1 << 28
+    for start in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - start)
+        flat[start:start + n] = torch.randn(n, generator=g, device=t.device).to(t.dtype)
+    return t
+
+
+def build_step_state(w, device, seed, num_sets):
+    """Caches for every layer and `num_sets` distinct device input sets of one step."""
+    from decode_llm_kernel_b200.harness.decode_loop import StepInputs
+    g = torch.Generator(device=device).manual_seed(seed)
+    shape = (w.batch, w.cache_alloc_len, w.num_kv_heads, w.head_dim)
+    k_caches = [normal_(torch.empty(shape, dtype=w.dtype, device=device), g)
+                for _ in range(w.layers)]
+    v_caches = [normal_(torch.empty(shape, dtype=w.dtype, device=device), g)
+                for _ in range(w.layers)]
+    idx = torch.int32 if w.index_dtype == "int32" else torch.int64
+    sets = []
+    for i in range(num_sets):
+        L, T = w.layers, w.batch
+        sets.append(StepInputs(
+            normal_(torch.empty(L, T, w.num_q_heads, w.head_dim, dtype=w.dtype, device=device), g),
+            normal_(torch.empty(L, T, w.num_kv_heads, w.head_dim, dtype=w.dtype, device=device), g),
+            normal_(torch.empty(L, T, w.num_kv_heads, w.head_dim, dtype=w.dtype, device=device), g),
+            make_positions(w, seed + i, device),
+            torch.arange(T, device=device, dtype=idx)))
+    return k_caches, v_caches, sets
+
+
+def input_set_bytes(w):
+    return (w.layers * w.batch * (2 * w.num_q_heads + 2 * w.num_kv_heads) * w.head_dim
+            * w.elem_bytes)
+
+
+def sets_needed(w):
+    return max(4, min(64, -(-3 * L2_BYTES // max(1, input_set_bytes(w)))))
+
+
+def time_graph_steps(captured, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(steps):
+        captured[i % len(captured)].replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
+def bandwidth_probe(world, rank, device, seed, peak):
+    """The bandwidth-bound workload (mistral_b4096, sharded by batch): one fused launch per
+    call, 8 input sets rotated, device time per launch from CUDA events."""
+    from decode_llm_kernel_b200.cuda import ops
+    w = WORKLOADS["mistral_b4096"].shard_for(rank, world)
+    g = torch.Generator(device=device).manual_seed(seed + 17)
+    shape = (w.batch, w.cache_alloc_len, w.num_kv_heads, w.head_dim)
+    kc = normal_(torch.empty(shape, dtype=w.dtype, device=device), g)
+    vc = normal_(torch.empty(shape, dtype=w.dtype, device=device), g)
+    cos, sin = build_tables(w, device)
+    nsets = max(4, -(-3 * L2_BYTES // (w.bytes_per_call())))
+    idx = torch.int32
+    sets = []
+    for i in range(nsets):
+        sets.append((normal_(torch.empty(w.batch, w.num_q_heads, w.head_dim, dtype=w.dtype,
+                                         device=device), g),
+                     normal_(torch.empty(w.batch, w.num_kv_heads, w.head_dim, dtype=w.dtype,
+                                         device=device), g),
+                     normal_(torch.empty(w.batch, w.num_kv_heads, w.head_dim, dtype=w.dtype,
+                                         device=device), g),
+                     make_positions(w, seed + 100 + i, device),
+                     torch.arange(w.batch, device=device, dtype=idx),
+                     torch.empty(w.batch, w.num_q_heads, w.head_dim, dtype=w.dtype,
+                                 device=device)))
+
+    def call(i):
+        q, k, v, p, ri, qo = sets[i % nsets]
+        ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo)
+
+    for i in range(20):
+        call(i)
+    iters = 400
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(iters):
+        call(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    per_launch_s = ms / 1e3 / iters
+    gbs_rank = w.bytes_per_call() / per_launch_s / 1e9
+    out = {"workload": "mistral_b4096", "batch_per_gpu": w.batch, "dtype": w.dtype_label,
+           "bytes_per_launch": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
+           "achieved_gbs_per_gpu": gbs_rank, "frac_of_peak": gbs_rank / peak,
+           "aggregate_gbs": gbs_rank * world, "input_sets": nsets}
+    del kc, vc, sets
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args, world, rank, local):
+    from decode_llm_kernel_b200 import cuda
+    from decode_llm_kernel_b200.harness.decode_loop import DecodeStep, pinned_like
+    cuda.require()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = WORKLOADS[args.workload].shard_for(rank, world)
+    peak, peak_src = measured_hbm_peak()
+    cos, sin = build_tables(w, device)
+    nsets = sets_needed(w)
+    k_caches, v_caches, sets = build_step_state(w, device, args.seed + 7919 * rank, nsets)
+    step = DecodeStep(k_caches, v_caches, cos, sin, pdl=not args.no_pdl)
+    captured = [step.capture(s) for s in sets]
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+
+    sampler = ClockSampler(local).start()
+    time.sleep(0.3)
+    t_load0 = time.perf_counter()
+    for i in range(args.warmup):
+        captured[i % nsets].replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    t_timed0 = time.perf_counter()
+    ms = time_graph_steps(captured, args.steps, stream)
+    t_timed1 = time.perf_counter()
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    sampler.stop()
+    clocks = sampler.summary(t_timed0, t_timed1)
+    cuda.check_status(local)
+
+    per_step_s = ms_max / 1e3 / args.steps
+    bytes_step = w.bytes_per_step()
+    value = world * bytes_step / per_step_s / 1e9
+    per_launch_s = per_step_s / w.layers
+    achieved = w.bytes_per_call() / per_launch_s / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                "kernel": "drk::rope_kv_kernel<BF16, int, 16, kFused, kStrided>",
+                "per_launch_bytes": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
+                "note": "average launch = graph step time / layers, so it includes the gaps "
+                        "between the chained launches"}
+
+    # end to end: one graph per step that copies q/k/v/positions in from pinned host memory,
+    # runs the layers, and copies q_out back
+    e2e = None
+    if not args.no_e2e:
+        host = pinned_like(sets[0])
+        e2e_cap = step.capture(sets[0], host=host)
+        h2d = sum(t.numel() * t.element_size() for t in (host.q, host.k, host.v,
+                                                          host.positions, host.request_indices))
+        d2h = e2e_cap.host_q_out.numel() * e2e_cap.host_q_out.element_size()
+        for _ in range(max(3, args.warmup // 4)):
+            e2e_cap.replay()
+        torch.cuda.synchronize()
+        e2e_steps = max(10, min(args.steps, 400))
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_cap.replay()
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+        barrier(world)
+        e2e = {"value": world * bytes_step * e2e_steps / e2e_s / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "us_per_step": e2e_s / e2e_steps * 1e6, "steps": e2e_steps,
+               "path": "DecodeStep.capture(host=pinned): H2D copies + 32 fused launches + "
+                       "D2H copy in one graph, wall clock with a sync on both sides"}
+        e2e_cap.release()
+
+    floor = launch_floor(stream, w.layers)
+    del captured, sets, k_caches, v_caches
+    torch.cuda.empty_cache()
+    bw = None if args.no_bw_probe else bandwidth_probe(world, rank, device, args.seed, peak)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, args.seed, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step_s * 1e3,
+            "us_per_step": per_step_s * 1e6, "us_per_call": per_launch_s * 1e6,
+            "tokens_per_s": world * w.batch / per_step_s,
+            "frac_of_hbm_peak": value / world / peak,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": w.dtype_label,
+            "data": "synthetic (seeded N(0,1) q/k/v and caches, int32 positions)",
+            "config": dict(w.describe(), **{
+                "parallelism": f"batch shard x{world} (64 sequences and own caches per GPU)",
+                "global_batch": w.batch * world, "seq_len": w.cache_alloc_len,
+                "l2": f"inputs rotate over {nsets} distinct sets "
+                      f"({nsets * input_set_bytes(w) / 2**20:.0f} MiB > 3x L2)",
+                "pdl": not args.no_pdl}),
+            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": args.steps * w.layers, "launch_floor": floor,
+            "bandwidth_config": bw,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def launch_floor(stream, layers):
+    """Empty-kernel floor: direct launches (amortised) and a graph of `layers` chained empty
+    kernels, with and without programmatic dependent launch."""
+    from decode_llm_kernel_b200 import cuda
+    ext = cuda.require()
+    out = {}
+    for pdl in (False, True):
+        ext.launch_empty(50, pdl)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ext.launch_empty(2000, pdl)
+        torch.cuda.synchronize()
+        out[f"direct_us{'_pdl' if pdl else ''}"] = (time.perf_counter() - t0) / 2000 * 1e6
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            ext.launch_empty(1, pdl)
+        stream.wait_stream(side)
+        with torch.cuda.graph(g):
+            ext.launch_empty(layers, pdl)
+        for _ in range(20):
+            g.replay()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(500):
+            g.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        out[f"graph_us_per_node{'_pdl' if pdl else ''}"] = start.elapsed_time(end) * 1e3 / (500 * layers)
+    return out
+
+
+def cpu_baseline(w, seed, seconds):
+    """The CPU oracle (a port of the reference's PyTorch algorithm) on a bounded sample of the
+    workload: whole steps (every layer, every token) with caches cut to 64 positions per request
+    -- the op touches one slot per token, so per-token work is unchanged -- on all host
+    threads."""
+    from oracle import oracle
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    threads = os.cpu_count() or 1
+    S = 64
+    g = torch.Generator().manual_seed(seed)
+    L, T = w.layers, w.batch
+    q = torch.randn(L, T, w.num_q_heads, w.head_dim, generator=g).to(w.dtype)
+    k = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+    v = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+    kcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+           for _ in range(L)]
+    vcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+           for _ in range(L)]
+    cos, sin = build_rope_tables(S, w.rotary_dim or w.head_dim, w.theta)
+    pos = torch.randint(0, S, (T,), generator=g)
+    ri = torch.arange(T)
+
+    def one_step():
+        for layer in range(L):
+            oracle.fused_rope_kv_append(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer],
+                                        vcs[layer], ri, nthreads=threads)
+
+    one_step()
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        one_step()
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds or steps >= 100000:
+            break
+    per_step = elapsed / steps
+    return {"value": w.bytes_per_step() / per_step / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port", "ms_per_step": per_step * 1e3, "steps": steps,
+            "sample": f"{steps} whole {L}-layer steps of {T} tokens through the CPU oracle "
+                      f"(C, OpenMP, {threads} threads); caches cut to {S} positions per request "
+                      f"and positions drawn in [0, {S}), which leaves per-token work unchanged"}
+
+
+def run_reference(args, world, rank):
+    """The reference's algorithm on the host CPU (the oracle port, all threads), same workload,
+    metric and unit; rank 0 only."""
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    # size each timed step so K + W steps stay within about two minutes
+    probe = cpu_baseline(w, args.seed, 0.5)
+    per_step_s = probe["ms_per_step"] / 1e3
+    total = (args.steps + args.warmup) * per_step_s
+    if total > 120.0:
+        note = (f"; {args.steps} steps would take {total:.0f} s, so each timed step is "
+                f"{args.steps} x a 2-minute budget")
+    else:
+        note = ""
+    from oracle import oracle
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    threads = os.cpu_count() or 1
+    S = 64
+    g = torch.Generator().manual_seed(args.seed)
+    L, T = w.layers, w.batch
+    q = torch.randn(L, T, w.num_q_heads, w.head_dim, generator=g).to(w.dtype)
+    k = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+    v = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+    kcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+           for _ in range(L)]
+    vcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+           for _ in range(L)]
+    cos, sin = build_rope_tables(S, w.rotary_dim or w.head_dim, w.theta)
+    pos = torch.randint(0, S, (T,), generator=g)
+    ri = torch.arange(T)
+    layers_per_step = L
+    if total > 120.0:
+        layers_per_step = max(1, int(L * 120.0 / total))
+
+    def one_step():
+        for layer in range(layers_per_step):
+            oracle.fused_rope_kv_append(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer],
+                                        vcs[layer], ri, nthreads=threads)
+
+    for _ in range(args.warmup):
+        one_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+    elapsed = time.perf_counter() - t0
+    per = elapsed / args.steps
+    bytes_step = w.bytes_per_call() * layers_per_step
+    value = bytes_step / per / 1e9
+    sample = (f"{layers_per_step} of {L} layers x {T} tokens per step through the CPU oracle "
+              f"(C port of the reference's PyTorch algorithm, OpenMP, {threads} threads); "
+              f"caches cut to {S} positions per request{note}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per * 1e3 * (L / layers_per_step), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype_label,
+        "data": "synthetic (seeded N(0,1) q/k/v and caches)",
+        "config": dict(w.describe(), **{"parallelism": "host CPU, rank 0 only",
+                                        "global_batch": w.batch, "seq_len": w.cache_alloc_len}),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world, rank, local = init_dist(args)
+    if args.gpus != world and world > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            if dist.is_initialized():
+                dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

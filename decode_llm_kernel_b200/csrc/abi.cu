@@ -1,0 +1,675 @@
+// C ABI of libdecode_rope.so (include/decode_rope.h): argument checks, launch shape, dispatch.
+//
+// The checks, their order and their messages follow the reference's host launchers
+// (csrc/fused_rope_kv_append.cu:93-115, csrc/rope.cu:67-79, csrc/kv_append.cu:53-71) and
+// helpers (csrc/kernel_common.cuh:56-125), so a binding that raises the message reproduces the
+// reference's RuntimeErrors. Nothing here allocates, synchronises or reads device memory
+// (drk_build_info excepted, a diagnostic).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+
+#include "decode_rope.h"
+#include "rope_kv_launch.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local std::string g_status_text;
+
+struct InvalidArgument : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct Unsupported : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct CudaFailure : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+template <typename... A>
+std::string cat(const A&... a) {
+  std::ostringstream os;
+  (os << ... << a);
+  return os.str();
+}
+
+template <typename... A>
+[[noreturn]] void invalid(const A&... a) {
+  throw InvalidArgument(cat(a...));
+}
+
+const char* dtype_name(int32_t dt) {
+  switch (dt) {
+    case DRK_F32: return "Float";
+    case DRK_F16: return "Half";
+    case DRK_BF16: return "BFloat16";
+    case DRK_F64: return "Double";
+    case DRK_I32: return "Int";
+    case DRK_I64: return "Long";
+    default: return "Unknown";
+  }
+}
+
+std::string device_name(int32_t d) { return d < 0 ? std::string("cpu") : cat("cuda:", d); }
+
+std::string sizes_str(const drk_tensor* t) {
+  std::ostringstream os;
+  os << "[";
+  for (int i = 0; i < t->ndim; ++i) os << (i ? ", " : "") << t->sizes[i];
+  os << "]";
+  return os.str();
+}
+
+int64_t elem_size(int32_t dt) {
+  switch (dt) {
+    case DRK_F32: case DRK_I32: return 4;
+    case DRK_F16: case DRK_BF16: return 2;
+    case DRK_F64: case DRK_I64: return 8;
+    default: return 0;
+  }
+}
+
+bool is_float(int32_t dt) {
+  return dt == DRK_F32 || dt == DRK_F16 || dt == DRK_BF16 || dt == DRK_F64;
+}
+
+int64_t numel(const drk_tensor* t) {
+  int64_t n = 1;
+  for (int i = 0; i < t->ndim; ++i) n *= t->sizes[i];
+  return n;
+}
+
+// Row-major contiguity with PyTorch's rule: strides of size-1 dims do not matter.
+bool is_contiguous(const drk_tensor* t) {
+  if (numel(t) == 0) return true;
+  int64_t expected = 1;
+  for (int i = t->ndim - 1; i >= 0; --i) {
+    if (t->sizes[i] != 1 && t->strides[i] != expected) return false;
+    expected *= t->sizes[i];
+  }
+  return true;
+}
+
+void require(const drk_tensor* t, const char* name) {
+  if (t == nullptr) invalid(name, " is NULL");
+  if (t->ndim < 0 || t->ndim > 4) invalid(name, " has an unsupported number of dims ", t->ndim);
+}
+
+void check_device(const drk_tensor* t, const char* name, int32_t device) {
+  if (t->device < 0) invalid(name, " must be a CUDA tensor, got ", device_name(t->device));
+  if (t->device != device)
+    invalid(name, " is on ", device_name(t->device), " but the operation runs on ",
+            device_name(device), "; every tensor must be on one device");
+}
+
+// csrc/kernel_common.cuh:62-74, plus the partial-rotary extension.
+void check_rope_tables(const drk_tensor* cos, const drk_tensor* sin, int64_t head_dim,
+                       int32_t rotary_dim, int32_t device) {
+  require(cos, "cos");
+  require(sin, "sin");
+  check_device(cos, "cos", device);
+  check_device(sin, "sin", device);
+  if (cos->dtype != DRK_F32 || sin->dtype != DRK_F32)
+    invalid("cos/sin must be FP32 per the locked RoPE semantics, got ", dtype_name(cos->dtype),
+            "/", dtype_name(sin->dtype));
+  if (!is_contiguous(cos) || !is_contiguous(sin)) invalid("cos/sin must be contiguous");
+  if (cos->ndim != 2 || sin->ndim != 2) invalid("cos/sin must be [max_position, head_dim]");
+  if (rotary_dim == 0) {
+    if (cos->sizes[1] != head_dim || sin->sizes[1] != head_dim)
+      invalid("cos/sin head_dim ", cos->sizes[1], " does not match q/k head_dim ", head_dim);
+  } else if (cos->sizes[1] != rotary_dim || sin->sizes[1] != rotary_dim) {
+    invalid("cos/sin width ", cos->sizes[1], " does not match rotary_dim ", rotary_dim);
+  }
+  if (cos->sizes[0] != sin->sizes[0] || cos->sizes[1] != sin->sizes[1])
+    invalid("cos and sin must have the same shape");
+}
+
+// csrc/kernel_common.cuh:78-88
+void check_qkv(const drk_tensor* t, const char* name, int64_t num_tokens, int64_t head_dim,
+               int32_t device) {
+  require(t, name);
+  check_device(t, name, device);
+  if (t->ndim != 3)
+    invalid(name, " must be [num_tokens, num_heads, head_dim], got ", t->ndim, " dims");
+  if (t->sizes[0] != num_tokens)
+    invalid(name, " has ", t->sizes[0], " tokens, expected ", num_tokens);
+  if (t->sizes[2] != head_dim) invalid(name, " head_dim ", t->sizes[2], " expected ", head_dim);
+  if (t->strides[2] != 1)
+    invalid(name, " needs a contiguous head_dim (last-dim stride ", t->strides[2], ")");
+}
+
+// csrc/kernel_common.cuh:90-98
+void check_index_tensor(const drk_tensor* t, const char* name, int64_t num_tokens,
+                        int32_t device) {
+  require(t, name);
+  check_device(t, name, device);
+  if (t->dtype != DRK_I32 && t->dtype != DRK_I64)
+    invalid(name, " must be int32 or int64, got ", dtype_name(t->dtype));
+  if (t->ndim != 1 || t->sizes[0] != num_tokens)
+    invalid(name, " must be [num_tokens]; got ", sizes_str(t));
+  if (!is_contiguous(t)) invalid(name, " must be contiguous");
+}
+
+// csrc/kernel_common.cuh:100-114; DRK_FLAG_STRIDED_CACHE relaxes contiguity to a contiguous
+// last dim.
+void check_cache(const drk_tensor* cache, const char* name, int32_t like_dtype,
+                 int64_t num_kv_heads, int64_t head_dim, int32_t device, bool strided_ok) {
+  require(cache, name);
+  check_device(cache, name, device);
+  if (!strided_ok && !is_contiguous(cache)) invalid(name, " must be contiguous, token-major");
+  if (cache->ndim != 4)
+    invalid(name, " must be [batch, cache_alloc_len, num_kv_heads, head_dim], got ",
+            cache->ndim, " dims");
+  if (cache->sizes[2] != num_kv_heads || cache->sizes[3] != head_dim)
+    invalid(name, " kv-head/head_dim ", cache->sizes[2], "/", cache->sizes[3], " expected ",
+            num_kv_heads, "/", head_dim);
+  if (cache->dtype != like_dtype)
+    invalid(name, " dtype ", dtype_name(cache->dtype), " must match its source dtype ",
+            dtype_name(like_dtype));
+  if (strided_ok && numel(cache) != 0 && cache->strides[3] != 1)
+    invalid(name, " needs a contiguous head_dim (last-dim stride ", cache->strides[3], ")");
+}
+
+// csrc/kernel_common.cuh:116-125
+void check_caches_are_distinct(const drk_tensor* k_cache, const drk_tensor* v_cache) {
+  bool same_shape = k_cache->ndim == v_cache->ndim;
+  for (int i = 0; same_shape && i < k_cache->ndim; ++i)
+    same_shape = k_cache->sizes[i] == v_cache->sizes[i];
+  if (!same_shape) invalid("k_cache and v_cache must have the same shape");
+  if (numel(k_cache) != 0 && k_cache->data == v_cache->data)
+    invalid("k_cache and v_cache must be distinct buffers; sharing one makes the K and V "
+            "writes race for the same slot");
+  for (int i = 0; numel(k_cache) != 0 && i < k_cache->ndim; ++i)
+    if (k_cache->sizes[i] != 1 && k_cache->strides[i] != v_cache->strides[i])
+      invalid("k_cache and v_cache must have the same strides");
+}
+
+void check_output(const drk_tensor* t, const char* name, int32_t dtype, int64_t d0, int64_t d1,
+                  int64_t d2, int32_t device) {
+  require(t, name);
+  check_device(t, name, device);
+  if (t->dtype != dtype)
+    invalid(name, " dtype ", dtype_name(t->dtype), " must match its source dtype ",
+            dtype_name(dtype));
+  if (t->ndim != 3 || t->sizes[0] != d0 || t->sizes[1] != d1 || t->sizes[2] != d2 ||
+      !is_contiguous(t))
+    invalid(name, " must be a contiguous [", d0, ", ", d1, ", ", d2, "] tensor, got ",
+            sizes_str(t));
+}
+
+void check_float_dtype(int32_t dt, const char* op) {
+  if (!is_float(dt)) invalid("\"", op, "\" not implemented for '", dtype_name(dt), "'");
+}
+
+int32_t elem_code(int32_t dt) {
+  switch (dt) {
+    case DRK_F32: return drk::kElemF32;
+    case DRK_F16: return drk::kElemF16;
+    case DRK_BF16: return drk::kElemBF16;
+    default: return drk::kElemF64;
+  }
+}
+
+// Widest vector (bytes) such that every row segment a lane moves starts on a VB boundary.
+struct Aligner {
+  int64_t es;
+  int64_t R, D;
+  uintptr_t ptr_or = 0;    // OR of every base address
+  int64_t stride_or = 0;   // OR of every relevant element stride
+  void ptr(const void* p) { ptr_or |= reinterpret_cast<uintptr_t>(p); }
+  void stride(int64_t size, int64_t s) {
+    if (size > 1) stride_or |= s;
+  }
+  int pick() const {
+    for (int vb : {16, 8, 4, 2}) {
+      if (vb < es || vb % es) continue;
+      const int64_t vec = vb / es;
+      if ((R / 2) % vec || ((D - R) / 2) % vec || (D / 2) % vec) continue;
+      if (ptr_or % vb) continue;
+      if ((stride_or * es) % vb) continue;
+      return vb;
+    }
+    return 0;
+  }
+};
+
+struct Shape {
+  int vb;
+  int nslots, nrot, G, threads;
+};
+
+Shape plan(const Aligner& al, int nrows, bool rotates) {
+  Shape s{};
+  s.vb = al.pick();
+  if (s.vb == 0) throw Unsupported("tensors are not aligned to their element size");
+  const int64_t vec = s.vb / al.es;
+  const int64_t nslots = al.D / (2 * vec);
+  if (nslots > drk::kMaxThreadsPerBlock)
+    throw Unsupported(cat("head_dim ", al.D, " needs ", nslots,
+                          " lanes per row at this alignment; at most ",
+                          drk::kMaxThreadsPerBlock, " are supported"));
+  s.nslots = static_cast<int>(nslots);
+  s.nrot = rotates ? static_cast<int>(al.R / (2 * vec)) : 0;
+  // About three rows per thread; a block holds whole row groups.
+  const int want_groups = std::max(1, (nrows + 2) / 3);
+  s.G = std::max(1, std::min(want_groups, drk::kMaxThreadsPerBlock / s.nslots));
+  s.threads = s.G * s.nslots;
+  return s;
+}
+
+int grid_for(int64_t tokens) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tokens, 1 << 20)));
+}
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) throw CudaFailure("cudaGetDevice failed");
+    if (cur != device) {
+      if (cudaSetDevice(device) != cudaSuccess)
+        throw CudaFailure(cat("cudaSetDevice(", device, ") failed"));
+      prev_ = cur;
+    }
+  }
+  ~DeviceGuard() {
+    if (prev_ >= 0) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = -1;
+};
+
+void check_launch(cudaError_t err) {
+  if (err != cudaSuccess) throw CudaFailure(cat("kernel launch failed: ", cudaGetErrorString(err)));
+}
+
+template <typename F>
+int guarded(F&& body) {
+  try {
+    body();
+    g_last_error.clear();
+    return DRK_OK;
+  } catch (const InvalidArgument& e) {
+    g_last_error = e.what();
+    return DRK_ERR_INVALID;
+  } catch (const Unsupported& e) {
+    g_last_error = e.what();
+    return DRK_ERR_UNSUPPORTED;
+  } catch (const CudaFailure& e) {
+    g_last_error = e.what();
+    return DRK_ERR_CUDA;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return DRK_ERR_INVALID;
+  }
+}
+
+drk_options options_or_default(const drk_options* opts) {
+  drk_options o{};
+  if (opts) o = *opts;
+  return o;
+}
+
+int32_t resolve_rotary(const drk_options& o, int64_t head_dim) {
+  if (o.rotary_dim == 0) return 0;
+  if (o.rotary_dim < 0 || o.rotary_dim % 2 || o.rotary_dim > head_dim)
+    invalid("rotary_dim must be even and in (0, head_dim]; got ", o.rotary_dim, " for head_dim ",
+            head_dim);
+  return o.rotary_dim == head_dim ? 0 : o.rotary_dim;
+}
+
+void fill_table(drk::KernelParams& p, const drk_tensor* cos, const drk_tensor* sin,
+                const drk_options& o, int64_t R) {
+  p.cos_t = static_cast<const float*>(cos->data);
+  p.sin_t = static_cast<const float*>(sin->data);
+  p.table_rows = cos->sizes[0];
+  p.table_stride = cos->sizes[1];
+  p.table_vec4 = (reinterpret_cast<uintptr_t>(cos->data) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(sin->data) % 16 == 0 &&
+                  (p.table_stride * 4) % 16 == 0) ? 1 : 0;
+  if (o.flags & DRK_FLAG_INREG_TRIG) {
+    if (o.inv_freq == nullptr) invalid("DRK_FLAG_INREG_TRIG needs opts->inv_freq");
+    p.inv_freq = o.inv_freq;
+    p.inreg_trig = 1;
+  }
+  (void)R;
+}
+
+// The common body of the fused entry points (strided and paged caches).
+void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                const drk_tensor* positions, const drk_tensor* cos, const drk_tensor* sin,
+                const drk_tensor* k_cache, const drk_tensor* v_cache,
+                const drk_tensor* block_table, const drk_tensor* request_indices,
+                const drk_tensor* q_out, const drk_options* opts, uint32_t* status,
+                drk_stream_t stream) {
+  const drk_options o = options_or_default(opts);
+  const bool paged = block_table != nullptr;
+  require(q, "q");
+  if (q->ndim != 3) invalid("q must be [num_tokens, num_q_heads, head_dim]");
+  const int64_t T = q->sizes[0], Hq = q->sizes[1], D = q->sizes[2];
+  if (D % 2) invalid("head_dim must be even for split-half RoPE, got ", D);
+  const int32_t device = q->device;
+  check_qkv(q, "q", T, D, device);
+  check_qkv(k, "k", T, D, device);
+  check_qkv(v, "v", T, D, device);
+  const int64_t Hkv = k->sizes[1];
+  if (v->sizes[1] != Hkv) invalid("v has ", v->sizes[1], " kv heads, expected ", Hkv);
+  if (q->dtype != k->dtype || q->dtype != v->dtype) invalid("q, k and v must share a dtype");
+  check_index_tensor(positions, "positions", T, device);
+  check_index_tensor(request_indices, "request_indices", T, device);
+  if (positions->dtype != request_indices->dtype)
+    invalid("positions and request_indices must share a dtype, got ",
+            dtype_name(positions->dtype), "/", dtype_name(request_indices->dtype));
+  const int32_t rot = resolve_rotary(o, D);
+  check_rope_tables(cos, sin, D, rot, device);
+  const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0;
+  check_cache(k_cache, paged ? "k_pages" : "k_cache", k->dtype, Hkv, D, device,
+              strided_ok && !paged);
+  check_cache(v_cache, paged ? "v_pages" : "v_cache", v->dtype, Hkv, D, device,
+              strided_ok && !paged);
+  check_caches_are_distinct(k_cache, v_cache);
+  if (paged) {
+    require(block_table, "block_table");
+    check_device(block_table, "block_table", device);
+    if (block_table->dtype != positions->dtype)
+      invalid("block_table must share the index dtype of positions, got ",
+              dtype_name(block_table->dtype), "/", dtype_name(positions->dtype));
+    if (block_table->ndim != 2 || !is_contiguous(block_table))
+      invalid("block_table must be a contiguous [num_requests, max_blocks_per_request] tensor");
+    if (k_cache->sizes[1] <= 0 && numel(k_cache) != 0) invalid("block_size must be positive");
+  }
+  check_output(q_out, "q_out", q->dtype, T, Hq, D, device);
+  check_float_dtype(q->dtype, "fused_rope_kv_append");
+  if (T == 0) return;
+
+  const int64_t R = rot ? rot : D;
+  const int64_t es = elem_size(q->dtype);
+  drk::KernelParams p{};
+  p.q = static_cast<const char*>(q->data);
+  p.k = static_cast<const char*>(k->data);
+  p.v = static_cast<const char*>(v->data);
+  p.q_out = static_cast<char*>(q_out->data);
+  p.k_dst = static_cast<char*>(k_cache->data);
+  p.v_dst = static_cast<char*>(v_cache->data);
+  p.positions = positions->data;
+  p.request_indices = request_indices->data;
+  p.status = status;
+  p.T = T;
+  p.q_ts = q->strides[0]; p.q_hs = q->strides[1];
+  p.k_ts = k->strides[0]; p.k_hs = k->strides[1];
+  p.v_ts = v->strides[0]; p.v_hs = v->strides[1];
+  p.c_bs = k_cache->strides[0]; p.c_ss = k_cache->strides[1]; p.c_hs = k_cache->strides[2];
+  if (paged) {
+    p.block_table = block_table->data;
+    p.num_blocks = k_cache->sizes[0];
+    p.block_size = k_cache->sizes[1];
+    p.bt_stride = block_table->sizes[1];
+    p.B = block_table->sizes[0];
+    p.S = block_table->sizes[1] * k_cache->sizes[1];
+  } else {
+    p.B = k_cache->sizes[0];
+    p.S = k_cache->sizes[1];
+  }
+  p.Hq = static_cast<int32_t>(Hq);
+  p.Hkv = static_cast<int32_t>(Hkv);
+  p.D = static_cast<int32_t>(D);
+  p.R = static_cast<int32_t>(R);
+  fill_table(p, cos, sin, o, R);
+
+  Aligner al{es, R, D};
+  for (const drk_tensor* t : {q, k, v, q_out, k_cache, v_cache}) al.ptr(t->data);
+  al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
+  al.stride(T, k->strides[0]); al.stride(Hkv, k->strides[1]);
+  al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
+  for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
+  const int nrows = static_cast<int>(Hq + 2 * Hkv);
+  const Shape s = plan(al, nrows, true);
+  p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G;
+
+  DeviceGuard guard(device);
+  const drk::LaunchShape shape{grid_for(T), s.threads, (o.flags & DRK_FLAG_PDL) != 0};
+  const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+  check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeFused,
+                                   paged ? drk::kCachePaged : drk::kCacheStrided, shape,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // namespace
+
+extern "C" {
+
+int drk_fused_rope_kv_append(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                             const drk_tensor* positions, const drk_tensor* cos,
+                             const drk_tensor* sin, const drk_tensor* k_cache,
+                             const drk_tensor* v_cache, const drk_tensor* request_indices,
+                             const drk_tensor* q_out, uint32_t* status, drk_stream_t stream) {
+  return guarded([&] {
+    fused_impl(q, k, v, positions, cos, sin, k_cache, v_cache, nullptr, request_indices, q_out,
+               nullptr, status, stream);
+  });
+}
+
+int drk_fused_rope_kv_append_ex(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                                const drk_tensor* positions, const drk_tensor* cos,
+                                const drk_tensor* sin, const drk_tensor* k_cache,
+                                const drk_tensor* v_cache, const drk_tensor* request_indices,
+                                const drk_tensor* q_out, const drk_options* opts,
+                                uint32_t* status, drk_stream_t stream) {
+  return guarded([&] {
+    fused_impl(q, k, v, positions, cos, sin, k_cache, v_cache, nullptr, request_indices, q_out,
+               opts, status, stream);
+  });
+}
+
+int drk_paged_rope_kv_append(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                             const drk_tensor* positions, const drk_tensor* cos,
+                             const drk_tensor* sin, const drk_tensor* k_pages,
+                             const drk_tensor* v_pages, const drk_tensor* block_table,
+                             const drk_tensor* request_indices, const drk_tensor* q_out,
+                             const drk_options* opts, uint32_t* status, drk_stream_t stream) {
+  return guarded([&] {
+    if (block_table == nullptr) invalid("block_table is NULL");
+    fused_impl(q, k, v, positions, cos, sin, k_pages, v_pages, block_table, request_indices,
+               q_out, opts, status, stream);
+  });
+}
+
+int drk_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor* positions,
+                     const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* q_out,
+                     const drk_tensor* k_out, const drk_options* opts, uint32_t* status,
+                     drk_stream_t stream) {
+  return guarded([&] {
+    const drk_options o = options_or_default(opts);
+    require(q, "q");
+    if (q->ndim != 3) invalid("q must be [num_tokens, num_q_heads, head_dim]");
+    const int64_t T = q->sizes[0], Hq = q->sizes[1], D = q->sizes[2];
+    if (D % 2) invalid("head_dim must be even for split-half RoPE, got ", D);
+    const int32_t device = q->device;
+    check_qkv(q, "q", T, D, device);
+    check_qkv(k, "k", T, D, device);
+    if (q->dtype != k->dtype)
+      invalid("q and k must share a dtype, got ", dtype_name(q->dtype), "/",
+              dtype_name(k->dtype));
+    check_index_tensor(positions, "positions", T, device);
+    const int32_t rot = resolve_rotary(o, D);
+    check_rope_tables(cos, sin, D, rot, device);
+    const int64_t Hkv = k->sizes[1];
+    check_output(q_out, "q_out", q->dtype, T, Hq, D, device);
+    check_output(k_out, "k_out", k->dtype, T, Hkv, D, device);
+    check_float_dtype(q->dtype, "rope_forward");
+    if (T == 0) return;
+
+    const int64_t R = rot ? rot : D;
+    drk::KernelParams p{};
+    p.q = static_cast<const char*>(q->data);
+    p.k = static_cast<const char*>(k->data);
+    p.q_out = static_cast<char*>(q_out->data);
+    p.k_dst = static_cast<char*>(k_out->data);
+    p.positions = positions->data;
+    p.status = status;
+    p.T = T;
+    p.q_ts = q->strides[0]; p.q_hs = q->strides[1];
+    p.k_ts = k->strides[0]; p.k_hs = k->strides[1];
+    p.Hq = static_cast<int32_t>(Hq);
+    p.Hkv = static_cast<int32_t>(Hkv);
+    p.D = static_cast<int32_t>(D);
+    p.R = static_cast<int32_t>(R);
+    fill_table(p, cos, sin, o, R);
+    Aligner al{elem_size(q->dtype), R, D};
+    for (const drk_tensor* t : {q, k, q_out, k_out}) al.ptr(t->data);
+    al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
+    al.stride(T, k->strides[0]); al.stride(Hkv, k->strides[1]);
+    const Shape s = plan(al, static_cast<int>(Hq + Hkv), true);
+    p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G;
+    DeviceGuard guard(device);
+    const drk::LaunchShape shape{grid_for(T), s.threads, (o.flags & DRK_FLAG_PDL) != 0};
+    const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+    check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeRope,
+                                     drk::kCacheStrided, shape,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+  });
+}
+
+int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor* positions,
+                  const drk_tensor* request_indices, const drk_tensor* k_cache,
+                  const drk_tensor* v_cache, const drk_options* opts, uint32_t* status,
+                  drk_stream_t stream) {
+  return guarded([&] {
+    const drk_options o = options_or_default(opts);
+    require(k_rot, "k_rot");
+    if (k_rot->ndim != 3) invalid("k_rot must be [num_tokens, num_kv_heads, head_dim]");
+    const int64_t T = k_rot->sizes[0], Hkv = k_rot->sizes[1], D = k_rot->sizes[2];
+    const int32_t device = k_rot->device;
+    check_qkv(k_rot, "k_rot", T, D, device);
+    check_qkv(v, "v", T, D, device);
+    if (v->sizes[1] != Hkv) invalid("v has ", v->sizes[1], " kv heads, expected ", Hkv);
+    if (k_rot->dtype != v->dtype)
+      invalid("k_rot and v must share a dtype, got ", dtype_name(k_rot->dtype), "/",
+              dtype_name(v->dtype));
+    check_index_tensor(positions, "positions", T, device);
+    check_index_tensor(request_indices, "request_indices", T, device);
+    if (positions->dtype != request_indices->dtype)
+      invalid("positions and request_indices must share a dtype, got ",
+              dtype_name(positions->dtype), "/", dtype_name(request_indices->dtype));
+    const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0;
+    check_cache(k_cache, "k_cache", k_rot->dtype, Hkv, D, device, strided_ok);
+    check_cache(v_cache, "v_cache", v->dtype, Hkv, D, device, strided_ok);
+    check_caches_are_distinct(k_cache, v_cache);
+    check_float_dtype(k_rot->dtype, "kv_append");
+    if (T == 0) return;
+    if (D % 2)
+      throw Unsupported(cat("kv_append needs an even head_dim, got ", D));
+
+    drk::KernelParams p{};
+    p.k = static_cast<const char*>(k_rot->data);
+    p.v = static_cast<const char*>(v->data);
+    p.k_dst = static_cast<char*>(k_cache->data);
+    p.v_dst = static_cast<char*>(v_cache->data);
+    p.positions = positions->data;
+    p.request_indices = request_indices->data;
+    p.status = status;
+    p.T = T;
+    p.k_ts = k_rot->strides[0]; p.k_hs = k_rot->strides[1];
+    p.v_ts = v->strides[0]; p.v_hs = v->strides[1];
+    p.c_bs = k_cache->strides[0]; p.c_ss = k_cache->strides[1]; p.c_hs = k_cache->strides[2];
+    p.B = k_cache->sizes[0];
+    p.S = k_cache->sizes[1];
+    p.Hkv = static_cast<int32_t>(Hkv);
+    p.D = static_cast<int32_t>(D);
+    p.R = 0;
+    p.table_rows = INT64_MAX;
+    Aligner al{elem_size(k_rot->dtype), 0, D};
+    for (const drk_tensor* t : {k_rot, v, k_cache, v_cache}) al.ptr(t->data);
+    al.stride(T, k_rot->strides[0]); al.stride(Hkv, k_rot->strides[1]);
+    al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
+    for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
+    const Shape s = plan(al, static_cast<int>(2 * Hkv), false);
+    p.nslots = s.nslots; p.nrot = 0; p.G = s.G;
+    DeviceGuard guard(device);
+    const drk::LaunchShape shape{grid_for(T), s.threads, (o.flags & DRK_FLAG_PDL) != 0};
+    const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+    check_launch(drk::launch_rope_kv(p, elem_code(k_rot->dtype), index_bits, s.vb,
+                                     drk::kModeAppend, drk::kCacheStrided, shape,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+  });
+}
+
+int drk_smoke_fill(const drk_tensor* tensor, double value, drk_stream_t stream) {
+  return guarded([&] {
+    require(tensor, "tensor");
+    if (tensor->device < 0)
+      invalid("smoke_fill expects a CUDA tensor, got ", device_name(tensor->device));
+    if (!is_contiguous(tensor)) invalid("smoke_fill expects a contiguous tensor");
+    check_float_dtype(tensor->dtype, "smoke_fill");
+    const int64_t n = numel(tensor);
+    if (n == 0) return;
+    DeviceGuard guard(tensor->device);
+    check_launch(drk::launch_smoke_fill(tensor->data, elem_code(tensor->dtype), n, value,
+                                        reinterpret_cast<cudaStream_t>(stream)));
+  });
+}
+
+int drk_build_info(char* buf, size_t len, drk_stream_t stream) {
+  return guarded([&] {
+    if (buf == nullptr || len == 0) invalid("buf is NULL or empty");
+    int arch = 0, runtime = 0, driver = 0;
+    cudaError_t err = drk::run_arch_probe(&arch, reinterpret_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) throw CudaFailure(cat("arch probe failed: ", cudaGetErrorString(err)));
+    cudaRuntimeGetVersion(&runtime);
+    cudaDriverGetVersion(&driver);
+    auto ver = [](int packed) {
+      return packed <= 0 ? std::string() : cat(packed / 1000, ".", (packed % 1000) / 10);
+    };
+#if defined(__FAST_MATH__) || defined(__USE_FAST_MATH__)
+    const char* fast_math = "1";
+#else
+    const char* fast_math = "0";
+#endif
+    const std::string text =
+        cat("gencode_arch=", arch, "\ncuda_version_compiled=", ver(CUDART_VERSION),
+            "\ncuda_version_runtime=", ver(runtime), "\ncuda_version_driver=", ver(driver),
+            "\nnvcc_version=", __CUDACC_VER_MAJOR__, ".", __CUDACC_VER_MINOR__, ".",
+            __CUDACC_VER_BUILD__, "\nfast_math=", fast_math, "\n");
+    if (text.size() + 1 > len) invalid("buf too small: need ", text.size() + 1, " bytes");
+    std::memcpy(buf, text.c_str(), text.size() + 1);
+  });
+}
+
+int drk_launch_empty(int count, int pdl, drk_stream_t stream) {
+  return guarded([&] {
+    if (count < 0) invalid("count must be >= 0");
+    check_launch(drk::launch_empty(count, pdl != 0, reinterpret_cast<cudaStream_t>(stream)));
+  });
+}
+
+const char* drk_last_error(void) { return g_last_error.c_str(); }
+
+const char* drk_status_string(uint32_t status) {
+  if (status == 0) {
+    g_status_text = "ok";
+    return g_status_text.c_str();
+  }
+  std::string s;
+  auto add = [&](uint32_t bit, const char* text) {
+    if (status & bit) s += (s.empty() ? "" : "; ") + std::string(text);
+  };
+  add(DRK_STATUS_POSITION_OUT_OF_CACHE, "a position was outside [0, cache_alloc_len)");
+  add(DRK_STATUS_REQUEST_OUT_OF_RANGE, "a request index was outside [0, batch)");
+  add(DRK_STATUS_POSITION_OUT_OF_TABLE, "a position was outside the cos/sin table");
+  add(DRK_STATUS_BLOCK_OUT_OF_RANGE, "a block-table entry was outside the page pool");
+  if (status & ~0xFu) s += (s.empty() ? "" : "; ") + cat("unknown bits 0x", std::hex, status);
+  g_status_text = s;
+  return g_status_text.c_str();
+}
+
+const char* drk_version(void) { return "0.1.0"; }
+
+}  // extern "C"

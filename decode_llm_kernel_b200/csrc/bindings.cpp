@@ -1,0 +1,320 @@
+// PyTorch binding over the C ABI (include/decode_rope.h): the drop-in for the reference's
+// decode_kernels.cuda._ext module (csrc/bindings.cpp:18-34 of the reference), with the same
+// function names, keyword names, return types and error messages.
+//
+// The binding owns what the C ABI leaves to its caller: it allocates outputs through PyTorch's
+// caching allocator (so calls stay graph-capturable), launches on the current stream of the
+// inputs' device, and keeps one status word per device for the kernels' bounds reports.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "decode_rope.h"
+
+namespace {
+
+int32_t dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return DRK_F32;
+    case at::kHalf: return DRK_F16;
+    case at::kBFloat16: return DRK_BF16;
+    case at::kDouble: return DRK_F64;
+    case at::kInt: return DRK_I32;
+    case at::kLong: return DRK_I64;
+    default: return -1;
+  }
+}
+
+drk_tensor describe(const at::Tensor& t) {
+  drk_tensor d{};
+  d.data = t.data_ptr();
+  d.dtype = dtype_code(t.scalar_type());
+  d.ndim = static_cast<int32_t>(std::min<int64_t>(t.dim(), 4));
+  d.device = t.is_cuda() ? t.get_device() : -1;
+  for (int i = 0; i < d.ndim; ++i) {
+    d.sizes[i] = t.size(i);
+    d.strides[i] = t.stride(i);
+  }
+  if (t.dim() > 4) d.ndim = static_cast<int32_t>(t.dim());  // rejected by the ABI's checks
+  return d;
+}
+
+void raise_on_error(int rc) {
+  if (rc == DRK_OK) return;
+  TORCH_CHECK(false, drk_last_error());
+}
+
+cudaStream_t stream_for(const at::Tensor& t) {
+  if (!t.is_cuda()) return nullptr;
+  return at::cuda::getCurrentCUDAStream(t.get_device()).stream();
+}
+
+// One zero-initialised uint32 per device, allocated outside any stream capture's view (relaxed
+// capture mode) so the first call may happen while a graph is being captured.
+std::mutex g_status_mutex;
+std::map<int, uint32_t*> g_status;
+
+uint32_t* status_word(int device) {
+  std::lock_guard<std::mutex> lock(g_status_mutex);
+  auto it = g_status.find(device);
+  if (it != g_status.end()) return it->second;
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  uint32_t* ptr = nullptr;
+  cudaError_t err = cudaMalloc(&ptr, sizeof(uint32_t));
+  cudaStream_t side = nullptr;
+  if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking);
+  if (err == cudaSuccess) err = cudaMemsetAsync(ptr, 0, sizeof(uint32_t), side);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(side);
+  if (side) cudaStreamDestroy(side);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  TORCH_CHECK(err == cudaSuccess, "could not allocate the status word: ",
+              cudaGetErrorString(err));
+  g_status[device] = ptr;
+  return ptr;
+}
+
+uint32_t* status_for(const at::Tensor& t) {
+  return t.is_cuda() ? status_word(t.get_device()) : nullptr;
+}
+
+drk_options make_options(uint32_t flags, int64_t rotary_dim, const c10::optional<at::Tensor>& inv_freq) {
+  drk_options o{};
+  o.flags = flags;
+  o.rotary_dim = static_cast<int32_t>(rotary_dim);
+  if (inv_freq.has_value() && inv_freq->defined()) {
+    TORCH_CHECK(inv_freq->is_cuda() && inv_freq->scalar_type() == at::kFloat &&
+                    inv_freq->is_contiguous(),
+                "inv_freq must be a contiguous fp32 CUDA tensor");
+    o.inv_freq = inv_freq->data_ptr<float>();
+    o.flags |= DRK_FLAG_INREG_TRIG;
+  }
+  return o;
+}
+
+at::Tensor empty_like_rows(const at::Tensor& src, int64_t heads) {
+  return at::empty({src.size(0), heads, src.size(2)}, src.options());
+}
+
+// ---- the reference's five functions ----
+
+at::Tensor fused_rope_kv_append(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor positions,
+                                at::Tensor cos, at::Tensor sin, at::Tensor k_cache,
+                                at::Tensor v_cache, at::Tensor request_indices) {
+  at::Tensor q_out;
+  if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
+  const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
+                   dp = describe(positions), dc = describe(cos), ds = describe(sin),
+                   dkc = describe(k_cache), dvc = describe(v_cache),
+                   dri = describe(request_indices);
+  drk_tensor dqo{};
+  if (q_out.defined()) dqo = describe(q_out);
+  raise_on_error(drk_fused_rope_kv_append(&dq, &dk, &dv, &dp, &dc, &ds, &dkc, &dvc, &dri,
+                                          q_out.defined() ? &dqo : nullptr, status_for(q),
+                                          stream_for(q)));
+  return q_out;
+}
+
+std::tuple<at::Tensor, at::Tensor> rope_forward(at::Tensor q, at::Tensor k, at::Tensor positions,
+                                                at::Tensor cos, at::Tensor sin) {
+  at::Tensor q_out, k_out;
+  if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
+  if (k.dim() == 3) k_out = empty_like_rows(k, k.size(1));
+  const drk_tensor dq = describe(q), dk = describe(k), dp = describe(positions),
+                   dc = describe(cos), ds = describe(sin);
+  drk_tensor dqo{}, dko{};
+  if (q_out.defined()) dqo = describe(q_out);
+  if (k_out.defined()) dko = describe(k_out);
+  raise_on_error(drk_rope_forward(&dq, &dk, &dp, &dc, &ds, q_out.defined() ? &dqo : nullptr,
+                                  k_out.defined() ? &dko : nullptr, nullptr, status_for(q),
+                                  stream_for(q)));
+  return {q_out, k_out};
+}
+
+void kv_append(at::Tensor k_rot, at::Tensor v, at::Tensor positions, at::Tensor request_indices,
+               at::Tensor k_cache, at::Tensor v_cache) {
+  const drk_tensor dk = describe(k_rot), dv = describe(v), dp = describe(positions),
+                   dri = describe(request_indices), dkc = describe(k_cache),
+                   dvc = describe(v_cache);
+  raise_on_error(drk_kv_append(&dk, &dv, &dp, &dri, &dkc, &dvc, nullptr, status_for(k_rot),
+                               stream_for(k_rot)));
+}
+
+void smoke_fill(at::Tensor tensor, double value) {
+  const drk_tensor d = describe(tensor);
+  raise_on_error(drk_smoke_fill(&d, value, stream_for(tensor)));
+}
+
+std::map<std::string, std::string> build_info() {
+  const int device = c10::cuda::current_device();
+  char buf[1024];
+  raise_on_error(drk_build_info(buf, sizeof(buf), at::cuda::getCurrentCUDAStream(device).stream()));
+  std::map<std::string, std::string> info;
+  std::string text(buf);
+  size_t start = 0;
+  while (start < text.size()) {
+    size_t end = text.find('\n', start);
+    if (end == std::string::npos) end = text.size();
+    const std::string line = text.substr(start, end - start);
+    const size_t eq = line.find('=');
+    if (eq != std::string::npos) info[line.substr(0, eq)] = line.substr(eq + 1);
+    start = end + 1;
+  }
+  return info;
+}
+
+// ---- extensions (no counterpart in the reference's binding) ----
+
+at::Tensor fused_rope_kv_append_ex(at::Tensor q, at::Tensor k, at::Tensor v,
+                                   at::Tensor positions, at::Tensor cos, at::Tensor sin,
+                                   at::Tensor k_cache, at::Tensor v_cache,
+                                   at::Tensor request_indices, int64_t rotary_dim, bool pdl,
+                                   bool strided_cache, c10::optional<at::Tensor> inv_freq,
+                                   c10::optional<at::Tensor> q_out_opt) {
+  at::Tensor q_out;
+  if (q_out_opt.has_value() && q_out_opt->defined()) q_out = *q_out_opt;
+  else if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
+  const drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
+                                         (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
+                                     rotary_dim, inv_freq);
+  const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
+                   dp = describe(positions), dc = describe(cos), ds = describe(sin),
+                   dkc = describe(k_cache), dvc = describe(v_cache),
+                   dri = describe(request_indices);
+  drk_tensor dqo{};
+  if (q_out.defined()) dqo = describe(q_out);
+  raise_on_error(drk_fused_rope_kv_append_ex(&dq, &dk, &dv, &dp, &dc, &ds, &dkc, &dvc, &dri,
+                                             q_out.defined() ? &dqo : nullptr, &o,
+                                             status_for(q), stream_for(q)));
+  return q_out;
+}
+
+at::Tensor paged_rope_kv_append(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor positions,
+                                at::Tensor cos, at::Tensor sin, at::Tensor k_pages,
+                                at::Tensor v_pages, at::Tensor block_table,
+                                at::Tensor request_indices, int64_t rotary_dim, bool pdl) {
+  at::Tensor q_out;
+  if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
+  const drk_options o = make_options(pdl ? DRK_FLAG_PDL : 0u, rotary_dim, c10::nullopt);
+  const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
+                   dp = describe(positions), dc = describe(cos), ds = describe(sin),
+                   dkp = describe(k_pages), dvp = describe(v_pages), dbt = describe(block_table),
+                   dri = describe(request_indices);
+  drk_tensor dqo{};
+  if (q_out.defined()) dqo = describe(q_out);
+  raise_on_error(drk_paged_rope_kv_append(&dq, &dk, &dv, &dp, &dc, &ds, &dkp, &dvp, &dbt, &dri,
+                                          q_out.defined() ? &dqo : nullptr, &o, status_for(q),
+                                          stream_for(q)));
+  return q_out;
+}
+
+std::tuple<at::Tensor, at::Tensor> rope_forward_ex(at::Tensor q, at::Tensor k,
+                                                   at::Tensor positions, at::Tensor cos,
+                                                   at::Tensor sin, int64_t rotary_dim,
+                                                   bool pdl) {
+  at::Tensor q_out, k_out;
+  if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
+  if (k.dim() == 3) k_out = empty_like_rows(k, k.size(1));
+  const drk_options o = make_options(pdl ? DRK_FLAG_PDL : 0u, rotary_dim, c10::nullopt);
+  const drk_tensor dq = describe(q), dk = describe(k), dp = describe(positions),
+                   dc = describe(cos), ds = describe(sin);
+  drk_tensor dqo{}, dko{};
+  if (q_out.defined()) dqo = describe(q_out);
+  if (k_out.defined()) dko = describe(k_out);
+  raise_on_error(drk_rope_forward(&dq, &dk, &dp, &dc, &ds, q_out.defined() ? &dqo : nullptr,
+                                  k_out.defined() ? &dko : nullptr, &o, status_for(q),
+                                  stream_for(q)));
+  return {q_out, k_out};
+}
+
+void kv_append_ex(at::Tensor k_rot, at::Tensor v, at::Tensor positions,
+                  at::Tensor request_indices, at::Tensor k_cache, at::Tensor v_cache, bool pdl,
+                  bool strided_cache) {
+  const drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
+                                         (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
+                                     0, c10::nullopt);
+  const drk_tensor dk = describe(k_rot), dv = describe(v), dp = describe(positions),
+                   dri = describe(request_indices), dkc = describe(k_cache),
+                   dvc = describe(v_cache);
+  raise_on_error(drk_kv_append(&dk, &dv, &dp, &dri, &dkc, &dvc, &o, status_for(k_rot),
+                               stream_for(k_rot)));
+}
+
+// Reads (and by default clears) the device's status word. Synchronises the current stream:
+// call it outside timed regions.
+int64_t read_status(int64_t device, bool clear) {
+  uint32_t* word = status_word(static_cast<int>(device));
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(static_cast<c10::DeviceIndex>(device));
+  uint32_t host = 0;
+  cudaError_t err = cudaMemcpyAsync(&host, word, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+  if (err == cudaSuccess && clear) {
+    err = cudaMemsetAsync(word, 0, sizeof(uint32_t), stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+  }
+  TORCH_CHECK(err == cudaSuccess, "reading the status word failed: ", cudaGetErrorString(err));
+  return static_cast<int64_t>(host);
+}
+
+int64_t status_address(int64_t device) {
+  return static_cast<int64_t>(reinterpret_cast<uintptr_t>(status_word(static_cast<int>(device))));
+}
+
+std::string status_string(int64_t status) {
+  return drk_status_string(static_cast<uint32_t>(status));
+}
+
+void launch_empty(int64_t count, bool pdl) {
+  const int device = c10::cuda::current_device();
+  raise_on_error(drk_launch_empty(static_cast<int>(count), pdl ? 1 : 0,
+                                  at::cuda::getCurrentCUDAStream(device).stream()));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("smoke_fill", &smoke_fill, py::arg("tensor"), py::arg("value"),
+        "Fill a contiguous CUDA tensor in place; exercises launch + dtype dispatch.");
+  m.def("build_info", &build_info, "Compile-time and runtime facts about this binary.");
+  m.def("rope_forward", &rope_forward, py::arg("q"), py::arg("k"), py::arg("positions"),
+        py::arg("cos"), py::arg("sin"),
+        "Split-half RoPE over strided Q and K in one launch; returns (q_rot, k_rot).");
+  m.def("kv_append", &kv_append, py::arg("k_rot"), py::arg("v"), py::arg("positions"),
+        py::arg("request_indices"), py::arg("k_cache"), py::arg("v_cache"),
+        "Scatter rotated K and raw V into a contiguous token-major cache, in place.");
+  m.def("fused_rope_kv_append", &fused_rope_kv_append, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("request_indices"),
+        "Rotate Q and K and append K/V to the cache in one launch; returns q_rot.");
+
+  m.def("fused_rope_kv_append_ex", &fused_rope_kv_append_ex, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("request_indices"), py::arg("rotary_dim") = 0,
+        py::arg("pdl") = false, py::arg("strided_cache") = false,
+        py::arg("inv_freq") = py::none(), py::arg("q_out") = py::none(),
+        "fused_rope_kv_append with partial rotary, PDL, strided caches, in-register trig.");
+  m.def("paged_rope_kv_append", &paged_rope_kv_append, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_pages"),
+        py::arg("v_pages"), py::arg("block_table"), py::arg("request_indices"),
+        py::arg("rotary_dim") = 0, py::arg("pdl") = false,
+        "Fused RoPE + append into a paged (block-table) KV cache; returns q_rot.");
+  m.def("rope_forward_ex", &rope_forward_ex, py::arg("q"), py::arg("k"), py::arg("positions"),
+        py::arg("cos"), py::arg("sin"), py::arg("rotary_dim") = 0, py::arg("pdl") = false);
+  m.def("kv_append_ex", &kv_append_ex, py::arg("k_rot"), py::arg("v"), py::arg("positions"),
+        py::arg("request_indices"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("pdl") = false, py::arg("strided_cache") = false);
+  m.def("read_status", &read_status, py::arg("device"), py::arg("clear") = true);
+  m.def("status_address", &status_address, py::arg("device"));
+  m.def("status_string", &status_string, py::arg("status"));
+  m.def("launch_empty", &launch_empty, py::arg("count"), py::arg("pdl") = false);
+}

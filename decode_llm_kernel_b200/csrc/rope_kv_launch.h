@@ -1,0 +1,57 @@
+// Host-visible launch interface between the C ABI layer (abi.cpp) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace drk {
+
+// Threads per block the kernels are compiled for (__launch_bounds__).
+constexpr int kMaxThreadsPerBlock = 256;
+
+struct KernelParams {
+  const char* q;              // Q (fused/rope)
+  const char* k;              // K (fused/rope) or k_rot (append)
+  const char* v;              // V (fused/append)
+  char* q_out;                // contiguous [T, Hq, D]
+  char* k_dst;                // k cache, or contiguous k_out [T, Hkv, D] in rope mode
+  char* v_dst;                // v cache
+  const float* cos_t;
+  const float* sin_t;
+  const float* inv_freq;      // in-register trig only
+  const void* positions;
+  const void* request_indices;
+  const void* block_table;    // paged only
+  uint32_t* status;           // may be null
+  int64_t T;
+  int64_t q_ts, q_hs, k_ts, k_hs, v_ts, v_hs;  // element strides of the sources
+  int64_t c_bs, c_ss, c_hs;   // cache element strides: batch (paged: block), position, head
+  int64_t B, S;               // cache rows and positions (paged: requests, max positions)
+  int64_t num_blocks, block_size, bt_stride;
+  int64_t table_rows, table_stride;
+  int32_t Hq, Hkv, D, R;
+  int32_t nslots, nrot, G;
+  int32_t inreg_trig;
+  int32_t table_vec4;         // table base and row stride allow 16-byte loads
+};
+
+enum { kElemF32 = 0, kElemF16 = 1, kElemBF16 = 2, kElemF64 = 3 };
+enum { kModeFused = 0, kModeRope = 1, kModeAppend = 2 };
+enum { kCacheStrided = 0, kCachePaged = 1 };
+
+struct LaunchShape {
+  int grid;
+  int threads;
+  bool pdl;
+};
+
+cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits, int vb,
+                           int mode, int cache, const LaunchShape& shape, cudaStream_t stream);
+
+// smoke.cu
+cudaError_t launch_smoke_fill(void* data, int elem_code, int64_t numel, double value,
+                              cudaStream_t stream);
+cudaError_t run_arch_probe(int* arch_out, cudaStream_t stream);
+cudaError_t launch_empty(int count, bool pdl, cudaStream_t stream);
+
+}  // namespace drk

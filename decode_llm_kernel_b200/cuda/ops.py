@@ -1,0 +1,75 @@
+"""The RoPE + KV-append ops, behind the reference's own signatures
+(decode_kernels/cuda/ops.py:15-43 of the reference).
+
+Nothing here synchronises, reads device memory on the host, or allocates outside PyTorch's
+caching allocator, so every op can be timed at microsecond scale and captured into a CUDA
+graph. Out-of-range positions or request indices do not trap: the kernel skips those writes and
+records them in a status word that `decode_llm_kernel_b200.cuda.check_status()` reads.
+"""
+from . import require
+
+
+def rope_forward(q, k, positions, cos, sin):
+    """Split-half RoPE over strided Q and K in one launch. Returns (q_rot, k_rot)."""
+    return require().rope_forward(q, k, positions, cos, sin)
+
+
+def kv_append(k_rot, v, positions, request_indices, k_cache, v_cache):
+    """Scatter rotated K and raw V into their cache slots, in place."""
+    require().kv_append(k_rot, v, positions, request_indices, k_cache, v_cache)
+
+
+def separate_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices):
+    """RoPE kernel then append kernel, with `k_rot` materialised between them: two launches and
+    one intermediate, the ablation the fused op is measured against."""
+    q_rot, k_rot = rope_forward(q, k, positions, cos, sin)
+    kv_append(k_rot, v, positions, request_indices, k_cache, v_cache)
+    return q_rot
+
+
+def fused_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices):
+    """One launch: rotate Q into a fresh q_rot, rotate K straight into its cache slot, copy V."""
+    return require().fused_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache,
+                                          request_indices)
+
+
+# ---- extensions beyond the reference's surface ----
+
+def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
+                            *, rotary_dim=0, pdl=False, strided_cache=False, inv_freq=None,
+                            q_out=None):
+    """fused_rope_kv_append with:
+    rotary_dim     rotate only the first rotary_dim dims (table [P, rotary_dim]), copy the rest;
+    pdl            programmatic dependent launch (indices and table read before waiting on the
+                   preceding kernel -- the caller guarantees that kernel does not write them);
+    strided_cache  caches of any strides with a contiguous last dim, e.g. a head-major
+                   [B, Hkv, S, D] cache passed as cache.transpose(1, 2);
+    inv_freq       fp32 [rotary_dim/2] device tensor: cos/sin from sincosf in registers
+                   (within 1 ulp of the table path, not bit-exact);
+    q_out          write into this contiguous [T, Hq, D] tensor instead of a fresh one."""
+    return require().fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache,
+                                             request_indices, rotary_dim, pdl, strided_cache,
+                                             inv_freq, q_out)
+
+
+def paged_rope_kv_append(q, k, v, positions, cos, sin, k_pages, v_pages, block_table,
+                         request_indices, *, rotary_dim=0, pdl=False):
+    """Fused RoPE + append into a paged cache: k_pages/v_pages [num_blocks, block_size, Hkv, D],
+    block_table [num_requests, max_blocks] (positions' dtype). Token t goes to block
+    block_table[ri[t], pos[t] // block_size], row pos[t] % block_size. Returns q_rot."""
+    return require().paged_rope_kv_append(q, k, v, positions, cos, sin, k_pages, v_pages,
+                                          block_table, request_indices, rotary_dim, pdl)
+
+
+def rope_forward_ex(q, k, positions, cos, sin, *, rotary_dim=0, pdl=False):
+    return require().rope_forward_ex(q, k, positions, cos, sin, rotary_dim, pdl)
+
+
+def kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, *, pdl=False,
+                 strided_cache=False):
+    require().kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, pdl,
+                           strided_cache)
+
+
+__all__ = ["fused_rope_kv_append", "fused_rope_kv_append_ex", "kv_append", "kv_append_ex",
+           "paged_rope_kv_append", "rope_forward", "rope_forward_ex", "separate_rope_kv_append"]

@@ -1,0 +1,191 @@
+/*
+ * decode_rope.h -- C ABI of the B200 (sm_100a) decode-step RoPE + KV-cache append library,
+ * libdecode_rope.so.
+ *
+ * Every entry point takes plain tensor descriptors (a data pointer, a dtype code, sizes and
+ * element strides), an optional device status word and a CUDA stream. No entry point
+ * allocates device memory, synchronises the stream or reads device memory on the host, except
+ * drk_build_info, which is a diagnostic. Return value: DRK_OK, or a negative DRK_ERR_* code
+ * with a message available from drk_last_error() on the same thread.
+ *
+ * The argument checks and their messages follow the reference's host checks
+ * (csrc/kernel_common.cuh:56-125 and csrc/fused_rope_kv_append.cu:93-115 of the reference
+ * project), so a binding that raises the message reproduces the reference's errors.
+ *
+ * Out-of-range positions or request indices do not trap (the reference uses a device assert,
+ * csrc/kernel_common.cuh:38-51, which ends the CUDA context): the kernel skips that token's
+ * cache writes and ORs a DRK_STATUS_* bit into *status when status is not NULL. The caller
+ * reads the word when it chooses to (outside any timed region).
+ */
+#ifndef DECODE_ROPE_H_
+#define DECODE_ROPE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DRK_API __attribute__((visibility("default")))
+#else
+#define DRK_API
+#endif
+
+/* Same object as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* drk_stream_t;
+
+/* Element type codes. */
+enum {
+  DRK_F32 = 0,
+  DRK_F16 = 1,
+  DRK_BF16 = 2,
+  DRK_F64 = 3,
+  DRK_I32 = 4,
+  DRK_I64 = 5
+};
+
+/* Return codes. */
+enum {
+  DRK_OK = 0,
+  DRK_ERR_INVALID = -1,     /* an argument check failed; see drk_last_error() */
+  DRK_ERR_CUDA = -2,        /* a CUDA runtime call failed; see drk_last_error() */
+  DRK_ERR_UNSUPPORTED = -3  /* a dtype or layout this build has no kernel for */
+};
+
+/* Bits a kernel ORs into the optional status word. */
+enum {
+  DRK_STATUS_POSITION_OUT_OF_CACHE = 1u << 0, /* position < 0 or >= cache_alloc_len */
+  DRK_STATUS_REQUEST_OUT_OF_RANGE = 1u << 1,  /* request index < 0 or >= batch */
+  DRK_STATUS_POSITION_OUT_OF_TABLE = 1u << 2, /* position >= rows of the cos/sin table */
+  DRK_STATUS_BLOCK_OUT_OF_RANGE = 1u << 3     /* paged cache: block id outside the pool */
+};
+
+/* Launch options (drk_options.flags). */
+enum {
+  /* Launch with programmatic dependent launch: the kernel reads positions, request indices
+   * and the cos/sin rows before waiting on the preceding kernel in the stream, then waits
+   * (griddepcontrol.wait) before it reads q/k/v or writes anything. The caller guarantees the
+   * immediately preceding kernel does not write positions, request indices or the tables. */
+  DRK_FLAG_PDL = 1u << 0,
+  /* Accept caches with any element strides whose last dim is contiguous (e.g. head-major
+   * [B, Hkv, S, D] passed as its [B, S, Hkv, D] transposed view). Without it the cache must be
+   * contiguous token-major, as the reference requires. */
+  DRK_FLAG_STRIDED_CACHE = 1u << 1,
+  /* Take cos/sin from sincosf of position * inv_freq in registers instead of the table
+   * (needs drk_options.inv_freq). Within 1 ulp of the table path, not bit-exact. */
+  DRK_FLAG_INREG_TRIG = 1u << 2
+};
+
+/* A strided view of device (or host) memory. Sizes and strides are in elements; unused
+ * trailing dims are ignored. device is the CUDA ordinal, or -1 for host memory. */
+typedef struct drk_tensor {
+  void* data;
+  int32_t dtype;
+  int32_t ndim;
+  int32_t device;
+  int32_t reserved;
+  int64_t sizes[4];
+  int64_t strides[4];
+} drk_tensor;
+
+/* Extensions beyond the reference contract; zero-initialised means reference behaviour. */
+typedef struct drk_options {
+  uint32_t flags;         /* DRK_FLAG_* */
+  int32_t rotary_dim;     /* 0: the table width must equal head_dim (reference). Otherwise the
+                             table width, even and <= head_dim; dims past it are copied raw. */
+  const float* inv_freq;  /* [rotary_dim/2] fp32 device array, only for DRK_FLAG_INREG_TRIG */
+  int64_t reserved[4];
+} drk_options;
+
+/*
+ * Fused RoPE + KV append, one launch.
+ * Replaces fused_rope_kv_append (csrc/fused_rope_kv_append.cu:89-141, bound at
+ * csrc/bindings.cpp:30-33 of the reference). q [T, Hq, D], k and v [T, Hkv, D] with a
+ * contiguous last dim and any token/head strides; positions and request_indices [T], both
+ * int32 or both int64; cos and sin fp32 contiguous [P, D]; k_cache and v_cache contiguous
+ * [B, S, Hkv, D] of q's dtype; q_out contiguous [T, Hq, D] of q's dtype, allocated by the
+ * caller (the reference returns a fresh tensor). Writes q_out = RoPE(q),
+ * k_cache[ri[t], pos[t]] = RoPE(k[t]), v_cache[ri[t], pos[t]] = v[t] (byte copy).
+ * Q and K are bit-exact to the reference's PyTorch oracle.
+ */
+DRK_API int drk_fused_rope_kv_append(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                             const drk_tensor* positions, const drk_tensor* cos,
+                             const drk_tensor* sin, const drk_tensor* k_cache,
+                             const drk_tensor* v_cache, const drk_tensor* request_indices,
+                             const drk_tensor* q_out, uint32_t* status, drk_stream_t stream);
+
+/* drk_fused_rope_kv_append with the extensions in *opts (NULL = none). */
+DRK_API int drk_fused_rope_kv_append_ex(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                                const drk_tensor* positions, const drk_tensor* cos,
+                                const drk_tensor* sin, const drk_tensor* k_cache,
+                                const drk_tensor* v_cache, const drk_tensor* request_indices,
+                                const drk_tensor* q_out, const drk_options* opts,
+                                uint32_t* status, drk_stream_t stream);
+
+/*
+ * RoPE only: q_out = RoPE(q), k_out = RoPE(k), both contiguous and caller-allocated.
+ * Replaces rope_forward (csrc/rope.cu:64-105, bound at csrc/bindings.cpp:22-24).
+ */
+DRK_API int drk_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor* positions,
+                     const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* q_out,
+                     const drk_tensor* k_out, const drk_options* opts, uint32_t* status,
+                     drk_stream_t stream);
+
+/*
+ * Append only: byte copies of k_rot and v into k_cache/v_cache at [ri[t], pos[t]].
+ * Replaces kv_append (csrc/kv_append.cu:45-86, bound at csrc/bindings.cpp:25-27).
+ */
+DRK_API int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor* positions,
+                  const drk_tensor* request_indices, const drk_tensor* k_cache,
+                  const drk_tensor* v_cache, const drk_options* opts, uint32_t* status,
+                  drk_stream_t stream);
+
+/*
+ * Fused RoPE + append into a paged KV cache (no counterpart in the reference, whose cache is
+ * one contiguous row per request; this is the block-table layout its notes name as the next
+ * step). k_pages and v_pages are [num_blocks, block_size, Hkv, D] contiguous; block_table is
+ * [num_requests, max_blocks_per_request] contiguous, of the index dtype; token t lands in
+ * block block_table[ri[t], pos[t] / block_size], row pos[t] % block_size.
+ */
+DRK_API int drk_paged_rope_kv_append(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                             const drk_tensor* positions, const drk_tensor* cos,
+                             const drk_tensor* sin, const drk_tensor* k_pages,
+                             const drk_tensor* v_pages, const drk_tensor* block_table,
+                             const drk_tensor* request_indices, const drk_tensor* q_out,
+                             const drk_options* opts, uint32_t* status, drk_stream_t stream);
+
+/*
+ * Fills a contiguous fp64/fp32/fp16/bf16 tensor with value (converted once on the host, so
+ * fp64 keeps full precision). Replaces smoke_fill (csrc/smoke.cu:42-60, bound at
+ * csrc/bindings.cpp:19-20).
+ */
+DRK_API int drk_smoke_fill(const drk_tensor* tensor, double value, drk_stream_t stream);
+
+/*
+ * Writes "key=value" lines (gencode_arch, cuda_version_compiled, cuda_version_runtime,
+ * cuda_version_driver, nvcc_version, fast_math) into buf. gencode_arch comes from a kernel
+ * run on the current device, so this call synchronises the stream. Replaces build_info
+ * (csrc/smoke.cu:62-87, bound at csrc/bindings.cpp:21).
+ */
+DRK_API int drk_build_info(char* buf, size_t len, drk_stream_t stream);
+
+/* Launch-floor probe: `count` back-to-back launches of an empty one-warp kernel on stream,
+ * with programmatic dependent launch when pdl != 0. */
+DRK_API int drk_launch_empty(int count, int pdl, drk_stream_t stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+DRK_API const char* drk_last_error(void);
+
+/* Human-readable description of a status word's bits. */
+DRK_API const char* drk_status_string(uint32_t status);
+
+/* Library version, e.g. "0.1.0". */
+DRK_API const char* drk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DECODE_ROPE_H_ */
