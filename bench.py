@@ -53,6 +53,11 @@ def parse_args():
     p.add_argument("--no-bw-probe", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--mode", choices=["full", "bw"], default="full",
+                   help="bw: only the bandwidth-bound launch loop (for profiling small cases)")
+    p.add_argument("--cache-len", type=int, default=0,
+                   help="bw mode: override cache_alloc_len (keeps a profiled case small)")
+    p.add_argument("--launches", type=int, default=400, help="bw mode: timed launches")
     return p.parse_args()
 
 
@@ -105,7 +110,10 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index):
-        self.device_index = device_index
+        try:
+            self.device_id = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:  # noqa: BLE001 -- fall back to the ordinal
+            self.device_id = str(device_index)
         self.samples = []
         self._proc = None
         self._thread = None
@@ -113,7 +121,7 @@ class ClockSampler:
     def start(self):
         try:
             self._proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={self.device_id}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
@@ -219,11 +227,15 @@ def time_graph_steps(captured, steps, stream):
     return start.elapsed_time(end)
 
 
-def bandwidth_probe(world, rank, device, seed, peak):
+def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
     """The bandwidth-bound workload (mistral_b4096, sharded by batch): one fused launch per
-    call, 8 input sets rotated, device time per launch from CUDA events."""
+    call, input sets rotated so they exceed 3x L2, device time per launch from CUDA events.
+    cache_len > 0 shrinks the caches (same per-token work) for profiling runs."""
+    from dataclasses import replace
     from decode_llm_kernel_b200.cuda import ops
     w = WORKLOADS["mistral_b4096"].shard_for(rank, world)
+    if cache_len:
+        w = replace(w, cache_alloc_len=cache_len)
     g = torch.Generator(device=device).manual_seed(seed + 17)
     shape = (w.batch, w.cache_alloc_len, w.num_kv_heads, w.head_dim)
     kc = normal_(torch.empty(shape, dtype=w.dtype, device=device), g)
@@ -250,7 +262,6 @@ def bandwidth_probe(world, rank, device, seed, peak):
 
     for i in range(20):
         call(i)
-    iters = 400
     stream = torch.cuda.current_stream()
     barrier(world)
     torch.cuda.synchronize()
@@ -265,6 +276,7 @@ def bandwidth_probe(world, rank, device, seed, peak):
     per_launch_s = ms / 1e3 / iters
     gbs_rank = w.bytes_per_call() / per_launch_s / 1e9
     out = {"workload": "mistral_b4096", "batch_per_gpu": w.batch, "dtype": w.dtype_label,
+           "cache_alloc_len": w.cache_alloc_len, "launches": iters,
            "bytes_per_launch": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
            "achieved_gbs_per_gpu": gbs_rank, "frac_of_peak": gbs_rank / peak,
            "aggregate_gbs": gbs_rank * world, "input_sets": nsets}
@@ -345,7 +357,7 @@ def run_ours(args, world, rank, local):
         e2e_cap.release()
 
     floor = launch_floor(stream, w.layers)
-    del captured, sets, k_caches, v_caches
+    del captured, sets, k_caches, v_caches, step
     torch.cuda.empty_cache()
     bw = None if args.no_bw_probe else bandwidth_probe(world, rank, device, args.seed, peak)
 
@@ -530,6 +542,14 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.mode == "bw":
+            local_dev = torch.device("cuda", local)
+            torch.cuda.set_device(local_dev)
+            peak, _ = measured_hbm_peak()
+            out = bandwidth_probe(world, rank, local_dev, args.seed, peak, args.cache_len,
+                                  args.launches)
+            if rank == 0:
+                print(json.dumps(out), flush=True)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -87,7 +87,8 @@ uint32_t* status_for(const at::Tensor& t) {
   return t.is_cuda() ? status_word(t.get_device()) : nullptr;
 }
 
-drk_options make_options(uint32_t flags, int64_t rotary_dim, const c10::optional<at::Tensor>& inv_freq) {
+drk_options make_options(uint32_t flags, int64_t rotary_dim,
+                         const c10::optional<at::Tensor>& inv_freq, int64_t head_dim = 0) {
   drk_options o{};
   o.flags = flags;
   o.rotary_dim = static_cast<int32_t>(rotary_dim);
@@ -95,6 +96,9 @@ drk_options make_options(uint32_t flags, int64_t rotary_dim, const c10::optional
     TORCH_CHECK(inv_freq->is_cuda() && inv_freq->scalar_type() == at::kFloat &&
                     inv_freq->is_contiguous(),
                 "inv_freq must be a contiguous fp32 CUDA tensor");
+    const int64_t width = rotary_dim ? rotary_dim : head_dim;
+    TORCH_CHECK(inv_freq->numel() == width / 2, "inv_freq must hold rotary_dim/2 = ", width / 2,
+                " frequencies, got ", inv_freq->numel());
     o.inv_freq = inv_freq->data_ptr<float>();
     o.flags |= DRK_FLAG_INREG_TRIG;
   }
@@ -185,7 +189,7 @@ at::Tensor fused_rope_kv_append_ex(at::Tensor q, at::Tensor k, at::Tensor v,
   else if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
   const drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
                                          (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
-                                     rotary_dim, inv_freq);
+                                     rotary_dim, inv_freq, q.dim() == 3 ? q.size(2) : 0);
   const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
                    dp = describe(positions), dc = describe(cos), ds = describe(sin),
                    dkc = describe(k_cache), dvc = describe(v_cache),
