@@ -444,6 +444,11 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
 
 }  // namespace
 
+namespace drk {
+// For entry points defined in other files of this library (noalloc.cu).
+void set_last_error(const std::string& message) { g_last_error = message; }
+}  // namespace drk
+
 extern "C" {
 
 int drk_fused_rope_kv_append(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,

@@ -157,6 +157,29 @@ DRK_API int drk_paged_rope_kv_append(const drk_tensor* q, const drk_tensor* k, c
                              const drk_options* opts, uint32_t* status, drk_stream_t stream);
 
 /*
+ * The separate op (drk_rope_forward, then drk_kv_append) for callers that cannot allocate
+ * device memory when they launch it. No counterpart in the reference: it is this library's
+ * allocation-free form of separate_rope_kv_append (decode_kernels/cuda/ops.py:25-34 of the
+ * reference), whose k_rot intermediate the reference allocates per call.
+ *
+ * Callers it is for: code recorded under a global-mode stream capture (where cudaMalloc is not
+ * allowed), serving runtimes that have given all free HBM to their KV-cache pool, and hosts
+ * reaching the library through this C ABI without an allocator of their own. The caller still
+ * provides every input and output (q_out included); the k_rot intermediate lives in an 8 MiB
+ * static device array inside the library, which every GPU that loads the library holds until
+ * the process exits. Calls whose k_rot ([T, Hkv, D] of k's dtype) exceeds 8 MiB are rejected
+ * with DRK_ERR_INVALID. The first call on a device looks up the array's address with that
+ * device current; make it before any stream capture. All calls share the array, so calls that
+ * overlap on the GPU race. Nothing in the array needs to start zeroed. Results are bit-identical
+ * to drk_rope_forward + drk_kv_append with a caller-allocated k_rot.
+ */
+DRK_API int drk_separate_rope_kv_append_noalloc(
+    const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,
+    const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* k_cache,
+    const drk_tensor* v_cache, const drk_tensor* request_indices, const drk_tensor* q_out,
+    uint32_t* status, drk_stream_t stream);
+
+/*
  * Fills a contiguous fp64/fp32/fp16/bf16 tensor with value (converted once on the host, so
  * fp64 keeps full precision). Replaces smoke_fill (csrc/smoke.cu:42-60, bound at
  * csrc/bindings.cpp:19-20).
