@@ -51,6 +51,7 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-bw-probe", action="store_true")
+    p.add_argument("--no-floor", action="store_true", help="skip the empty-kernel launch floor")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--mode", choices=["full", "bw"], default="full",
@@ -356,7 +357,7 @@ def run_ours(args, world, rank, local):
                        "D2H copy in one graph, wall clock with a sync on both sides"}
         e2e_cap.release()
 
-    floor = launch_floor(stream, w.layers)
+    floor = None if args.no_floor else launch_floor(stream, w.layers)
     del captured, sets, k_caches, v_caches, step
     torch.cuda.empty_cache()
     bw = None if args.no_bw_probe else bandwidth_probe(world, rank, device, args.seed, peak)
