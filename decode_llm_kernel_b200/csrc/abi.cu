@@ -257,11 +257,78 @@ Shape plan(const Aligner& al, int nrows, bool rotates) {
                           drk::kMaxThreadsPerBlock, " are supported"));
   s.nslots = static_cast<int>(nslots);
   s.nrot = rotates ? static_cast<int>(al.R / (2 * vec)) : 0;
-  // About three rows per thread; a block holds whole row groups.
-  const int want_groups = std::max(1, (nrows + 2) / 3);
+  // kRowsPerThread rows per thread; a block holds whole row groups.
+  const int want_groups = std::max(1, (nrows + drk::kRowsPerThread - 1) / drk::kRowsPerThread);
   s.G = std::max(1, std::min(want_groups, drk::kMaxThreadsPerBlock / s.nslots));
   s.threads = s.G * s.nslots;
   return s;
+}
+
+// The bulk-copy kernel's plan: eligible only if every row block it copies is one contiguous,
+// 16-byte-aligned run.
+#ifndef DRK_STAGED_MIN_TOKENS
+#define DRK_STAGED_MIN_TOKENS 1024
+#endif
+
+struct StagedPlan {
+  bool ok = false;
+  std::string why;
+  int vb = 0, nrot = 0, groups = 0;
+  drk::StagedParams sp{};
+};
+
+StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                       const drk_tensor* q_out, const drk_tensor* k_cache,
+                       const drk_tensor* v_cache, int64_t T, int64_t Hq, int64_t Hkv,
+                       int64_t D, int64_t R, int64_t es) {
+  StagedPlan pl;
+  auto fail = [&](const char* why) {
+    pl.why = why;
+    return pl;
+  };
+  auto rows_contig = [&](const drk_tensor* t, int64_t heads) {
+    return heads == 1 || t->strides[1] == D;
+  };
+  if (!rows_contig(q, Hq) || !rows_contig(k, Hkv) || !rows_contig(v, Hkv))
+    return fail("a token's q/k/v heads are not one contiguous run (head stride != head_dim)");
+  if (Hkv > 1 && k_cache->strides[2] != D)
+    return fail("a cache slot is not contiguous (head stride != head_dim)");
+  const int64_t q_bytes = Hq * D * es, kv_bytes = Hkv * D * es;
+  if (q_bytes % 16 || kv_bytes % 16) return fail("row blocks are not multiples of 16 bytes");
+  uintptr_t addr = 0;
+  for (const drk_tensor* t : {q, k, v, q_out, k_cache, v_cache})
+    addr |= reinterpret_cast<uintptr_t>(t->data);
+  if (addr % 16) return fail("a base address is not 16-byte aligned");
+  int64_t strides = 0;
+  if (T > 1) strides |= q->strides[0] | k->strides[0] | v->strides[0];
+  for (int i = 0; i < 2; ++i)
+    if (k_cache->sizes[i] > 1) strides |= k_cache->strides[i];
+  if ((strides * es) % 16) return fail("a token or cache stride is not a multiple of 16 bytes");
+  for (int vb : {16, 8, 4, 2}) {
+    if (vb < es || vb % es) continue;
+    const int64_t vec = vb / es;
+    if ((R / 2) % vec || (D * es) % vb) continue;
+    pl.vb = vb;
+    pl.nrot = static_cast<int>(R / (2 * vec));
+    break;
+  }
+  if (pl.vb == 0 || pl.nrot > drk::kStagedThreadsPerBlock)
+    return fail("no vector width fits the rotary dims");
+  const int64_t rot_rows = Hq + Hkv;
+  pl.groups = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(rot_rows, drk::kStagedThreadsPerBlock / pl.nrot)));
+  const int64_t stage = (q_bytes + 2 * kv_bytes + 127) / 128 * 128;
+  int stages = static_cast<int>(std::min<int64_t>(4, (96 * 1024) / stage));
+  if (stages < 2) {
+    if (2 * stage > 200 * 1024) return fail("one token's rows do not fit two shared-memory stages");
+    stages = 2;
+  }
+  pl.sp.q_bytes = static_cast<uint32_t>(q_bytes);
+  pl.sp.kv_bytes = static_cast<uint32_t>(kv_bytes);
+  pl.sp.stage_bytes = static_cast<uint32_t>(stage);
+  pl.sp.stages = stages;
+  pl.ok = true;
+  return pl;
 }
 
 int grid_for(int64_t tokens) {
@@ -424,6 +491,28 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   p.R = static_cast<int32_t>(R);
   fill_table(p, cos, sin, o, R);
 
+  const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+  const bool pdl = (o.flags & DRK_FLAG_PDL) != 0;
+  const bool force_staged = (o.flags & DRK_FLAG_FORCE_STAGED_PATH) != 0;
+  const bool force_register = (o.flags & DRK_FLAG_FORCE_REGISTER_PATH) != 0;
+  if (force_staged && force_register)
+    invalid("DRK_FLAG_FORCE_STAGED_PATH and DRK_FLAG_FORCE_REGISTER_PATH are exclusive");
+  if (!force_register && (force_staged || T >= DRK_STAGED_MIN_TOKENS)) {
+    const StagedPlan pl = plan_staged(q, k, v, q_out, k_cache, v_cache, T, Hq, Hkv, D, R, es);
+    if (pl.ok) {
+      p.nrot = pl.nrot;
+      p.G = pl.groups;
+      p.nslots = pl.nrot;
+      DeviceGuard guard(device);
+      const drk::LaunchShape shape{0, pl.nrot, pl.groups, pdl};
+      check_launch(drk::launch_rope_kv_staged(p, pl.sp, elem_code(q->dtype), index_bits, pl.vb,
+                                              paged ? drk::kCachePaged : drk::kCacheStrided,
+                                              shape, reinterpret_cast<cudaStream_t>(stream)));
+      return;
+    }
+    if (force_staged) throw Unsupported("the bulk-copy kernel cannot take this call: " + pl.why);
+  }
+
   Aligner al{es, R, D};
   for (const drk_tensor* t : {q, k, v, q_out, k_cache, v_cache}) al.ptr(t->data);
   al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
@@ -435,8 +524,7 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G;
 
   DeviceGuard guard(device);
-  const drk::LaunchShape shape{grid_for(T), s.threads, (o.flags & DRK_FLAG_PDL) != 0};
-  const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+  const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, pdl};
   check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeFused,
                                    paged ? drk::kCachePaged : drk::kCacheStrided, shape,
                                    reinterpret_cast<cudaStream_t>(stream)));
@@ -535,7 +623,7 @@ int drk_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor*
     const Shape s = plan(al, static_cast<int>(Hq + Hkv), true);
     p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G;
     DeviceGuard guard(device);
-    const drk::LaunchShape shape{grid_for(T), s.threads, (o.flags & DRK_FLAG_PDL) != 0};
+    const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
     const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
     check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeRope,
                                      drk::kCacheStrided, shape,
@@ -599,7 +687,7 @@ int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor
     const Shape s = plan(al, static_cast<int>(2 * Hkv), false);
     p.nslots = s.nslots; p.nrot = 0; p.G = s.G;
     DeviceGuard guard(device);
-    const drk::LaunchShape shape{grid_for(T), s.threads, (o.flags & DRK_FLAG_PDL) != 0};
+    const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
     const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
     check_launch(drk::launch_rope_kv(p, elem_code(k_rot->dtype), index_bits, s.vb,
                                      drk::kModeAppend, drk::kCacheStrided, shape,
@@ -670,7 +758,8 @@ const char* drk_status_string(uint32_t status) {
   add(DRK_STATUS_REQUEST_OUT_OF_RANGE, "a request index was outside [0, batch)");
   add(DRK_STATUS_POSITION_OUT_OF_TABLE, "a position was outside the cos/sin table");
   add(DRK_STATUS_BLOCK_OUT_OF_RANGE, "a block-table entry was outside the page pool");
-  if (status & ~0xFu) s += (s.empty() ? "" : "; ") + cat("unknown bits 0x", std::hex, status);
+  add(DRK_STATUS_TIMEOUT, "a bounded in-kernel wait ran out and a CTA stopped early");
+  if (status & ~0x1Fu) s += (s.empty() ? "" : "; ") + cat("unknown bits 0x", std::hex, status);
   g_status_text = s;
   return g_status_text.c_str();
 }

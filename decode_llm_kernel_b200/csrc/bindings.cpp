@@ -105,6 +105,13 @@ drk_options make_options(uint32_t flags, int64_t rotary_dim,
   return o;
 }
 
+uint32_t path_flags(const std::string& path) {
+  if (path == "auto") return 0u;
+  if (path == "register") return DRK_FLAG_FORCE_REGISTER_PATH;
+  if (path == "staged") return DRK_FLAG_FORCE_STAGED_PATH;
+  TORCH_CHECK(false, "path must be 'auto', 'register' or 'staged', got '", path, "'");
+}
+
 at::Tensor empty_like_rows(const at::Tensor& src, int64_t heads) {
   return at::empty({src.size(0), heads, src.size(2)}, src.options());
 }
@@ -183,12 +190,13 @@ at::Tensor fused_rope_kv_append_ex(at::Tensor q, at::Tensor k, at::Tensor v,
                                    at::Tensor k_cache, at::Tensor v_cache,
                                    at::Tensor request_indices, int64_t rotary_dim, bool pdl,
                                    bool strided_cache, c10::optional<at::Tensor> inv_freq,
-                                   c10::optional<at::Tensor> q_out_opt) {
+                                   c10::optional<at::Tensor> q_out_opt, const std::string& path) {
   at::Tensor q_out;
   if (q_out_opt.has_value() && q_out_opt->defined()) q_out = *q_out_opt;
   else if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
   const drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
-                                         (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
+                                         (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u) |
+                                         path_flags(path),
                                      rotary_dim, inv_freq, q.dim() == 3 ? q.size(2) : 0);
   const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
                    dp = describe(positions), dc = describe(cos), ds = describe(sin),
@@ -205,10 +213,12 @@ at::Tensor fused_rope_kv_append_ex(at::Tensor q, at::Tensor k, at::Tensor v,
 at::Tensor paged_rope_kv_append(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor positions,
                                 at::Tensor cos, at::Tensor sin, at::Tensor k_pages,
                                 at::Tensor v_pages, at::Tensor block_table,
-                                at::Tensor request_indices, int64_t rotary_dim, bool pdl) {
+                                at::Tensor request_indices, int64_t rotary_dim, bool pdl,
+                                const std::string& path) {
   at::Tensor q_out;
   if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
-  const drk_options o = make_options(pdl ? DRK_FLAG_PDL : 0u, rotary_dim, c10::nullopt);
+  const drk_options o =
+      make_options((pdl ? DRK_FLAG_PDL : 0u) | path_flags(path), rotary_dim, c10::nullopt);
   const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
                    dp = describe(positions), dc = describe(cos), ds = describe(sin),
                    dkp = describe(k_pages), dvp = describe(v_pages), dbt = describe(block_table),
@@ -306,11 +316,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_cache"), py::arg("request_indices"), py::arg("rotary_dim") = 0,
         py::arg("pdl") = false, py::arg("strided_cache") = false,
         py::arg("inv_freq") = py::none(), py::arg("q_out") = py::none(),
+        py::arg("path") = "auto",
         "fused_rope_kv_append with partial rotary, PDL, strided caches, in-register trig.");
   m.def("paged_rope_kv_append", &paged_rope_kv_append, py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_pages"),
         py::arg("v_pages"), py::arg("block_table"), py::arg("request_indices"),
-        py::arg("rotary_dim") = 0, py::arg("pdl") = false,
+        py::arg("rotary_dim") = 0, py::arg("pdl") = false, py::arg("path") = "auto",
         "Fused RoPE + append into a paged (block-table) KV cache; returns q_rot.");
   m.def("rope_forward_ex", &rope_forward_ex, py::arg("q"), py::arg("k"), py::arg("positions"),
         py::arg("cos"), py::arg("sin"), py::arg("rotary_dim") = 0, py::arg("pdl") = false);

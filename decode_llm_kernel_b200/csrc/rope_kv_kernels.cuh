@@ -9,8 +9,8 @@
 // append-only modes are the reference's two separate kernels (csrc/rope.cu:14-59,
 // csrc/kv_append.cu:11-40) on the same code.
 //
-// Work layout. A CTA owns one token at a time (grid-stride over tokens). Its threads form
-// `G` row groups of `nslots` lanes: lane j of a group moves two vectors of VB bytes of one head
+// Work layout. A CTA walks tokens (grid-stride). Its threads form `G` row groups (threadIdx.y)
+// of `nslots` lanes (threadIdx.x): lane j of a group moves two vectors of VB bytes of one head
 // row -- for a rotated row, x1 = x[j*VEC ..) and x2 = x[R/2 + j*VEC ..), which is exactly the
 // rotate_half pairing, so the rotation needs no data exchange between lanes. Rows are the
 // token's Q heads, then its K heads, then its V heads; group g takes rows g, g+G, g+2G, ...
@@ -30,15 +30,19 @@
 // CUDA_KERNEL_ASSERT, csrc/kernel_common.cuh:38-51, kills the context): the token's writes
 // that would need the bad index are skipped and a bit is ORed into the status word.
 //
-// Programmatic dependent launch. The indices and the table slice are read before
-// griddepcontrol.wait; q/k/v are read and every store is issued after it. Launched without the
-// PDL attribute the wait returns at once.
+// Order of a token's memory traffic. The position and request-index loads are issued first
+// (before griddepcontrol.wait: they never come from the preceding kernel); then every q/k/v
+// row load of the thread, which do not depend on the position; only then is the position
+// consumed for the bounds, the cache slot and the table slice. So a CTA's HBM reads are in
+// flight while its index and table loads resolve, instead of after them. Launched without the
+// programmatic-dependent-launch attribute, griddepcontrol.wait returns at once.
 #pragma once
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "rope_kv_launch.h"
 
@@ -47,7 +51,8 @@ namespace drk {
 enum class Mode : int { kFused = 0, kRope = 1, kAppend = 2 };
 enum class Cache : int { kStrided = 0, kPaged = 1 };
 
-constexpr int kMaxRowsInFlight = 4;
+constexpr int kMaxRowsInFlight = kRowsPerThread;
+constexpr int kMinBlocksPerSM = DRK_MIN_BLOCKS_PER_SM;
 
 enum : uint32_t {
   kStatusPosCache = 1u << 0,
@@ -58,7 +63,8 @@ enum : uint32_t {
 
 // KernelParams lives in rope_kv_launch.h so the host layer can fill it.
 
-// ---- element traits: storage bits <-> fp32 ----
+// ---- element traits: storage bits <-> fp32, one element or a packed pair ----
+// A pair is two adjacent elements in one 32-bit word, element j in the low half.
 struct F32 {
   using raw = float;
   static __device__ __forceinline__ float to_f(raw x) { return x; }
@@ -70,6 +76,17 @@ struct F16 {
   static __device__ __forceinline__ raw from_f(float f) {
     return __half_as_ushort(__float2half_rn(f));
   }
+  static __device__ __forceinline__ float2 pair_to_f(unsigned int w) {
+    __half2 h;
+    memcpy(&h, &w, 4);
+    return __half22float2(h);
+  }
+  static __device__ __forceinline__ unsigned int pair_from_f(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    unsigned int w;
+    memcpy(&w, &h, 4);
+    return w;
+  }
 };
 struct BF16 {
   using raw = unsigned short;
@@ -78,6 +95,15 @@ struct BF16 {
   }
   static __device__ __forceinline__ raw from_f(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  }
+  static __device__ __forceinline__ float2 pair_to_f(unsigned int w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  }
+  static __device__ __forceinline__ unsigned int pair_from_f(float lo, float hi) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+    unsigned int w;
+    memcpy(&w, &b, 4);
+    return w;
   }
 };
 struct F64 {
@@ -96,7 +122,43 @@ template <typename E, int VB>
 union Pack {
   typename VecBits<VB>::type bits;
   typename E::raw e[VB / sizeof(typename E::raw)];
+  unsigned int w[VB >= 4 ? VB / 4 : 1];
 };
+
+// x1 <- fl(fl(x1*c) - fl(x2*s)), x2 <- fl(fl(x2*c) + fl(x1*s)), element by element, rounded to
+// the storage type once. 16-bit types unpack and repack two elements per 32-bit word; the
+// arithmetic is the scalar __fmul_rn / __fsub_rn / __fadd_rn chain, which the compiler may not
+// contract into a fused multiply-add.
+template <typename E, int VB>
+__device__ __forceinline__ void rotate_pack(Pack<E, VB>& x1, Pack<E, VB>& x2, const float* c,
+                                            const float* s) {
+  using raw = typename E::raw;
+  constexpr int VEC = VB / static_cast<int>(sizeof(raw));
+  if constexpr (sizeof(raw) == 2 && VB >= 4) {
+#pragma unroll
+    for (int w = 0; w < VB / 4; ++w) {
+      const float2 a = E::pair_to_f(x1.w[w]);
+      const float2 b = E::pair_to_f(x2.w[w]);
+      const float c0 = c[2 * w], c1 = c[2 * w + 1], s0 = s[2 * w], s1 = s[2 * w + 1];
+      const float y1lo = __fsub_rn(__fmul_rn(a.x, c0), __fmul_rn(b.x, s0));
+      const float y1hi = __fsub_rn(__fmul_rn(a.y, c1), __fmul_rn(b.y, s1));
+      const float y2lo = __fadd_rn(__fmul_rn(b.x, c0), __fmul_rn(a.x, s0));
+      const float y2hi = __fadd_rn(__fmul_rn(b.y, c1), __fmul_rn(a.y, s1));
+      x1.w[w] = E::pair_from_f(y1lo, y1hi);
+      x2.w[w] = E::pair_from_f(y2lo, y2hi);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float a = E::to_f(x1.e[j]);
+      const float b = E::to_f(x2.e[j]);
+      const float y1 = __fsub_rn(__fmul_rn(a, c[j]), __fmul_rn(b, s[j]));
+      const float y2 = __fadd_rn(__fmul_rn(b, c[j]), __fmul_rn(a, s[j]));
+      x1.e[j] = E::from_f(y1);
+      x2.e[j] = E::from_f(y2);
+    }
+  }
+}
 
 // Sources are read once: evict-first in L1 and L2.
 template <int VB>
@@ -149,43 +211,91 @@ __device__ __forceinline__ void row_kind(const KernelParams& p, int r, int& kind
 }
 
 template <typename E, typename Idx, int VB, Mode M, Cache C>
-__global__ void __launch_bounds__(kMaxThreadsPerBlock)
+__global__ void __launch_bounds__(kMaxThreadsPerBlock, kMinBlocksPerSM)
 rope_kv_kernel(const __grid_constant__ KernelParams p) {
   using raw = typename E::raw;
-  using Bits = typename VecBits<VB>::type;
   constexpr int VEC = VB / static_cast<int>(sizeof(raw));
   constexpr int64_t ES = static_cast<int64_t>(sizeof(raw));
+  constexpr int NR = kMaxRowsInFlight;
 
   // Let the next kernel in the stream start its own prologue while this one runs.
   pdl_launch_dependents();
 
-  const int lane = static_cast<int>(threadIdx.x) % p.nslots;
-  const int grp = static_cast<int>(threadIdx.x) / p.nslots;
-  if (grp >= p.G) return;
+  // blockDim = (nslots, G): threadIdx.x is the lane within a row, threadIdx.y the row group.
+  const int lane = static_cast<int>(threadIdx.x);
+  const int grp = static_cast<int>(threadIdx.y);
   const int nrows = num_rows<M>(p);
-  const int half_r = p.R >> 1;
   const bool lane_rotates = (M != Mode::kAppend) && lane < p.nrot;
+  // Element offsets of the lane's two vectors: in a Q/K row (the rotate_half pair, or two
+  // pass-through vectors past the rotary dims) and in a V row (a plain copy).
+  const int qk_base = (M == Mode::kAppend) ? 0 : p.R;
+  const int qk_off1 = lane_rotates ? lane * VEC : qk_base + (lane - (qk_base ? p.nrot : 0)) * VEC;
+  const int qk_off2 = lane_rotates ? (p.R >> 1) + lane * VEC : qk_off1 + ((p.D - qk_base) >> 1);
+  const int v_off1 = lane * VEC;
+  const int v_off2 = v_off1 + (p.D >> 1);
   bool waited = false;
 
-  for (int64_t t = blockIdx.x; t < p.T; t += gridDim.x) {
-    // ---- prologue: indices, bounds, table slice (independent of the preceding kernel) ----
-    const int64_t pos = load_index<Idx>(p.positions, t);
-    uint32_t bad = 0;
-    const bool table_ok = pos >= 0 && pos < p.table_rows;
-    if (!table_ok && M != Mode::kAppend) bad |= kStatusPosTable;
-    int64_t slot = 0;
-    bool cache_ok = true;
-    if constexpr (M != Mode::kRope) {
-      const int64_t ri = load_index<Idx>(p.request_indices, t);
-      const bool pos_ok = pos >= 0 && pos < p.S;
-      const bool ri_ok = ri >= 0 && ri < p.B;
-      if (!pos_ok) bad |= kStatusPosCache;
-      if (!ri_ok) bad |= kStatusRequest;
-      cache_ok = pos_ok && ri_ok;
-      if constexpr (C == Cache::kStrided) {
-        slot = ri * p.c_bs + pos * p.c_ss;
-      } else {
-        if (cache_ok) {
+  for (int r0 = grp; r0 < nrows; r0 += p.G * NR) {
+    // Per-row constants of this batch of rows: which tensor, the byte offset of the lane's
+    // first vector inside a token's source row and inside its destination row, the distance
+    // to the second vector.
+    int kind[NR];
+    int64_t src_off[NR], dst_off[NR];
+    int gap[NR];
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const int r = r0 + i * p.G;
+      int k = kRowV, head = 0;
+      if (r < nrows) row_kind<M>(p, r, k, head);
+      kind[i] = r < nrows ? k : -1;
+      const int o1 = k == kRowV ? v_off1 : qk_off1;
+      const int o2 = k == kRowV ? v_off2 : qk_off2;
+      gap[i] = (o2 - o1) * static_cast<int>(ES);
+      const int64_t hs = k == kRowQ ? p.q_hs : (k == kRowK ? p.k_hs : p.v_hs);
+      src_off[i] = (head * hs + o1) * ES;
+      if (k == kRowQ || M == Mode::kRope) dst_off[i] = (static_cast<int64_t>(head) * p.D + o1) * ES;
+      else dst_off[i] = (head * p.c_hs + o1) * ES;
+    }
+
+    for (int64_t t = blockIdx.x; t < p.T; t += gridDim.x) {
+      // Indices first: they never come from the preceding kernel, and nothing below waits on
+      // them until the row loads are in flight.
+      const int64_t pos = load_index<Idx>(p.positions, t);
+      int64_t ri = 0;
+      if constexpr (M != Mode::kRope) ri = load_index<Idx>(p.request_indices, t);
+      if (!waited) {
+        pdl_wait();   // q/k/v may be written by the preceding kernel
+        waited = true;
+      }
+
+      Pack<E, VB> x1[NR], x2[NR];
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        if (kind[i] >= 0) {
+          const char* base = kind[i] == kRowQ ? p.q + t * p.q_ts * ES
+                           : kind[i] == kRowK ? p.k + t * p.k_ts * ES
+                                              : p.v + t * p.v_ts * ES;
+          const char* src = base + src_off[i];
+          x1[i].bits = load_stream<VB>(src);
+          x2[i].bits = load_stream<VB>(src + gap[i]);
+        }
+      }
+
+      // ---- bounds, destination slot and the table slice (needs the position) ----
+      uint32_t bad = 0;
+      const bool table_ok = pos >= 0 && pos < p.table_rows;
+      if (!table_ok && M != Mode::kAppend) bad |= kStatusPosTable;
+      bool cache_ok = true;
+      int64_t slot = 0;
+      if constexpr (M != Mode::kRope) {
+        const bool pos_ok = pos >= 0 && pos < p.S;
+        const bool ri_ok = ri >= 0 && ri < p.B;
+        if (!pos_ok) bad |= kStatusPosCache;
+        if (!ri_ok) bad |= kStatusRequest;
+        cache_ok = pos_ok && ri_ok;
+        if constexpr (C == Cache::kStrided) {
+          slot = ri * p.c_bs + pos * p.c_ss;
+        } else if (cache_ok) {
           const int64_t blk_i = pos / p.block_size;
           const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
           if (blk < 0 || blk >= p.num_blocks) {
@@ -195,23 +305,24 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
           slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
         }
       }
-    }
-    if (bad && threadIdx.x == 0 && p.status != nullptr) atomicOr(p.status, bad);
+      if (bad && threadIdx.x == 0 && threadIdx.y == 0 && p.status != nullptr)
+        atomicOr(p.status, bad);
 
-    float c[VEC], s[VEC];
-    if (lane_rotates && table_ok) {
-      if (p.inreg_trig) {
-        const float pf = static_cast<float>(pos);
+      float c[VEC], s[VEC];
+      if (lane_rotates && table_ok) {
+        if (p.inreg_trig) {
+          const float pf = static_cast<float>(pos);
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + j));
-          sincosf(ang, &s[j], &c[j]);
-        }
-      } else {
-        const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
-        const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
-        if constexpr (VEC % 4 == 0) {
-          if (p.table_vec4) {
+          for (int j = 0; j < VEC; ++j) {
+            const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + j));
+            sincosf(ang, &s[j], &c[j]);
+          }
+        } else {
+          const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
+          const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
+          bool vec4 = false;
+          if constexpr (VEC % 4 == 0) vec4 = p.table_vec4 != 0;
+          if (vec4) {
 #pragma unroll
             for (int j = 0; j < VEC; j += 4) {
               const float4 cv = __ldg(reinterpret_cast<const float4*>(crow + j));
@@ -223,82 +334,29 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
 #pragma unroll
             for (int j = 0; j < VEC; ++j) { c[j] = __ldg(crow + j); s[j] = __ldg(srow + j); }
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) { c[j] = __ldg(crow + j); s[j] = __ldg(srow + j); }
         }
       }
-    }
 
-    // ---- everything below may depend on the preceding kernel ----
-    if (!waited) {
-      pdl_wait();
-      waited = true;
-    }
-
-    for (int r0 = grp; r0 < nrows; r0 += p.G * kMaxRowsInFlight) {
-      Pack<E, VB> x1[kMaxRowsInFlight], x2[kMaxRowsInFlight];
-      // Issue every load of this batch of rows first.
 #pragma unroll
-      for (int i = 0; i < kMaxRowsInFlight; ++i) {
-        const int r = r0 + i * p.G;
-        if (r < nrows) {
-          int kind, head;
-          row_kind<M>(p, r, kind, head);
-          const char* src;
-          if (kind == kRowQ) src = p.q + (t * p.q_ts + head * p.q_hs) * ES;
-          else if (kind == kRowK) src = p.k + (t * p.k_ts + head * p.k_hs) * ES;
-          else src = p.v + (t * p.v_ts + head * p.v_hs) * ES;
-          const bool rot = lane_rotates && kind != kRowV;
-          const int rb = (kind == kRowV || M == Mode::kAppend) ? 0 : p.R;
-          const int off1 = rot ? lane * VEC : rb + (lane - (rb ? p.nrot : 0)) * VEC;
-          const int off2 = rot ? half_r + lane * VEC : off1 + ((p.D - rb) >> 1);
-          x1[i].bits = load_stream<VB>(src + off1 * ES);
-          x2[i].bits = load_stream<VB>(src + off2 * ES);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kMaxRowsInFlight; ++i) {
-        const int r = r0 + i * p.G;
-        if (r < nrows) {
-          int kind, head;
-          row_kind<M>(p, r, kind, head);
-          const bool rot = lane_rotates && kind != kRowV;
-          const int rb = (kind == kRowV || M == Mode::kAppend) ? 0 : p.R;
-          const int off1 = rot ? lane * VEC : rb + (lane - (rb ? p.nrot : 0)) * VEC;
-          const int off2 = rot ? half_r + lane * VEC : off1 + ((p.D - rb) >> 1);
-          if (rot) {
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-              const float a = E::to_f(x1[i].e[j]);
-              const float b = E::to_f(x2[i].e[j]);
-              const float y1 = __fsub_rn(__fmul_rn(a, c[j]), __fmul_rn(b, s[j]));
-              const float y2 = __fadd_rn(__fmul_rn(b, c[j]), __fmul_rn(a, s[j]));
-              x1[i].e[j] = E::from_f(y1);
-              x2[i].e[j] = E::from_f(y2);
-            }
+      for (int i = 0; i < NR; ++i) {
+        if (kind[i] < 0) continue;
+        if (lane_rotates && kind[i] != kRowV) rotate_pack<E, VB>(x1[i], x2[i], c, s);
+        if (kind[i] == kRowQ) {
+          if (table_ok) {
+            char* dst = p.q_out + t * (static_cast<int64_t>(p.Hq) * p.D * ES) + dst_off[i];
+            store_keep<VB>(dst, x1[i].bits);
+            store_keep<VB>(dst + gap[i], x2[i].bits);
           }
-          if (kind == kRowQ) {
-            if (table_ok) {
-              char* dst = p.q_out + ((t * p.Hq + head) * static_cast<int64_t>(p.D)) * ES;
-              store_keep<VB>(dst + off1 * ES, x1[i].bits);
-              store_keep<VB>(dst + off2 * ES, x2[i].bits);
-            }
-          } else if (M == Mode::kRope) {
-            if (table_ok) {
-              char* dst = p.k_dst + ((t * p.Hkv + head) * static_cast<int64_t>(p.D)) * ES;
-              store_keep<VB>(dst + off1 * ES, x1[i].bits);
-              store_keep<VB>(dst + off2 * ES, x2[i].bits);
-            }
-          } else {
-            const bool ok = cache_ok && (kind == kRowV || M == Mode::kAppend || table_ok);
-            if (ok) {
-              char* base = kind == kRowK ? p.k_dst : p.v_dst;
-              char* dst = base + (slot + head * p.c_hs) * ES;
-              store_stream<VB>(dst + off1 * ES, x1[i].bits);
-              store_stream<VB>(dst + off2 * ES, x2[i].bits);
-            }
+        } else if (M == Mode::kRope) {
+          if (table_ok) {
+            char* dst = p.k_dst + t * (static_cast<int64_t>(p.Hkv) * p.D * ES) + dst_off[i];
+            store_keep<VB>(dst, x1[i].bits);
+            store_keep<VB>(dst + gap[i], x2[i].bits);
           }
+        } else if (cache_ok && (kind[i] == kRowV || M == Mode::kAppend || table_ok)) {
+          char* dst = (kind[i] == kRowK ? p.k_dst : p.v_dst) + slot * ES + dst_off[i];
+          store_stream<VB>(dst, x1[i].bits);
+          store_stream<VB>(dst + gap[i], x2[i].bits);
         }
       }
     }

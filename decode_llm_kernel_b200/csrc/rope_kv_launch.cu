@@ -4,8 +4,13 @@
 // width VB the alignment allows; this file maps (dtype, index type, VB, mode, cache kind) to a
 // kernel instantiation and launches it with cudaLaunchKernelEx, adding the programmatic
 // stream serialization attribute when the caller asked for PDL.
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "rope_kv_kernels.cuh"
 #include "rope_kv_launch.h"
+#include "rope_kv_staged.cuh"
 
 namespace drk {
 namespace {
@@ -14,7 +19,7 @@ template <typename E, typename Idx, int VB, Mode M, Cache C>
 cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(shape.grid, 1, 1);
-  cfg.blockDim = dim3(shape.threads, 1, 1);
+  cfg.blockDim = dim3(shape.lanes, shape.groups, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -70,7 +75,122 @@ cudaError_t launch_idx(const KernelParams& p, int index_bits, int vb, int mode, 
   return launch_vb<E, long long>(p, vb, mode, cache, shape, stream);
 }
 
+// ---- the staged (TMA bulk copy) kernel ----
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(device);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+    n = 1;
+  cache[device] = n;
+  return n;
+}
+
+template <typename E, typename Idx, int VB, Cache C>
+cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp,
+                              const LaunchShape& shape, cudaStream_t stream) {
+  auto kernel = rope_kv_staged_kernel<E, Idx, VB, C>;
+  const size_t smem = static_cast<size_t>(sp.stages) * (sp.stage_bytes + sizeof(uint64_t));
+  const int threads = shape.lanes * shape.groups;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  // Per instantiation and device: the dynamic shared-memory opt-in (raised once to the
+  // device's limit, so any stage size a later call needs is allowed) and the occupancy per
+  // (smem, threads).
+  static std::mutex mu;
+  static std::map<int, bool> opted_in;
+  static std::map<std::pair<int, std::pair<size_t, int>>, int> occupancy;
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!opted_in[device]) {
+      int limit = 0;
+      err = cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+      if (err != cudaSuccess) return err;
+      err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 limit - 1024);
+      if (err != cudaSuccess) return err;
+      opted_in[device] = true;
+    }
+    const auto key = std::make_pair(device, std::make_pair(smem, threads));
+    auto it = occupancy.find(key);
+    if (it == occupancy.end()) {
+      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+      if (err != cudaSuccess) return err;
+      if (per_sm < 1) return cudaErrorInvalidConfiguration;
+      occupancy[key] = per_sm;
+    } else {
+      per_sm = it->second;
+    }
+  }
+  const int64_t slots = static_cast<int64_t>(sm_count(device)) * per_sm;
+  const int grid = static_cast<int>(p.T < slots ? p.T : slots);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(shape.lanes, shape.groups, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (shape.pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, p, sp);
+}
+
+template <typename E, typename Idx, int VB>
+cudaError_t launch_staged_cache(const KernelParams& p, const StagedParams& sp, int cache,
+                                const LaunchShape& shape, cudaStream_t stream) {
+  if (cache == kCachePaged) return launch_staged_one<E, Idx, VB, Cache::kPaged>(p, sp, shape, stream);
+  return launch_staged_one<E, Idx, VB, Cache::kStrided>(p, sp, shape, stream);
+}
+
+template <typename E, typename Idx>
+cudaError_t launch_staged_vb(const KernelParams& p, const StagedParams& sp, int vb, int cache,
+                             const LaunchShape& shape, cudaStream_t stream) {
+  constexpr int es = static_cast<int>(sizeof(typename E::raw));
+  switch (vb) {
+    case 16: return launch_staged_cache<E, Idx, 16>(p, sp, cache, shape, stream);
+    case 8: return launch_staged_cache<E, Idx, 8>(p, sp, cache, shape, stream);
+    case 4:
+      if constexpr (es <= 4) return launch_staged_cache<E, Idx, 4>(p, sp, cache, shape, stream);
+      break;
+    case 2:
+      if constexpr (es <= 2) return launch_staged_cache<E, Idx, 2>(p, sp, cache, shape, stream);
+      break;
+    default:
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename E>
+cudaError_t launch_staged_idx(const KernelParams& p, const StagedParams& sp, int index_bits,
+                              int vb, int cache, const LaunchShape& shape, cudaStream_t stream) {
+  if (index_bits == 32) return launch_staged_vb<E, int>(p, sp, vb, cache, shape, stream);
+  return launch_staged_vb<E, long long>(p, sp, vb, cache, shape, stream);
+}
+
 }  // namespace
+
+cudaError_t launch_rope_kv_staged(const KernelParams& p, const StagedParams& sp, int elem_code,
+                                  int index_bits, int vb, int cache, const LaunchShape& shape,
+                                  cudaStream_t stream) {
+  switch (elem_code) {
+    case kElemF32: return launch_staged_idx<F32>(p, sp, index_bits, vb, cache, shape, stream);
+    case kElemF16: return launch_staged_idx<F16>(p, sp, index_bits, vb, cache, shape, stream);
+    case kElemBF16: return launch_staged_idx<BF16>(p, sp, index_bits, vb, cache, shape, stream);
+    case kElemF64: return launch_staged_idx<F64>(p, sp, index_bits, vb, cache, shape, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits, int vb,
                            int mode, int cache, const LaunchShape& shape, cudaStream_t stream) {

@@ -8,6 +8,17 @@ namespace drk {
 
 // Threads per block the kernels are compiled for (__launch_bounds__).
 constexpr int kMaxThreadsPerBlock = 256;
+constexpr int kStagedThreadsPerBlock = 128;
+
+// Head rows a thread holds in registers at once (its loads are all issued before any store),
+// and the blocks of kMaxThreadsPerBlock threads per SM the register budget is set for.
+#ifndef DRK_ROWS_PER_THREAD
+#define DRK_ROWS_PER_THREAD 3
+#endif
+#ifndef DRK_MIN_BLOCKS_PER_SM
+#define DRK_MIN_BLOCKS_PER_SM 1
+#endif
+constexpr int kRowsPerThread = DRK_ROWS_PER_THREAD;
 
 struct KernelParams {
   const char* q;              // Q (fused/rope)
@@ -40,13 +51,28 @@ enum { kModeFused = 0, kModeRope = 1, kModeAppend = 2 };
 enum { kCacheStrided = 0, kCachePaged = 1 };
 
 struct LaunchShape {
-  int grid;
-  int threads;
+  int grid;      // CTAs; each walks tokens blockIdx.x, blockIdx.x + grid, ...
+  int lanes;     // blockDim.x: lanes per head row (nslots)
+  int groups;    // blockDim.y: row groups (G)
   bool pdl;
 };
 
 cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits, int vb,
                            int mode, int cache, const LaunchShape& shape, cudaStream_t stream);
+
+// Stage geometry of the bulk-copy kernel (rope_kv_staged.cuh), in bytes.
+struct StagedParams {
+  uint32_t q_bytes;      // Hq * D * es: one token's Q rows
+  uint32_t kv_bytes;     // Hkv * D * es: one token's K (or V) rows
+  uint32_t stage_bytes;  // q_bytes + 2 * kv_bytes, rounded up to 128
+  int32_t stages;        // pipeline depth
+};
+
+// Fused mode only. shape.grid is ignored: the launcher sizes a persistent grid of
+// min(T, SMs x resident CTAs per SM).
+cudaError_t launch_rope_kv_staged(const KernelParams& p, const StagedParams& sp, int elem_code,
+                                  int index_bits, int vb, int cache, const LaunchShape& shape,
+                                  cudaStream_t stream);
 
 // smoke.cu
 cudaError_t launch_smoke_fill(void* data, int elem_code, int64_t numel, double value,

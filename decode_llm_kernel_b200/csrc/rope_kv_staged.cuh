@@ -1,0 +1,267 @@
+// Bandwidth-regime form of the fused RoPE + KV append: TMA bulk copies through shared memory.
+//
+// Used when many tokens are in one call (the host picks it by token count) and every row
+// block the op moves is contiguous: a token's Q heads, K heads and V heads each form one run
+// of H*D elements in the source (head stride == D; fused-QKV views qualify), q_out is
+// contiguous, and a cache slot [Hkv, D] is contiguous (token-major or paged caches).
+//
+// Per CTA, a persistent loop over tokens t = blockIdx.x, blockIdx.x + gridDim.x, ... with a
+// kStages-deep pipeline in shared memory:
+//   1. one thread issues cp.async.bulk global->shared copies of the token's Q, K and V row
+//      blocks, completing on the stage's mbarrier (expect_tx bytes);
+//   2. every thread reads the position, request index and its cos/sin slice (L2 hits) while
+//      the copy lands, then waits on the mbarrier (bounded: see below);
+//   3. threads rotate only the rotary dims of the Q and K rows, in place in shared memory
+//      (lane j: elements [j*VEC, +VEC) and [R/2 + j*VEC, +VEC), the rotate_half pair), with
+//      the same per-element roundings as the register kernel (bit-exact to the oracle);
+//   4. after a proxy fence and a barrier, one thread issues cp.async.bulk shared->global
+//      copies: the Q block to q_out[t], the K and V blocks to the token's cache slots. V rows
+//      and the pass-through dims of partial rotary never pass through registers;
+//   5. a stage is refilled with the token kStages ahead once the bulk stores that read it
+//      have finished reading (cp.async.bulk.wait_group.read).
+// No multicast, no clusters: every copy is this CTA's own.
+//
+// Waits. Each mbarrier wait is bounded (kWaitLimit polls). If a wait runs out -- a copy that
+// never lands, which no valid input produces -- the CTA sets DRK_STATUS_TIMEOUT in the status
+// word, stops issuing work, waits (bounded) for its own copies in flight and returns.
+#pragma once
+
+#include "rope_kv_kernels.cuh"
+
+namespace drk {
+
+constexpr int kStagedThreads = kStagedThreadsPerBlock;
+constexpr uint32_t kStatusTimeout = 1u << 4;
+constexpr long long kWaitLimit = 1ll << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// True once the barrier's phase with this parity has completed; false after kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (long long i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N committed bulk-store groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Shared-memory vector access of VB bytes.
+template <int VB>
+__device__ __forceinline__ typename VecBits<VB>::type lds(const unsigned char* p) {
+  return *reinterpret_cast<const typename VecBits<VB>::type*>(p);
+}
+template <int VB>
+__device__ __forceinline__ void sts(unsigned char* p, typename VecBits<VB>::type x) {
+  *reinterpret_cast<typename VecBits<VB>::type*>(p) = x;
+}
+
+template <typename E, typename Idx, int VB, Cache C>
+__global__ void __launch_bounds__(kStagedThreads)
+rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
+                      const __grid_constant__ StagedParams sp) {
+  using raw = typename E::raw;
+  constexpr int VEC = VB / static_cast<int>(sizeof(raw));
+  constexpr int64_t ES = static_cast<int64_t>(sizeof(raw));
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(sp.stages) *
+                                               sp.stage_bytes);
+  __shared__ int s_abort;
+
+  pdl_launch_dependents();
+
+  const int tid = static_cast<int>(threadIdx.x + threadIdx.y * blockDim.x);
+  const int lane = static_cast<int>(threadIdx.x);   // < nrot
+  const int grp = static_cast<int>(threadIdx.y);
+  const int rot_rows = p.Hq + p.Hkv;
+  const int64_t my_tokens = p.T > blockIdx.x ? (p.T - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int row_bytes = p.D * static_cast<int>(ES);
+
+  if (tid == 0) {
+    for (int st = 0; st < sp.stages; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  __syncthreads();
+  pdl_wait();   // q/k/v may be written by the preceding kernel
+
+  int64_t issued = 0;   // tokens whose copies thread 0 has issued
+  auto issue_load = [&](int64_t j) {
+    issued = j + 1;
+    const int64_t t = blockIdx.x + j * gridDim.x;
+    const int st = static_cast<int>(j % sp.stages);
+    unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
+    mbar_expect_tx(&bars[st], sp.q_bytes + 2 * sp.kv_bytes);
+    bulk_load(stage, p.q + t * p.q_ts * ES, sp.q_bytes, &bars[st]);
+    bulk_load(stage + sp.q_bytes, p.k + t * p.k_ts * ES, sp.kv_bytes, &bars[st]);
+    bulk_load(stage + sp.q_bytes + sp.kv_bytes, p.v + t * p.v_ts * ES, sp.kv_bytes, &bars[st]);
+  };
+
+  if (tid == 0) {
+    for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) issue_load(j);
+  }
+
+  const bool lane_rotates = lane < p.nrot;
+  const int off1 = lane * VEC * static_cast<int>(ES);
+  const int off2 = off1 + (p.R >> 1) * static_cast<int>(ES);
+  int64_t j = 0;
+  for (; j < my_tokens; ++j) {
+    const int64_t t = blockIdx.x + j * gridDim.x;
+    const int st = static_cast<int>(j % sp.stages);
+    const uint32_t parity = static_cast<uint32_t>((j / sp.stages) & 1);
+    unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
+
+    // Token metadata while the copy lands.
+    const int64_t pos = load_index<Idx>(p.positions, t);
+    const int64_t ri = load_index<Idx>(p.request_indices, t);
+    uint32_t bad = 0;
+    const bool table_ok = pos >= 0 && pos < p.table_rows;
+    if (!table_ok) bad |= kStatusPosTable;
+    const bool pos_ok = pos >= 0 && pos < p.S;
+    const bool ri_ok = ri >= 0 && ri < p.B;
+    if (!pos_ok) bad |= kStatusPosCache;
+    if (!ri_ok) bad |= kStatusRequest;
+    bool cache_ok = pos_ok && ri_ok;
+    int64_t slot = 0;
+    if constexpr (C == Cache::kStrided) {
+      slot = ri * p.c_bs + pos * p.c_ss;
+    } else if (cache_ok) {
+      const int64_t blk_i = pos / p.block_size;
+      const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
+      if (blk < 0 || blk >= p.num_blocks) {
+        bad |= kStatusBlock;
+        cache_ok = false;
+      }
+      slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
+    }
+    float c[VEC], s[VEC];
+    if (lane_rotates && table_ok) {
+      if (p.inreg_trig) {
+        const float pf = static_cast<float>(pos);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + e));
+          sincosf(ang, &s[e], &c[e]);
+        }
+      } else {
+        const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
+        const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
+        bool vec4 = false;
+        if constexpr (VEC % 4 == 0) vec4 = p.table_vec4 != 0;
+        if (vec4) {
+#pragma unroll
+          for (int e = 0; e < VEC; e += 4) {
+            const float4 cv = __ldg(reinterpret_cast<const float4*>(crow + e));
+            const float4 sv = __ldg(reinterpret_cast<const float4*>(srow + e));
+            c[e] = cv.x; c[e + 1] = cv.y; c[e + 2] = cv.z; c[e + 3] = cv.w;
+            s[e] = sv.x; s[e + 1] = sv.y; s[e + 2] = sv.z; s[e + 3] = sv.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) { c[e] = __ldg(crow + e); s[e] = __ldg(srow + e); }
+        }
+      }
+    }
+
+    if (!mbar_wait(&bars[st], parity)) {
+      atomicOr(&s_abort, 1);
+    }
+    __syncthreads();
+    if (s_abort) break;
+
+    // Rotate the rotary dims of the Q and K rows in place.
+    if (lane_rotates && table_ok) {
+      for (int r = grp; r < rot_rows; r += blockDim.y) {
+        unsigned char* row = stage + static_cast<size_t>(r) * row_bytes;
+        Pack<E, VB> x1, x2;
+        x1.bits = lds<VB>(row + off1);
+        x2.bits = lds<VB>(row + off2);
+        rotate_pack<E, VB>(x1, x2, c, s);
+        sts<VB>(row + off1, x1.bits);
+        sts<VB>(row + off2, x2.bits);
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    if (tid == 0) {
+      if (bad && p.status != nullptr) atomicOr(p.status, bad);
+      if (table_ok) bulk_store(p.q_out + t * static_cast<int64_t>(sp.q_bytes), stage, sp.q_bytes);
+      if (cache_ok) {
+        if (table_ok) bulk_store(p.k_dst + slot * ES, stage + sp.q_bytes, sp.kv_bytes);
+        bulk_store(p.v_dst + slot * ES, stage + sp.q_bytes + sp.kv_bytes, sp.kv_bytes);
+      }
+      bulk_commit();
+      // Refill the stage read by the previous token's stores once they have read it.
+      if (j >= 1 && j - 1 + sp.stages < my_tokens) {
+        bulk_wait_read<1>();
+        issue_load(j - 1 + sp.stages);
+      }
+    }
+  }
+
+  if (tid == 0) {
+    bulk_wait_read<0>();
+    if (s_abort) {
+      if (p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+      // Let copies still landing in this CTA's stages finish before the CTA exits.
+      for (int64_t k = j; k < issued; ++k) {
+        mbar_wait(&bars[k % sp.stages], static_cast<uint32_t>((k / sp.stages) & 1));
+      }
+    }
+  }
+}
+
+}  // namespace drk

@@ -37,7 +37,7 @@ def fused_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request
 
 def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
                             *, rotary_dim=0, pdl=False, strided_cache=False, inv_freq=None,
-                            q_out=None):
+                            q_out=None, path="auto"):
     """fused_rope_kv_append with:
     rotary_dim     rotate only the first rotary_dim dims (table [P, rotary_dim]), copy the rest;
     pdl            programmatic dependent launch (indices and table read before waiting on the
@@ -46,19 +46,23 @@ def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, requ
                    [B, Hkv, S, D] cache passed as cache.transpose(1, 2);
     inv_freq       fp32 [rotary_dim/2] device tensor: cos/sin from sincosf in registers
                    (within 1 ulp of the table path, not bit-exact);
-    q_out          write into this contiguous [T, Hq, D] tensor instead of a fresh one."""
+    q_out          write into this contiguous [T, Hq, D] tensor instead of a fresh one;
+    path           "auto" (default), "register" (the register kernel) or "staged" (the
+                   bulk-copy kernel that stages tokens through shared memory; refused with a
+                   RuntimeError when the layout does not allow it). "auto" takes the staged
+                   kernel for large token counts when it can."""
     return require().fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache,
                                              request_indices, rotary_dim, pdl, strided_cache,
-                                             inv_freq, q_out)
+                                             inv_freq, q_out, path)
 
 
 def paged_rope_kv_append(q, k, v, positions, cos, sin, k_pages, v_pages, block_table,
-                         request_indices, *, rotary_dim=0, pdl=False):
+                         request_indices, *, rotary_dim=0, pdl=False, path="auto"):
     """Fused RoPE + append into a paged cache: k_pages/v_pages [num_blocks, block_size, Hkv, D],
     block_table [num_requests, max_blocks] (positions' dtype). Token t goes to block
     block_table[ri[t], pos[t] // block_size], row pos[t] % block_size. Returns q_rot."""
     return require().paged_rope_kv_append(q, k, v, positions, cos, sin, k_pages, v_pages,
-                                          block_table, request_indices, rotary_dim, pdl)
+                                          block_table, request_indices, rotary_dim, pdl, path)
 
 
 def rope_forward_ex(q, k, positions, cos, sin, *, rotary_dim=0, pdl=False):

@@ -59,7 +59,9 @@ enum {
   DRK_STATUS_POSITION_OUT_OF_CACHE = 1u << 0, /* position < 0 or >= cache_alloc_len */
   DRK_STATUS_REQUEST_OUT_OF_RANGE = 1u << 1,  /* request index < 0 or >= batch */
   DRK_STATUS_POSITION_OUT_OF_TABLE = 1u << 2, /* position >= rows of the cos/sin table */
-  DRK_STATUS_BLOCK_OUT_OF_RANGE = 1u << 3     /* paged cache: block id outside the pool */
+  DRK_STATUS_BLOCK_OUT_OF_RANGE = 1u << 3,    /* paged cache: block id outside the pool */
+  DRK_STATUS_TIMEOUT = 1u << 4                /* a bounded in-kernel wait ran out; the CTA
+                                                 stopped early (no valid input causes this) */
 };
 
 /* Launch options (drk_options.flags). */
@@ -75,7 +77,13 @@ enum {
   DRK_FLAG_STRIDED_CACHE = 1u << 1,
   /* Take cos/sin from sincosf of position * inv_freq in registers instead of the table
    * (needs drk_options.inv_freq). Within 1 ulp of the table path, not bit-exact. */
-  DRK_FLAG_INREG_TRIG = 1u << 2
+  DRK_FLAG_INREG_TRIG = 1u << 2,
+  /* Kernel choice for the fused op. By default calls with many tokens whose Q/K/V row blocks
+   * and cache slots are contiguous and 16-byte aligned use the bulk-copy (TMA) kernel that
+   * stages tokens through shared memory; other calls use the register kernel. These force
+   * one (forcing the bulk-copy kernel on an ineligible layout returns DRK_ERR_UNSUPPORTED). */
+  DRK_FLAG_FORCE_REGISTER_PATH = 1u << 3,
+  DRK_FLAG_FORCE_STAGED_PATH = 1u << 4
 };
 
 /* A strided view of device (or host) memory. Sizes and strides are in elements; unused

@@ -47,7 +47,7 @@ def _oracle_args(args):
 # ---------------------------------------------------------------- golden fixtures
 
 @pytest.mark.parametrize("name", names())
-@pytest.mark.parametrize("impl", ["fused", "separate", "fused_pdl"])
+@pytest.mark.parametrize("impl", ["fused", "separate", "fused_pdl", "register", "staged"])
 def test_golden_fixture_bit_exact(name, impl):
     g = Golden(name, device="cuda")
     m = g.meta
@@ -70,6 +70,14 @@ def test_golden_fixture_bit_exact(name, impl):
         q_out, k_rot = o.rope_forward_ex(g.q, g.k, g.positions, g.cos, g.sin)
         o.kv_append_ex(k_rot, g.v, g.positions, g.request_indices, kv, vv,
                        strided_cache=extra.get("strided_cache", False))
+    elif impl in ("register", "staged"):
+        if impl == "staged" and m["cache_layout"] != "token_major":
+            with pytest.raises(RuntimeError, match="bulk-copy kernel cannot take this call"):
+                o.fused_rope_kv_append_ex(g.q, g.k, g.v, g.positions, g.cos, g.sin, kv, vv,
+                                          g.request_indices, path="staged", **extra)
+            return
+        q_out = o.fused_rope_kv_append_ex(g.q, g.k, g.v, g.positions, g.cos, g.sin, kv, vv,
+                                          g.request_indices, path=impl, **extra)
     else:
         q_out = o.fused_rope_kv_append_ex(g.q, g.k, g.v, g.positions, g.cos, g.sin, kv, vv,
                                           g.request_indices, pdl=(impl == "fused_pdl"), **extra)
@@ -468,3 +476,80 @@ def test_fp32_margin_is_zero():
     assert report["ok"]
     assert report["max_abs_diff_q"] == 0.0 < TOLERANCES[torch.float32]["atol"]
     assert report["max_abs_diff_k_cache"] == 0.0
+
+
+# ---------------------------------------------------------------- the bulk-copy (staged) kernel
+
+@pytest.mark.parametrize("dtype_label", ["bf16", "fp16", "fp32", "fp64"])
+@pytest.mark.parametrize("head_cfg", HEAD_CONFIGS, ids=[h[0] for h in HEAD_CONFIGS])
+@pytest.mark.parametrize("layout", [PACKED, STRIDED])
+def test_staged_kernel_bit_exact(dtype_label, head_cfg, layout):
+    """Large token counts take the staged kernel by default; force it and compare."""
+    cfg = cfg_for(head_cfg, dtype_label, batch=1100, alloc=64, layout=layout,
+                  request_mapping="permuted")
+    p = pos.build_position_sets(1100, 64, pos.RAGGED, SEED, 1, "cuda")[0]
+    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    ref = _oracle_args(a)
+    q_ref = oracle.fused_rope_kv_append(*ref)
+    for path in ("staged", "auto"):
+        b = a._replace(k_cache=a.k_cache.clone(), v_cache=a.v_cache.clone())
+        q = ops().fused_rope_kv_append_ex(*b, path=path)
+        assert bits_equal(q.cpu(), q_ref), path
+        assert bits_equal(b.k_cache.cpu(), ref[6]), path
+        assert bits_equal(b.v_cache.cpu(), ref[7]), path
+
+
+@pytest.mark.parametrize("T", [1, 7, 148, 1000])
+def test_staged_kernel_token_counts_and_partial_rotary(T):
+    cfg = Config("phi2", 32, 32, 80, T, 128, "fp16", pos.RAGGED, rotary_dim=32)
+    p = pos.build_position_sets(T, 128, pos.RAGGED, SEED, 1, "cuda")[0]
+    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    ref = _oracle_args(a)
+    q_ref = oracle.fused_rope_kv_append(*ref)
+    q = ops().fused_rope_kv_append_ex(*a, rotary_dim=32, path="staged")
+    assert bits_equal(q.cpu(), q_ref)
+    assert bits_equal(a.k_cache.cpu(), ref[6])
+    assert bits_equal(a.v_cache.cpu(), ref[7])
+
+
+def test_staged_kernel_paged_cache():
+    T, Hq, Hkv, D, S, bs = 400, 32, 8, 128, 256, 16
+    cfg = Config("gqa", Hq, Hkv, D, T, S, "bf16", pos.RAGGED, request_mapping="permuted")
+    p = pos.build_position_sets(T, S, pos.RAGGED, SEED, 1, "cuda")[0]
+    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    max_blocks = S // bs
+    num_blocks = T * max_blocks + 5
+    perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(3))[
+        : T * max_blocks].view(T, max_blocks)
+    k_pages = torch.full((num_blocks, bs, Hkv, D), 7.5, dtype=torch.bfloat16, device="cuda")
+    v_pages = torch.full_like(k_pages, 7.5)
+    q = ops().paged_rope_kv_append(a.q, a.k, a.v, a.positions, a.cos, a.sin, k_pages, v_pages,
+                                   perm.cuda(), a.request_indices, path="staged")
+    ref = _oracle_args(a)
+    q_ref = oracle.fused_rope_kv_append(*ref)
+    assert bits_equal(q.cpu(), q_ref)
+    ri, pp = a.request_indices.long().cpu(), a.positions.long().cpu()
+    blk, row = perm[ri, pp // bs], pp % bs
+    assert bits_equal(k_pages.cpu()[blk, row], ref[6][ri, pp])
+    assert bits_equal(v_pages.cpu()[blk, row], ref[7][ri, pp])
+
+
+def test_staged_kernel_out_of_range_and_pdl():
+    from decode_llm_kernel_b200 import cuda
+    cuda.read_status(clear=True)
+    cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=300, alloc=32)
+    p = torch.randint(0, 32, (300,), generator=torch.Generator().manual_seed(1))
+    p[5] = 32        # outside the cache and the table
+    a = build_op_args(cfg, "cuda", SEED, p.cuda(), sentinel_cache=True)
+    q = ops().fused_rope_kv_append_ex(*a, path="staged", pdl=True)
+    assert cuda.read_status() & 5
+    kc = a.k_cache.cpu()
+    assert bool((kc[5] == 7.5).all())
+    good = torch.ones(300, dtype=torch.bool)
+    good[5] = False
+    pv = p.clone()
+    pv[5] = 0
+    a2 = build_op_args(cfg, "cuda", SEED, pv.cuda(), sentinel_cache=True)
+    ref = _oracle_args(a2)
+    q_ref = oracle.fused_rope_kv_append(*ref)
+    assert bits_equal(q.cpu()[good], q_ref[good])
