@@ -243,9 +243,16 @@ struct Aligner {
 struct Shape {
   int vb;
   int nslots, nrot, G, threads;
+  int rows;   // head rows per thread in flight
 };
 
-Shape plan(const Aligner& al, int nrows, bool rotates) {
+// Small batches run one head row per thread (more threads per token, shorter per-thread
+// chains: the latency regime); larger ones kRowsPerThread rows per thread.
+#ifndef DRK_SMALL_BATCH_TOKENS
+#define DRK_SMALL_BATCH_TOKENS 256
+#endif
+
+Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens) {
   Shape s{};
   s.vb = al.pick();
   if (s.vb == 0) throw Unsupported("tensors are not aligned to their element size");
@@ -257,9 +264,11 @@ Shape plan(const Aligner& al, int nrows, bool rotates) {
                           drk::kMaxThreadsPerBlock, " are supported"));
   s.nslots = static_cast<int>(nslots);
   s.nrot = rotates ? static_cast<int>(al.R / (2 * vec)) : 0;
-  // kRowsPerThread rows per thread; a block holds whole row groups.
-  const int want_groups = std::max(1, (nrows + drk::kRowsPerThread - 1) / drk::kRowsPerThread);
-  s.G = std::max(1, std::min(want_groups, drk::kMaxThreadsPerBlock / s.nslots));
+  s.rows = tokens <= DRK_SMALL_BATCH_TOKENS ? 1 : drk::kRowsPerThread;
+  const int max_threads = s.rows == 1 ? 1024 : drk::kMaxThreadsPerBlock;
+  // `rows` rows per thread; a block holds whole row groups.
+  const int want_groups = std::max(1, (nrows + s.rows - 1) / s.rows);
+  s.G = std::max(1, std::min(want_groups, max_threads / s.nslots));
   s.threads = s.G * s.nslots;
   return s;
 }
@@ -267,7 +276,7 @@ Shape plan(const Aligner& al, int nrows, bool rotates) {
 // The bulk-copy kernel's plan: eligible only if every row block it copies is one contiguous,
 // 16-byte-aligned run.
 #ifndef DRK_STAGED_MIN_TOKENS
-#define DRK_STAGED_MIN_TOKENS 1024
+#define DRK_STAGED_MIN_TOKENS 512
 #endif
 
 struct StagedPlan {
@@ -520,8 +529,9 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
   for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
   const int nrows = static_cast<int>(Hq + 2 * Hkv);
-  const Shape s = plan(al, nrows, true);
-  p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G;
+  const Shape s = plan(al, nrows, true, T);
+  p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
+  p.pdl = pdl ? 1 : 0;
 
   DeviceGuard guard(device);
   const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, pdl};
@@ -620,8 +630,9 @@ int drk_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor*
     for (const drk_tensor* t : {q, k, q_out, k_out}) al.ptr(t->data);
     al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
     al.stride(T, k->strides[0]); al.stride(Hkv, k->strides[1]);
-    const Shape s = plan(al, static_cast<int>(Hq + Hkv), true);
-    p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G;
+    const Shape s = plan(al, static_cast<int>(Hq + Hkv), true, T);
+    p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
+    p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
     DeviceGuard guard(device);
     const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
     const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
@@ -684,8 +695,9 @@ int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor
     al.stride(T, k_rot->strides[0]); al.stride(Hkv, k_rot->strides[1]);
     al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
     for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
-    const Shape s = plan(al, static_cast<int>(2 * Hkv), false);
-    p.nslots = s.nslots; p.nrot = 0; p.G = s.G;
+    const Shape s = plan(al, static_cast<int>(2 * Hkv), false, T);
+    p.nslots = s.nslots; p.nrot = 0; p.G = s.G; p.rows_per_thread = s.rows;
+    p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
     DeviceGuard guard(device);
     const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
     const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;

@@ -51,7 +51,6 @@ namespace drk {
 enum class Mode : int { kFused = 0, kRope = 1, kAppend = 2 };
 enum class Cache : int { kStrided = 0, kPaged = 1 };
 
-constexpr int kMaxRowsInFlight = kRowsPerThread;
 constexpr int kMinBlocksPerSM = DRK_MIN_BLOCKS_PER_SM;
 
 enum : uint32_t {
@@ -210,13 +209,25 @@ __device__ __forceinline__ void row_kind(const KernelParams& p, int r, int& kind
   }
 }
 
-template <typename E, typename Idx, int VB, Mode M, Cache C>
-__global__ void __launch_bounds__(kMaxThreadsPerBlock, kMinBlocksPerSM)
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Threads per block the kernel is compiled for: NR == 1 (one head row per thread, the small-batch
+// shape) runs up to 1024 threads, otherwise kMaxThreadsPerBlock.
+template <int NR>
+struct RegisterKernelBounds {
+  static constexpr int kThreads = NR == 1 ? 1024 : kMaxThreadsPerBlock;
+  static constexpr int kMinBlocks = NR == 1 ? 1 : kMinBlocksPerSM;
+};
+
+template <typename E, typename Idx, int VB, Mode M, Cache C, int NR>
+__global__ void __launch_bounds__(RegisterKernelBounds<NR>::kThreads,
+                                  RegisterKernelBounds<NR>::kMinBlocks)
 rope_kv_kernel(const __grid_constant__ KernelParams p) {
   using raw = typename E::raw;
   constexpr int VEC = VB / static_cast<int>(sizeof(raw));
   constexpr int64_t ES = static_cast<int64_t>(sizeof(raw));
-  constexpr int NR = kMaxRowsInFlight;
 
   // Let the next kernel in the stream start its own prologue while this one runs.
   pdl_launch_dependents();
@@ -233,6 +244,7 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
   const int qk_off2 = lane_rotates ? (p.R >> 1) + lane * VEC : qk_off1 + ((p.D - qk_base) >> 1);
   const int v_off1 = lane * VEC;
   const int v_off2 = v_off1 + (p.D >> 1);
+  const bool lead = threadIdx.x == 0 && threadIdx.y == 0;
   bool waited = false;
 
   for (int r0 = grp; r0 < nrows; r0 += p.G * NR) {
@@ -258,84 +270,117 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
     }
 
     for (int64_t t = blockIdx.x; t < p.T; t += gridDim.x) {
-      // Indices first: they never come from the preceding kernel, and nothing below waits on
-      // them until the row loads are in flight.
+      const char* src[NR];
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        const char* base = kind[i] == kRowQ ? p.q + t * p.q_ts * ES
+                         : kind[i] == kRowK ? p.k + t * p.k_ts * ES
+                                            : p.v + t * p.v_ts * ES;
+        src[i] = base + src_off[i];
+      }
+      // Indices first: they never come from the preceding kernel.
       const int64_t pos = load_index<Idx>(p.positions, t);
       int64_t ri = 0;
       if constexpr (M != Mode::kRope) ri = load_index<Idx>(p.request_indices, t);
-      if (!waited) {
-        pdl_wait();   // q/k/v may be written by the preceding kernel
-        waited = true;
-      }
 
-      Pack<E, VB> x1[NR], x2[NR];
-#pragma unroll
-      for (int i = 0; i < NR; ++i) {
-        if (kind[i] >= 0) {
-          const char* base = kind[i] == kRowQ ? p.q + t * p.q_ts * ES
-                           : kind[i] == kRowK ? p.k + t * p.k_ts * ES
-                                              : p.v + t * p.v_ts * ES;
-          const char* src = base + src_off[i];
-          x1[i].bits = load_stream<VB>(src);
-          x2[i].bits = load_stream<VB>(src + gap[i]);
-        }
-      }
-
-      // ---- bounds, destination slot and the table slice (needs the position) ----
       uint32_t bad = 0;
-      const bool table_ok = pos >= 0 && pos < p.table_rows;
-      if (!table_ok && M != Mode::kAppend) bad |= kStatusPosTable;
-      bool cache_ok = true;
+      bool table_ok = false, cache_ok = true;
       int64_t slot = 0;
-      if constexpr (M != Mode::kRope) {
-        const bool pos_ok = pos >= 0 && pos < p.S;
-        const bool ri_ok = ri >= 0 && ri < p.B;
-        if (!pos_ok) bad |= kStatusPosCache;
-        if (!ri_ok) bad |= kStatusRequest;
-        cache_ok = pos_ok && ri_ok;
-        if constexpr (C == Cache::kStrided) {
-          slot = ri * p.c_bs + pos * p.c_ss;
-        } else if (cache_ok) {
-          const int64_t blk_i = pos / p.block_size;
-          const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
-          if (blk < 0 || blk >= p.num_blocks) {
-            bad |= kStatusBlock;
-            cache_ok = false;
-          }
-          slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
-        }
-      }
-      if (bad && threadIdx.x == 0 && threadIdx.y == 0 && p.status != nullptr)
-        atomicOr(p.status, bad);
-
       float c[VEC], s[VEC];
-      if (lane_rotates && table_ok) {
-        if (p.inreg_trig) {
-          const float pf = static_cast<float>(pos);
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) {
-            const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + j));
-            sincosf(ang, &s[j], &c[j]);
+      // Bounds, destination slot and the table slice: everything that needs the position.
+      auto resolve = [&]() {
+        table_ok = pos >= 0 && pos < p.table_rows;
+        if (!table_ok && M != Mode::kAppend) bad |= kStatusPosTable;
+        if constexpr (M != Mode::kRope) {
+          const bool pos_ok = pos >= 0 && pos < p.S;
+          const bool ri_ok = ri >= 0 && ri < p.B;
+          if (!pos_ok) bad |= kStatusPosCache;
+          if (!ri_ok) bad |= kStatusRequest;
+          cache_ok = pos_ok && ri_ok;
+          if constexpr (C == Cache::kStrided) {
+            slot = ri * p.c_bs + pos * p.c_ss;
+          } else if (cache_ok) {
+            const int64_t blk_i = pos / p.block_size;
+            const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
+            if (blk < 0 || blk >= p.num_blocks) {
+              bad |= kStatusBlock;
+              cache_ok = false;
+            }
+            slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
           }
-        } else {
-          const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
-          const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
-          bool vec4 = false;
-          if constexpr (VEC % 4 == 0) vec4 = p.table_vec4 != 0;
-          if (vec4) {
+          // Warm the address translation of this token's cache slots before the stores.
+          if (cache_ok && lead) {
+            prefetch_l2(p.k_dst + slot * ES);
+            prefetch_l2(p.v_dst + slot * ES);
+          }
+        }
+        if (lane_rotates && table_ok) {
+          if (p.inreg_trig) {
+            const float pf = static_cast<float>(pos);
 #pragma unroll
-            for (int j = 0; j < VEC; j += 4) {
-              const float4 cv = __ldg(reinterpret_cast<const float4*>(crow + j));
-              const float4 sv = __ldg(reinterpret_cast<const float4*>(srow + j));
-              c[j] = cv.x; c[j + 1] = cv.y; c[j + 2] = cv.z; c[j + 3] = cv.w;
-              s[j] = sv.x; s[j + 1] = sv.y; s[j + 2] = sv.z; s[j + 3] = sv.w;
+            for (int j = 0; j < VEC; ++j) {
+              const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + j));
+              sincosf(ang, &s[j], &c[j]);
             }
           } else {
+            const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
+            const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
+            bool vec4 = false;
+            if constexpr (VEC % 4 == 0) vec4 = p.table_vec4 != 0;
+            if (vec4) {
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) { c[j] = __ldg(crow + j); s[j] = __ldg(srow + j); }
+              for (int j = 0; j < VEC; j += 4) {
+                const float4 cv = __ldg(reinterpret_cast<const float4*>(crow + j));
+                const float4 sv = __ldg(reinterpret_cast<const float4*>(srow + j));
+                c[j] = cv.x; c[j + 1] = cv.y; c[j + 2] = cv.z; c[j + 3] = cv.w;
+                s[j] = sv.x; s[j + 1] = sv.y; s[j + 2] = sv.z; s[j + 3] = sv.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < VEC; ++j) { c[j] = __ldg(crow + j); s[j] = __ldg(srow + j); }
+            }
           }
         }
+      };
+
+      Pack<E, VB> x1[NR], x2[NR];
+      auto load_rows = [&]() {
+#pragma unroll
+        for (int i = 0; i < NR; ++i) {
+          if (kind[i] >= 0) {
+            x1[i].bits = load_stream<VB>(src[i]);
+            x2[i].bits = load_stream<VB>(src[i] + gap[i]);
+          }
+        }
+      };
+
+      if (!waited && p.pdl) {
+        // Launched as a dependent: the preceding kernel may still be writing q/k/v, so they are
+        // only loaded after griddepcontrol.wait. Until then, pull their lines toward L2 (L2 is
+        // the coherence point, so a line written later is still read fresh) and resolve
+        // everything that needs the position.
+#pragma unroll
+        for (int i = 0; i < NR; ++i) {
+          if (kind[i] >= 0) {
+            prefetch_l2(src[i]);
+            prefetch_l2(src[i] + gap[i]);
+          }
+        }
+        resolve();
+        pdl_wait();
+        waited = true;
+        load_rows();
+      } else {
+        if (!waited) {
+          pdl_wait();   // returns at once when not launched as a dependent
+          waited = true;
+        }
+        // Row loads first: they do not depend on the position, so they are in flight while the
+        // position-dependent work resolves.
+        load_rows();
+        resolve();
       }
+      if (bad && lead && p.status != nullptr) atomicOr(p.status, bad);
 
 #pragma unroll
       for (int i = 0; i < NR; ++i) {

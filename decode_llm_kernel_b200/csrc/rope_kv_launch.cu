@@ -15,7 +15,7 @@
 namespace drk {
 namespace {
 
-template <typename E, typename Idx, int VB, Mode M, Cache C>
+template <typename E, typename Idx, int VB, Mode M, Cache C, int NR>
 cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(shape.grid, 1, 1);
@@ -29,24 +29,31 @@ cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStre
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, rope_kv_kernel<E, Idx, VB, M, C>, p);
+  return cudaLaunchKernelEx(&cfg, rope_kv_kernel<E, Idx, VB, M, C, NR>, p);
+}
+
+template <typename E, typename Idx, int VB, int NR>
+cudaError_t launch_mode_nr(const KernelParams& p, int mode, int cache, const LaunchShape& shape,
+                           cudaStream_t stream) {
+  switch (mode) {
+    case kModeFused:
+      if (cache == kCachePaged)
+        return launch_one<E, Idx, VB, Mode::kFused, Cache::kPaged, NR>(p, shape, stream);
+      return launch_one<E, Idx, VB, Mode::kFused, Cache::kStrided, NR>(p, shape, stream);
+    case kModeRope:
+      return launch_one<E, Idx, VB, Mode::kRope, Cache::kStrided, NR>(p, shape, stream);
+    case kModeAppend:
+      return launch_one<E, Idx, VB, Mode::kAppend, Cache::kStrided, NR>(p, shape, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 template <typename E, typename Idx, int VB>
 cudaError_t launch_mode(const KernelParams& p, int mode, int cache, const LaunchShape& shape,
                         cudaStream_t stream) {
-  switch (mode) {
-    case kModeFused:
-      if (cache == kCachePaged)
-        return launch_one<E, Idx, VB, Mode::kFused, Cache::kPaged>(p, shape, stream);
-      return launch_one<E, Idx, VB, Mode::kFused, Cache::kStrided>(p, shape, stream);
-    case kModeRope:
-      return launch_one<E, Idx, VB, Mode::kRope, Cache::kStrided>(p, shape, stream);
-    case kModeAppend:
-      return launch_one<E, Idx, VB, Mode::kAppend, Cache::kStrided>(p, shape, stream);
-    default:
-      return cudaErrorInvalidValue;
-  }
+  if (p.rows_per_thread == 1) return launch_mode_nr<E, Idx, VB, 1>(p, mode, cache, shape, stream);
+  return launch_mode_nr<E, Idx, VB, kRowsPerThread>(p, mode, cache, shape, stream);
 }
 
 template <typename E, typename Idx>

@@ -44,6 +44,8 @@ struct KernelParams {
   int32_t nslots, nrot, G;
   int32_t inreg_trig;
   int32_t table_vec4;         // table base and row stride allow 16-byte loads
+  int32_t pdl;                // launched with programmatic dependent launch
+  int32_t rows_per_thread;    // register kernel: 1 (small batches) or kRowsPerThread
 };
 
 enum { kElemF32 = 0, kElemF16 = 1, kElemBF16 = 2, kElemF64 = 3 };

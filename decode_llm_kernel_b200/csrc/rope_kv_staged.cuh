@@ -186,6 +186,11 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
       }
       slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
     }
+    // Warm the address translation of this token's cache slots before the bulk stores.
+    if (cache_ok && tid == 0) {
+      prefetch_l2(p.k_dst + slot * ES);
+      prefetch_l2(p.v_dst + slot * ES);
+    }
     float c[VEC], s[VEC];
     if (lane_rotates && table_ok) {
       if (p.inreg_trig) {
