@@ -57,7 +57,7 @@ def parse_args():
     p.add_argument("--mode", choices=["full", "bw"], default="full",
                    help="bw: only the bandwidth-bound launch loop (for profiling small cases)")
     p.add_argument("--cache-len", type=int, default=0,
-                   help="bw mode: override cache_alloc_len (keeps a profiled case small)")
+                   help="override cache_alloc_len (profiling runs only: keeps a case small)")
     p.add_argument("--launches", type=int, default=400, help="bw mode: timed launches")
     return p.parse_args()
 
@@ -259,7 +259,10 @@ def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
 
     def call(i):
         q, k, v, p, ri, qo = sets[i % nsets]
-        ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo)
+        # Back-to-back launches never write each other's positions, indices or tables, so
+        # each may start its prologue while the previous one drains (programmatic dependent
+        # launch); the q/k/v reads still wait for the previous launch to finish.
+        ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo, pdl=True)
 
     # Launches are replayed from a CUDA graph so host call overhead cannot pace the GPU.
     for i in range(nsets):
@@ -289,7 +292,8 @@ def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
     del graph
     gbs_rank = w.bytes_per_call() / per_launch_s / 1e9
     out = {"workload": "mistral_b4096", "batch_per_gpu": w.batch, "dtype": w.dtype_label,
-           "cache_alloc_len": w.cache_alloc_len, "launches": iters,
+           "cache_alloc_len": w.cache_alloc_len, "launches": iters, "pdl": True,
+           "kernel": "drk::rope_kv_staged_kernel (TMA bulk copies, 3-stage mbarrier pipeline)",
            "bytes_per_launch": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
            "achieved_gbs_per_gpu": gbs_rank, "frac_of_peak": gbs_rank / peak,
            "aggregate_gbs": gbs_rank * world, "input_sets": nsets}
@@ -305,6 +309,10 @@ def run_ours(args, world, rank, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     w = WORKLOADS[args.workload].shard_for(rank, world)
+    if args.cache_len:
+        # profiling runs only: smaller caches, same per-token work (one slot per token)
+        from dataclasses import replace
+        w = replace(w, cache_alloc_len=args.cache_len)
     peak, peak_src = measured_hbm_peak()
     cos, sin = build_tables(w, device)
     nsets = sets_needed(w)
@@ -327,7 +335,7 @@ def run_ours(args, world, rank, local):
     barrier(world)
     ms_max = max_over_ranks(ms, world)
     sampler.stop()
-    clocks = sampler.summary(t_timed0, t_timed1)
+    clocks = sampler.summary(t_load0, t_timed1)
     cuda.check_status(local)
 
     per_step_s = ms_max / 1e3 / args.steps
@@ -342,32 +350,38 @@ def run_ours(args, world, rank, local):
                 "note": "average launch = graph step time / layers, so it includes the gaps "
                         "between the chained launches"}
 
-    # end to end: one graph per step that copies q/k/v/positions in from pinned host memory,
-    # runs the layers, and copies q_out back
+    # end to end: the public API's pipelined host path -- one graph holding `depth` decode
+    # steps, each copying its q/k/v/positions in from pinned host memory and its q_out back
     e2e = None
     if not args.no_e2e:
-        host = pinned_like(sets[0])
-        e2e_cap = step.capture(sets[0], host=host)
-        h2d = sum(t.numel() * t.element_size() for t in (host.q, host.k, host.v,
-                                                          host.positions, host.request_indices))
-        d2h = e2e_cap.host_q_out.numel() * e2e_cap.host_q_out.element_size()
-        for _ in range(max(3, args.warmup // 4)):
-            e2e_cap.replay()
+        depth = min(8, nsets)
+        hosts = [pinned_like(sets[i]) for i in range(depth)]
+        pipe = step.capture_host_pipeline(sets[:depth], hosts)
+        h2d = sum(t.numel() * t.element_size() for t in (hosts[0].q, hosts[0].k, hosts[0].v,
+                                                          hosts[0].positions,
+                                                          hosts[0].request_indices))
+        d2h = pipe.host_q_outs[0].numel() * pipe.host_q_outs[0].element_size()
+        for _ in range(3):
+            pipe.replay()
         torch.cuda.synchronize()
-        e2e_steps = max(10, min(args.steps, 400))
+        replays = max(3, min(args.steps, 400) // depth)
         barrier(world)
         t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            e2e_cap.replay()
+        for _ in range(replays):
+            pipe.replay()
         torch.cuda.synchronize()
         e2e_s = max_over_ranks(time.perf_counter() - t0, world)
         barrier(world)
+        e2e_steps = replays * depth
         e2e = {"value": world * bytes_step * e2e_steps / e2e_s / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "us_per_step": e2e_s / e2e_steps * 1e6, "steps": e2e_steps,
-               "path": "DecodeStep.capture(host=pinned): H2D copies + 32 fused launches + "
-                       "D2H copy in one graph, wall clock with a sync on both sides"}
-        e2e_cap.release()
+               "path": f"DecodeStep.capture_host_pipeline: {depth} steps per graph, each "
+                       "copying q/k/v/positions in from pinned host memory, running the 32 "
+                       "fused launches and copying q_out back; copies on their own streams; "
+                       "wall clock with a sync on both sides"}
+        pipe.release()
+        del hosts
 
     floor = None if args.no_floor else launch_floor(stream, w.layers)
     del captured, sets, k_caches, v_caches, step

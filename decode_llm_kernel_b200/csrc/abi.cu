@@ -278,6 +278,13 @@ Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens) {
 #ifndef DRK_STAGED_MIN_TOKENS
 #define DRK_STAGED_MIN_TOKENS 512
 #endif
+// Pipeline depth of the bulk-copy kernel and the shared memory one CTA may use for its stages.
+#ifndef DRK_STAGED_STAGES
+#define DRK_STAGED_STAGES 3
+#endif
+#ifndef DRK_STAGED_SMEM_BUDGET
+#define DRK_STAGED_SMEM_BUDGET (192 * 1024)
+#endif
 
 struct StagedPlan {
   bool ok = false;
@@ -327,7 +334,7 @@ StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tenso
   pl.groups = static_cast<int>(std::max<int64_t>(
       1, std::min<int64_t>(rot_rows, drk::kStagedThreadsPerBlock / pl.nrot)));
   const int64_t stage = (q_bytes + 2 * kv_bytes + 127) / 128 * 128;
-  int stages = static_cast<int>(std::min<int64_t>(4, (96 * 1024) / stage));
+  int stages = static_cast<int>(std::min<int64_t>(DRK_STAGED_STAGES, DRK_STAGED_SMEM_BUDGET / stage));
   if (stages < 2) {
     if (2 * stage > 200 * 1024) return fail("one token's rows do not fit two shared-memory stages");
     stages = 2;

@@ -9,8 +9,9 @@
 // kStages-deep pipeline in shared memory:
 //   1. one thread issues cp.async.bulk global->shared copies of the token's Q, K and V row
 //      blocks, completing on the stage's mbarrier (expect_tx bytes);
-//   2. every thread reads the position, request index and its cos/sin slice (L2 hits) while
-//      the copy lands, then waits on the mbarrier (bounded: see below);
+//   2. every thread waits on the stage's mbarrier (bounded: see below); the position, request
+//      index, slot and cos/sin slice of a token were fetched while earlier tokens were being
+//      processed (two tokens ahead for the indices, one for the rest);
 //   3. threads rotate only the rotary dims of the Q and K rows, in place in shared memory
 //      (lane j: elements [j*VEC, +VEC) and [R/2 + j*VEC, +VEC), the rotate_half pair), with
 //      the same per-element roundings as the register kernel (bit-exact to the oracle);
@@ -156,43 +157,46 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
   const bool lane_rotates = lane < p.nrot;
   const int off1 = lane * VEC * static_cast<int>(ES);
   const int off2 = off1 + (p.R >> 1) * static_cast<int>(ES);
-  int64_t j = 0;
-  for (; j < my_tokens; ++j) {
-    const int64_t t = blockIdx.x + j * gridDim.x;
-    const int st = static_cast<int>(j % sp.stages);
-    const uint32_t parity = static_cast<uint32_t>((j / sp.stages) & 1);
-    unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
 
-    // Token metadata while the copy lands.
-    const int64_t pos = load_index<Idx>(p.positions, t);
-    const int64_t ri = load_index<Idx>(p.request_indices, t);
-    uint32_t bad = 0;
-    const bool table_ok = pos >= 0 && pos < p.table_rows;
-    if (!table_ok) bad |= kStatusPosTable;
+  // Per-token metadata runs ahead of the data: the indices of token j+2 and the bounds, slot
+  // and table slice of token j+1 are fetched while token j is processed, so the dependent
+  // index -> table/slot loads never sit on a token's critical path.
+  struct Meta {
+    int64_t slot;
+    uint32_t bad;
+    bool table_ok, cache_ok;
+  };
+  auto fetch_index = [&](int64_t jj, int64_t& pos, int64_t& ri) {
+    const int64_t t = blockIdx.x + jj * gridDim.x;
+    pos = load_index<Idx>(p.positions, t);
+    ri = load_index<Idx>(p.request_indices, t);
+  };
+  auto resolve = [&](int64_t pos, int64_t ri, float* c, float* s) {
+    Meta m{0, 0u, false, false};
+    m.table_ok = pos >= 0 && pos < p.table_rows;
+    if (!m.table_ok) m.bad |= kStatusPosTable;
     const bool pos_ok = pos >= 0 && pos < p.S;
     const bool ri_ok = ri >= 0 && ri < p.B;
-    if (!pos_ok) bad |= kStatusPosCache;
-    if (!ri_ok) bad |= kStatusRequest;
-    bool cache_ok = pos_ok && ri_ok;
-    int64_t slot = 0;
+    if (!pos_ok) m.bad |= kStatusPosCache;
+    if (!ri_ok) m.bad |= kStatusRequest;
+    m.cache_ok = pos_ok && ri_ok;
     if constexpr (C == Cache::kStrided) {
-      slot = ri * p.c_bs + pos * p.c_ss;
-    } else if (cache_ok) {
+      m.slot = ri * p.c_bs + pos * p.c_ss;
+    } else if (m.cache_ok) {
       const int64_t blk_i = pos / p.block_size;
       const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
       if (blk < 0 || blk >= p.num_blocks) {
-        bad |= kStatusBlock;
-        cache_ok = false;
+        m.bad |= kStatusBlock;
+        m.cache_ok = false;
       }
-      slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
+      m.slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
     }
-    // Warm the address translation of this token's cache slots before the bulk stores.
-    if (cache_ok && tid == 0) {
-      prefetch_l2(p.k_dst + slot * ES);
-      prefetch_l2(p.v_dst + slot * ES);
+    // Warm the address translation of the token's cache slots before the bulk stores.
+    if (m.cache_ok && tid == 0) {
+      prefetch_l2(p.k_dst + m.slot * ES);
+      prefetch_l2(p.v_dst + m.slot * ES);
     }
-    float c[VEC], s[VEC];
-    if (lane_rotates && table_ok) {
+    if (lane_rotates && m.table_ok) {
       if (p.inreg_trig) {
         const float pf = static_cast<float>(pos);
 #pragma unroll
@@ -219,6 +223,32 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
         }
       }
     }
+    return m;
+  };
+
+  float c_cur[VEC], s_cur[VEC];
+  int64_t pos_next = 0, ri_next = 0;
+  Meta cur{0, 0u, false, false};
+  if (my_tokens > 0) {
+    int64_t pos0, ri0;
+    fetch_index(0, pos0, ri0);
+    if (my_tokens > 1) fetch_index(1, pos_next, ri_next);
+    cur = resolve(pos0, ri0, c_cur, s_cur);
+  }
+
+  int64_t j = 0;
+  for (; j < my_tokens; ++j) {
+    const int64_t t = blockIdx.x + j * gridDim.x;
+    const int st = static_cast<int>(j % sp.stages);
+    const uint32_t parity = static_cast<uint32_t>((j / sp.stages) & 1);
+    unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
+
+    // Metadata of the next tokens, in flight while this one is processed.
+    int64_t pos_after = 0, ri_after = 0;
+    if (j + 2 < my_tokens) fetch_index(j + 2, pos_after, ri_after);
+    float c_nxt[VEC], s_nxt[VEC];
+    Meta nxt{0, 0u, false, false};
+    if (j + 1 < my_tokens) nxt = resolve(pos_next, ri_next, c_nxt, s_nxt);
 
     if (!mbar_wait(&bars[st], parity)) {
       atomicOr(&s_abort, 1);
@@ -227,13 +257,13 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     if (s_abort) break;
 
     // Rotate the rotary dims of the Q and K rows in place.
-    if (lane_rotates && table_ok) {
+    if (lane_rotates && cur.table_ok) {
       for (int r = grp; r < rot_rows; r += blockDim.y) {
         unsigned char* row = stage + static_cast<size_t>(r) * row_bytes;
         Pack<E, VB> x1, x2;
         x1.bits = lds<VB>(row + off1);
         x2.bits = lds<VB>(row + off2);
-        rotate_pack<E, VB>(x1, x2, c, s);
+        rotate_pack<E, VB>(x1, x2, c_cur, s_cur);
         sts<VB>(row + off1, x1.bits);
         sts<VB>(row + off2, x2.bits);
       }
@@ -242,11 +272,12 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     __syncthreads();
 
     if (tid == 0) {
-      if (bad && p.status != nullptr) atomicOr(p.status, bad);
-      if (table_ok) bulk_store(p.q_out + t * static_cast<int64_t>(sp.q_bytes), stage, sp.q_bytes);
-      if (cache_ok) {
-        if (table_ok) bulk_store(p.k_dst + slot * ES, stage + sp.q_bytes, sp.kv_bytes);
-        bulk_store(p.v_dst + slot * ES, stage + sp.q_bytes + sp.kv_bytes, sp.kv_bytes);
+      if (cur.bad && p.status != nullptr) atomicOr(p.status, cur.bad);
+      if (cur.table_ok)
+        bulk_store(p.q_out + t * static_cast<int64_t>(sp.q_bytes), stage, sp.q_bytes);
+      if (cur.cache_ok) {
+        if (cur.table_ok) bulk_store(p.k_dst + cur.slot * ES, stage + sp.q_bytes, sp.kv_bytes);
+        bulk_store(p.v_dst + cur.slot * ES, stage + sp.q_bytes + sp.kv_bytes, sp.kv_bytes);
       }
       bulk_commit();
       // Refill the stage read by the previous token's stores once they have read it.
@@ -255,6 +286,15 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
         issue_load(j - 1 + sp.stages);
       }
     }
+
+    cur = nxt;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      c_cur[e] = c_nxt[e];
+      s_cur[e] = s_nxt[e];
+    }
+    pos_next = pos_after;
+    ri_next = ri_after;
   }
 
   if (tid == 0) {

@@ -6,7 +6,9 @@ programmatic dependent launch, so each kernel reads its positions and table rows
 previous layer's kernel drains (positions and tables are never written by these kernels).
 Optionally the step's host<->device traffic is captured in the same graph: q/k/v and
 positions are copied in from pinned host buffers and q_out is copied back, so one replay is one
-end-to-end decode step.
+end-to-end decode step. `capture_host_pipeline` captures several such steps in one graph with
+the copies on their own streams: step i+1's inputs cross PCIe while step i computes and step
+i-1's q_out crosses back, and the layers of successive steps stay in order on one stream.
 """
 from dataclasses import dataclass
 
@@ -82,6 +84,64 @@ class DecodeStep:
             if host is not None:
                 host_q_out.copy_(q_out, non_blocking=True)
         return CapturedStep(graph, q_out, inputs, host, host_q_out)
+
+    def capture_host_pipeline(self, device_sets, host_sets, warmup=1):
+        """Capture len(device_sets) end-to-end steps in one graph. Step i copies host_sets[i]
+        into device_sets[i] on a copy-in stream, runs every layer on the capturing stream after
+        its copy and after step i-1's layers, and copies its q_out back into a pinned buffer on a
+        copy-out stream. One replay is len(device_sets) decode steps."""
+        return _capture_pipeline(self, device_sets, host_sets, warmup)
+
+
+class CapturedPipeline:
+    """Several end-to-end decode steps in one graph (see DecodeStep.capture_host_pipeline)."""
+
+    def __init__(self, graph, q_outs, host_q_outs, steps):
+        self.graph = graph
+        self.q_outs = q_outs
+        self.host_q_outs = host_q_outs
+        self.steps = steps
+
+    def replay(self):
+        self.graph.replay()
+
+    def release(self):
+        self.graph = None
+
+
+def _capture_pipeline(step, device_sets, host_sets, warmup=1):
+    if len(device_sets) != len(host_sets) or not device_sets:
+        raise ValueError("one pinned host set per device set")
+    dev = device_sets[0].q.device
+    q_outs = [torch.empty(d.q.shape, dtype=d.q.dtype, device=dev) for d in device_sets]
+    host_q_outs = [torch.empty(d.q.shape, dtype=d.q.dtype, pin_memory=True) for d in device_sets]
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            for d, qo in zip(device_sets, q_outs):
+                step.run(d, qo)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    copy_in = torch.cuda.Stream(device=dev)
+    copy_out = torch.cuda.Stream(device=dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        compute = torch.cuda.current_stream(dev)
+        copy_in.wait_stream(compute)
+        copy_out.wait_stream(compute)
+        for d, h, qo, hqo in zip(device_sets, host_sets, q_outs, host_q_outs):
+            with torch.cuda.stream(copy_in):
+                for dst, src in ((d.q, h.q), (d.k, h.k), (d.v, h.v), (d.positions, h.positions),
+                                 (d.request_indices, h.request_indices)):
+                    dst.copy_(src, non_blocking=True)
+            compute.wait_stream(copy_in)
+            step.run(d, qo)
+            copy_out.wait_stream(compute)
+            with torch.cuda.stream(copy_out):
+                hqo.copy_(qo, non_blocking=True)
+        compute.wait_stream(copy_in)
+        compute.wait_stream(copy_out)
+    return CapturedPipeline(graph, q_outs, host_q_outs, len(device_sets))
 
 
 def pinned_like(inputs):

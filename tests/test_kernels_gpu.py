@@ -553,3 +553,42 @@ def test_staged_kernel_out_of_range_and_pdl():
     ref = _oracle_args(a2)
     q_ref = oracle.fused_rope_kv_append(*ref)
     assert bits_equal(q.cpu()[good], q_ref[good])
+
+
+def test_host_pipeline_runs_steps_in_order_with_copies_overlapped():
+    """capture_host_pipeline: several end-to-end steps in one graph; each step's q_out comes
+    back to its pinned buffer and the caches end as if the steps ran one after another."""
+    from decode_llm_kernel_b200.harness.decode_loop import DecodeStep, StepInputs, pinned_like
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    L, T, Hq, Hkv, D, S, depth = 4, 8, 32, 8, 128, 16, 3
+    kcs = [torch.zeros(T, S, Hkv, D, dtype=torch.bfloat16, device="cuda") for _ in range(L)]
+    vcs = [torch.zeros_like(kcs[0]) for _ in range(L)]
+    cos, sin = build_rope_tables(S, D, 500000.0, device="cuda")
+    g = torch.Generator().manual_seed(11)
+    hosts, devs = [], []
+    for _ in range(depth):
+        h = StepInputs(torch.randn(L, T, Hq, D, generator=g).to(torch.bfloat16),
+                       torch.randn(L, T, Hkv, D, generator=g).to(torch.bfloat16),
+                       torch.randn(L, T, Hkv, D, generator=g).to(torch.bfloat16),
+                       torch.randint(0, S, (T,), generator=g, dtype=torch.int64).to(torch.int32),
+                       torch.randperm(T, generator=g).to(torch.int32))
+        hp = pinned_like(h)
+        hosts.append(hp)
+        devs.append(StepInputs(*(torch.zeros_like(x, device="cuda") for x in
+                                 (h.q, h.k, h.v, h.positions, h.request_indices))))
+    pipe = DecodeStep(kcs, vcs, cos, sin).capture_host_pipeline(devs, hosts)
+    for c in kcs + vcs:
+        c.zero_()
+    pipe.replay()
+    torch.cuda.synchronize()
+    ref_k = [torch.zeros(T, S, Hkv, D, dtype=torch.bfloat16) for _ in range(L)]
+    ref_v = [torch.zeros(T, S, Hkv, D, dtype=torch.bfloat16) for _ in range(L)]
+    for i, h in enumerate(hosts):
+        for layer in range(L):
+            q_ref = oracle.fused_rope_kv_append(h.q[layer], h.k[layer], h.v[layer], h.positions,
+                                                cos.cpu(), sin.cpu(), ref_k[layer], ref_v[layer],
+                                                h.request_indices)
+            assert bits_equal(pipe.host_q_outs[i][layer].clone(), q_ref)
+    for layer in range(L):
+        assert bits_equal(kcs[layer].cpu(), ref_k[layer])
+        assert bits_equal(vcs[layer].cpu(), ref_v[layer])
