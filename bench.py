@@ -52,6 +52,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-bw-probe", action="store_true")
     p.add_argument("--no-floor", action="store_true", help="skip the empty-kernel launch floor")
+    p.add_argument("--no-ladder", action="store_true",
+                   help="skip the per-call operator ladder at batch 8")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--mode", choices=["full", "bw"], default="full",
@@ -384,6 +386,7 @@ def run_ours(args, world, rank, local):
         del hosts
 
     floor = None if args.no_floor else launch_floor(stream, w.layers)
+    ladder = None if (args.no_ladder or rank != 0) else operator_ladder(device, args.seed)
     del captured, sets, k_caches, v_caches, step
     torch.cuda.empty_cache()
     bw = None if args.no_bw_probe else bandwidth_probe(world, rank, device, args.seed, peak)
@@ -410,9 +413,42 @@ def run_ours(args, world, rank, local):
                 "pdl": not args.no_pdl}),
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": args.steps * w.layers, "launch_floor": floor,
+            "operator_ladder": ladder,
             "bandwidth_config": bw,
         }
         print(json.dumps(line), flush=True)
+
+
+def operator_ladder(device, seed):
+    """The reference's operator benchmark at its headline shape, on this build: Llama-3-8B
+    heads (32 Q / 8 KV, head_dim 128), batch 8, bf16, cache [8, 4096, 8, 128], eight rotating
+    device position sets, every rung through the drop-in ops and the reference's runners, with
+    the reference's three timers (benchmarks/benchmark_utils.py:80-126 of the reference). The
+    inputs are 200 KB, so like the reference's own rows these are launch-latency numbers."""
+    from decode_llm_kernel_b200.harness import impls, timing
+    from decode_llm_kernel_b200.harness import positions as pos
+    from decode_llm_kernel_b200.harness.workload import Config, build_op_args
+    cfg = Config("gqa", 32, 8, 128, 8, 4096, "bf16", pos.RAGGED, theta=500000.0,
+                 index_dtype="int32")
+    sets = pos.build_position_sets(8, 4096, pos.RAGGED, seed, 8, device, torch.int32)
+    args = build_op_args(cfg, device, seed, sets[0])
+    nbytes = timing.logical_bytes(args.q, args.k, args.v, args.cos, args.sin, args.k_cache,
+                                  args.v_cache)["total_bytes"]
+    rows = {}
+    for spec in impls.IMPL_SPECS:
+        runner = spec.build()
+        thunk = runner.make_thunk(args, sets)
+        amort = timing.time_amortized_call(thunk, 200, 3000)
+        events = timing.time_device_events(thunk, 50, 500)
+        synced = timing.time_synchronized_call(thunk, 50, 500)
+        med = sorted(events)[len(events) // 2]
+        rows[spec.label] = {"amortized_us": amort * 1e3, "event_median_us": med * 1e3,
+                            "synchronized_us": synced * 1e3,
+                            "logical_gbs_amortized": timing.logical_eff_gbps(nbytes, amort)}
+        if hasattr(runner, "release"):
+            runner.release()
+    return {"workload": "llama3_8b_b8 (batch 8, 32/8 heads, head_dim 128, bf16, theta 5e5)",
+            "logical_bytes_per_call": nbytes, "rungs": rows}
 
 
 def launch_floor(stream, layers):

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <string>
@@ -58,14 +59,19 @@ cudaStream_t stream_for(const at::Tensor& t) {
 }
 
 // One zero-initialised uint32 per device, allocated outside any stream capture's view (relaxed
-// capture mode) so the first call may happen while a graph is being captured.
+// capture mode) so the first call may happen while a graph is being captured. The fast path
+// is one atomic load; the mutex only guards the first allocation on a device.
+constexpr int kMaxStatusDevices = 64;
 std::mutex g_status_mutex;
-std::map<int, uint32_t*> g_status;
+std::atomic<uint32_t*> g_status[kMaxStatusDevices];
 
 uint32_t* status_word(int device) {
+  TORCH_CHECK(device >= 0 && device < kMaxStatusDevices, "device ordinal ", device,
+              " is beyond the ", kMaxStatusDevices, " devices this binding tracks");
+  uint32_t* fast = g_status[device].load(std::memory_order_acquire);
+  if (fast != nullptr) return fast;
   std::lock_guard<std::mutex> lock(g_status_mutex);
-  auto it = g_status.find(device);
-  if (it != g_status.end()) return it->second;
+  if (uint32_t* again = g_status[device].load(std::memory_order_acquire)) return again;
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
   cudaThreadExchangeStreamCaptureMode(&mode);
@@ -79,7 +85,7 @@ uint32_t* status_word(int device) {
   cudaThreadExchangeStreamCaptureMode(&mode);
   TORCH_CHECK(err == cudaSuccess, "could not allocate the status word: ",
               cudaGetErrorString(err));
-  g_status[device] = ptr;
+  g_status[device].store(ptr, std::memory_order_release);
   return ptr;
 }
 

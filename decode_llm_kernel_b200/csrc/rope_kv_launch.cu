@@ -17,6 +17,12 @@ namespace {
 
 template <typename E, typename Idx, int VB, Mode M, Cache C, int NR>
 cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStream_t stream) {
+  if (!shape.pdl) {
+    // The plain launch path: no attributes to process on the host.
+    rope_kv_kernel<E, Idx, VB, M, C, NR>
+        <<<dim3(shape.grid, 1, 1), dim3(shape.lanes, shape.groups, 1), 0, stream>>>(p);
+    return cudaGetLastError();
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(shape.grid, 1, 1);
   cfg.blockDim = dim3(shape.lanes, shape.groups, 1);

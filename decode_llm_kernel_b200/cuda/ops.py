@@ -45,7 +45,7 @@ def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, requ
     strided_cache  caches of any strides with a contiguous last dim, e.g. a head-major
                    [B, Hkv, S, D] cache passed as cache.transpose(1, 2);
     inv_freq       fp32 [rotary_dim/2] device tensor: cos/sin from sincosf in registers
-                   (within 1 ulp of the table path, not bit-exact);
+                   (not bit-exact: within the reference's tolerance, almost always 1 ulp);
     q_out          write into this contiguous [T, Hq, D] tensor instead of a fresh one;
     path           "auto" (default), "register" (the register kernel) or "staged" (the
                    bulk-copy kernel that stages tokens through shared memory; refused with a

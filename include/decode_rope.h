@@ -76,7 +76,9 @@ enum {
    * contiguous token-major, as the reference requires. */
   DRK_FLAG_STRIDED_CACHE = 1u << 1,
   /* Take cos/sin from sincosf of position * inv_freq in registers instead of the table
-   * (needs drk_options.inv_freq). Within 1 ulp of the table path, not bit-exact. */
+   * (needs drk_options.inv_freq). Not bit-exact: sincosf and the table's cos/sin differ by an
+   * fp32 ulp at times, which cancellation in x1*c - x2*s can magnify for near-zero outputs;
+   * results stay within the reference's tolerance (bf16 8e-3, fp16 1e-3). */
   DRK_FLAG_INREG_TRIG = 1u << 2,
   /* Kernel choice for the fused op. By default calls with many tokens whose Q/K/V row blocks
    * and cache slots are contiguous and 16-byte aligned use the bulk-copy (TMA) kernel that
