@@ -66,6 +66,23 @@ def parse_args():
 
 # ------------------------------------------------------------------------- distributed setup
 
+class stdout_to_stderr:
+    """Sends file descriptor 1 to stderr for a block, so library banners printed while the
+    process group starts never mix with the one JSON line this script prints."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self._saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self._saved, 1)
+        os.close(self._saved)
+        return False
+
+
 def init_dist(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -75,8 +92,10 @@ def init_dist(args):
         import torch.distributed as dist
         if args.impl == "ours":
             torch.cuda.set_device(local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", local))
+            with stdout_to_stderr():
+                dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                        device_id=torch.device("cuda", local))
+                dist.barrier()
     return world, rank, local
 
 

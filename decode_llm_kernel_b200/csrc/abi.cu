@@ -714,6 +714,26 @@ int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor
   });
 }
 
+int drk_advance_positions(const drk_tensor* positions, int64_t delta, uint32_t flags,
+                          drk_stream_t stream) {
+  return guarded([&] {
+    require(positions, "positions");
+    if (positions->device < 0)
+      invalid("positions must be a CUDA tensor, got ", device_name(positions->device));
+    if (positions->dtype != DRK_I32 && positions->dtype != DRK_I64)
+      invalid("positions must be int32 or int64, got ", dtype_name(positions->dtype));
+    if (positions->ndim != 1 || !is_contiguous(positions))
+      invalid("positions must be a contiguous [num_tokens] tensor");
+    const int64_t n = positions->sizes[0];
+    if (n == 0) return;
+    DeviceGuard guard(positions->device);
+    check_launch(drk::launch_advance_positions(positions->data,
+                                               positions->dtype == DRK_I32 ? 32 : 64, n, delta,
+                                               (flags & DRK_FLAG_PDL) != 0,
+                                               reinterpret_cast<cudaStream_t>(stream)));
+  });
+}
+
 int drk_smoke_fill(const drk_tensor* tensor, double value, drk_stream_t stream) {
   return guarded([&] {
     require(tensor, "tensor");

@@ -294,6 +294,11 @@ std::string status_string(int64_t status) {
   return drk_status_string(static_cast<uint32_t>(status));
 }
 
+void advance_positions(at::Tensor positions, int64_t delta, bool pdl) {
+  const drk_tensor d = describe(positions);
+  raise_on_error(drk_advance_positions(&d, delta, pdl ? DRK_FLAG_PDL : 0u, stream_for(positions)));
+}
+
 void launch_empty(int64_t count, bool pdl) {
   const int device = c10::cuda::current_device();
   raise_on_error(drk_launch_empty(static_cast<int>(count), pdl ? 1 : 0,
@@ -338,4 +343,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_address", &status_address, py::arg("device"));
   m.def("status_string", &status_string, py::arg("status"));
   m.def("launch_empty", &launch_empty, py::arg("count"), py::arg("pdl") = false);
+  m.def("advance_positions", &advance_positions, py::arg("positions"), py::arg("delta") = 1,
+        py::arg("pdl") = false, "positions += delta on the device (a decode loop's step).");
 }

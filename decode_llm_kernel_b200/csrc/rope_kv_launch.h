@@ -76,6 +76,10 @@ cudaError_t launch_rope_kv_staged(const KernelParams& p, const StagedParams& sp,
                                   int index_bits, int vb, int cache, const LaunchShape& shape,
                                   cudaStream_t stream);
 
+// positions.cu
+cudaError_t launch_advance_positions(void* data, int index_bits, int64_t n, int64_t delta,
+                                     bool pdl, cudaStream_t stream);
+
 // smoke.cu
 cudaError_t launch_smoke_fill(void* data, int elem_code, int64_t numel, double value,
                               cudaStream_t stream);

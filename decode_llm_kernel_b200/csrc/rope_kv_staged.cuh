@@ -20,7 +20,8 @@
 //      and the pass-through dims of partial rotary never pass through registers;
 //   5. a stage is refilled with the token kStages ahead once the bulk stores that read it
 //      have finished reading (cp.async.bulk.wait_group.read).
-// No multicast, no clusters: every copy is this CTA's own.
+// No thread-block clusters: every copy moves data between global memory and this CTA's own
+// shared memory.
 //
 // Waits. Each mbarrier wait is bounded (kWaitLimit polls). If a wait runs out -- a copy that
 // never lands, which no valid input produces -- the CTA sets DRK_STATUS_TIMEOUT in the status

@@ -75,5 +75,12 @@ def kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, *, pdl=
                            strided_cache)
 
 
-__all__ = ["fused_rope_kv_append", "fused_rope_kv_append_ex", "kv_append", "kv_append_ex",
+def advance_positions(positions, delta=1, *, pdl=False):
+    """positions += delta on the device, in place: the step of a captured decode loop, so the
+    graph replays without a host-side position copy. With pdl=True it may launch while the
+    previous kernel drains and still writes only after that kernel has finished."""
+    require().advance_positions(positions, delta, pdl)
+
+
+__all__ = ["advance_positions", "fused_rope_kv_append", "fused_rope_kv_append_ex", "kv_append", "kv_append_ex",
            "paged_rope_kv_append", "rope_forward", "rope_forward_ex", "separate_rope_kv_append"]

@@ -42,13 +42,16 @@ class CapturedStep:
 
 
 class DecodeStep:
-    def __init__(self, k_caches, v_caches, cos, sin, *, pdl=True):
+    def __init__(self, k_caches, v_caches, cos, sin, *, pdl=True, advance_positions=False):
+        """advance_positions: end each step with positions += 1 on the device, so a captured
+        step can be replayed step after step (each replay appends at the next position)."""
         if len(k_caches) != len(v_caches):
             raise ValueError("one K and one V cache per layer")
         self.k_caches = list(k_caches)
         self.v_caches = list(v_caches)
         self.cos, self.sin = cos, sin
         self.pdl = pdl
+        self.advance = advance_positions
         self.layers = len(self.k_caches)
 
     def run(self, inputs, q_out):
@@ -58,6 +61,8 @@ class DecodeStep:
                 inputs.q[layer], inputs.k[layer], inputs.v[layer], inputs.positions, self.cos,
                 self.sin, self.k_caches[layer], self.v_caches[layer], inputs.request_indices,
                 pdl=self.pdl and layer > 0, q_out=q_out[layer])
+        if self.advance:
+            ops.advance_positions(inputs.positions, 1, pdl=self.pdl)
 
     def capture(self, inputs, host=None, warmup=1):
         """Capture one step over device `inputs`. With `host` (pinned StepInputs), the graph
@@ -69,9 +74,12 @@ class DecodeStep:
             host_q_out = torch.empty((L, T, Hq, D), dtype=inputs.q.dtype, pin_memory=True)
         side = torch.cuda.Stream(device=inputs.q.device)
         side.wait_stream(torch.cuda.current_stream(inputs.q.device))
+        saved = inputs.positions.clone() if self.advance else None
         with torch.cuda.stream(side):
             for _ in range(warmup):
                 self.run(inputs, q_out)
+            if saved is not None:
+                inputs.positions.copy_(saved)   # warm-up steps must not move the loop
         torch.cuda.current_stream(inputs.q.device).wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):

@@ -190,6 +190,17 @@ DRK_API int drk_separate_rope_kv_append_noalloc(
     uint32_t* status, drk_stream_t stream);
 
 /*
+ * positions[t] += delta for every token: the device-side step of a decode loop, so a captured
+ * step ending with this call replays without a host-side position copy. No counterpart in the
+ * reference, whose graph runner copies new positions in before every replay
+ * (benchmarks/impls.py:144-150). positions is a contiguous int32 or int64 [T] device tensor.
+ * With DRK_FLAG_PDL in flags it launches as a programmatic dependent and still writes only after
+ * the preceding kernel has finished (every layer of the step has read the positions).
+ */
+DRK_API int drk_advance_positions(const drk_tensor* positions, int64_t delta, uint32_t flags,
+                                  drk_stream_t stream);
+
+/*
  * Fills a contiguous fp64/fp32/fp16/bf16 tensor with value (converted once on the host, so
  * fp64 keeps full precision). Replaces smoke_fill (csrc/smoke.cu:42-60, bound at
  * csrc/bindings.cpp:19-20).

@@ -614,3 +614,39 @@ def test_staged_kernel_in_register_trig_within_the_reference_tolerance():
     q = ops().fused_rope_kv_append_ex(*a, inv_freq=inv, path="staged").cpu()
     _assert_inreg_close(q, q_ref)
     assert bits_equal(a.v_cache.cpu(), ref[7])
+
+
+def test_decode_loop_advances_positions_on_the_device():
+    """A captured step ending with advance_positions replays three decode steps with no
+    host-side position copy: each replay appends at the next position."""
+    from decode_llm_kernel_b200.harness.decode_loop import DecodeStep, StepInputs
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    L, T, Hq, Hkv, D, S = 3, 8, 32, 8, 128, 32
+    kcs = [torch.zeros(T, S, Hkv, D, dtype=torch.bfloat16, device="cuda") for _ in range(L)]
+    vcs = [torch.zeros_like(kcs[0]) for _ in range(L)]
+    cos, sin = build_rope_tables(S, D, 500000.0, device="cuda")
+    g = torch.Generator().manual_seed(5)
+    start = torch.randint(0, S - 4, (T,), generator=g, dtype=torch.int64).to(torch.int32)
+    inp = StepInputs(torch.randn(L, T, Hq, D, generator=g).to(torch.bfloat16).cuda(),
+                     torch.randn(L, T, Hkv, D, generator=g).to(torch.bfloat16).cuda(),
+                     torch.randn(L, T, Hkv, D, generator=g).to(torch.bfloat16).cuda(),
+                     start.clone().cuda(), torch.arange(T, dtype=torch.int32).cuda())
+    step = DecodeStep(kcs, vcs, cos, sin, pdl=True, advance_positions=True)
+    cap = step.capture(inp)
+    for c in kcs + vcs:
+        c.zero_()
+    assert torch.equal(inp.positions.cpu(), start)      # warm-up did not move the loop
+    ref_k = [torch.zeros(T, S, Hkv, D, dtype=torch.bfloat16) for _ in range(L)]
+    ref_v = [torch.zeros(T, S, Hkv, D, dtype=torch.bfloat16) for _ in range(L)]
+    for s in range(3):
+        cap.replay()
+        torch.cuda.synchronize()
+        for layer in range(L):
+            q_ref = oracle.fused_rope_kv_append(
+                inp.q[layer].cpu(), inp.k[layer].cpu(), inp.v[layer].cpu(), start + s,
+                cos.cpu(), sin.cpu(), ref_k[layer], ref_v[layer], inp.request_indices.cpu())
+            assert bits_equal(cap.q_out[layer].cpu(), q_ref)
+    assert torch.equal(inp.positions.cpu(), start + 3)
+    for layer in range(L):
+        assert bits_equal(kcs[layer].cpu(), ref_k[layer])
+        assert bits_equal(vcs[layer].cpu(), ref_v[layer])
