@@ -249,13 +249,15 @@ def time_graph_steps(captured, steps, stream):
     return start.elapsed_time(end)
 
 
-def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
-    """The bandwidth-bound workload (mistral_b4096, sharded by batch): one fused launch per
-    call, input sets rotated so they exceed 3x L2, device time per launch from CUDA events.
-    cache_len > 0 shrinks the caches (same per-token work) for profiling runs."""
+def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters=400):
+    """One fused launch per call of a single-layer workload (sharded for this rank), input sets
+    rotated so they exceed 3x L2, launches replayed from a CUDA graph with programmatic
+    dependent launch between them (no launch writes another's positions, indices or tables),
+    device time per launch from CUDA events, max over ranks. cache_len > 0 shrinks the caches
+    (same per-token work) for profiling runs."""
     from dataclasses import replace
     from decode_llm_kernel_b200.cuda import ops
-    w = WORKLOADS["mistral_b4096"].shard_for(rank, world)
+    w = WORKLOADS[name].shard_for(rank, world)
     if cache_len:
         w = replace(w, cache_alloc_len=cache_len)
     g = torch.Generator(device=device).manual_seed(seed + 17)
@@ -277,13 +279,12 @@ def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
                      torch.arange(w.batch, device=device, dtype=idx),
                      torch.empty(w.batch, w.num_q_heads, w.head_dim, dtype=w.dtype,
                                  device=device)))
+    rot = w.rotary_dim if w.rotary_dim and w.rotary_dim != w.head_dim else 0
 
     def call(i):
         q, k, v, p, ri, qo = sets[i % nsets]
-        # Back-to-back launches never write each other's positions, indices or tables, so
-        # each may start its prologue while the previous one drains (programmatic dependent
-        # launch); the q/k/v reads still wait for the previous launch to finish.
-        ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo, pdl=True)
+        ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo, pdl=True,
+                                    rotary_dim=rot)
 
     # Launches are replayed from a CUDA graph so host call overhead cannot pace the GPU.
     for i in range(nsets):
@@ -312,15 +313,25 @@ def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
     per_launch_s = ms / 1e3 / iters
     del graph
     gbs_rank = w.bytes_per_call() / per_launch_s / 1e9
-    out = {"workload": "mistral_b4096", "batch_per_gpu": w.batch, "dtype": w.dtype_label,
-           "cache_alloc_len": w.cache_alloc_len, "launches": iters, "pdl": True,
-           "kernel": "drk::rope_kv_staged_kernel (TMA bulk copies, 3-stage mbarrier pipeline)",
+    staged = w.batch >= 512
+    out = {"workload": name, "shard": w.shard, "batch_per_gpu": w.batch,
+           "q_heads_per_gpu": w.num_q_heads, "kv_heads_per_gpu": w.num_kv_heads,
+           "head_dim": w.head_dim, "rotary_dim": w.rotary_dim or w.head_dim,
+           "dtype": w.dtype_label, "cache_alloc_len": w.cache_alloc_len, "launches": iters,
+           "pdl": True,
+           "kernel": ("drk::rope_kv_staged_kernel (TMA bulk copies, 3-stage mbarrier pipeline)"
+                      if staged else "drk::rope_kv_kernel (register kernel)"),
            "bytes_per_launch": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
            "achieved_gbs_per_gpu": gbs_rank, "frac_of_peak": gbs_rank / peak,
            "aggregate_gbs": gbs_rank * world, "input_sets": nsets}
     del kc, vc, sets
     torch.cuda.empty_cache()
     return out
+
+
+def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
+    """The bandwidth-bound workload (mistral_b4096, sharded by batch)."""
+    return single_layer_probe("mistral_b4096", world, rank, device, seed, peak, cache_len, iters)
 
 
 def run_ours(args, world, rank, local):
@@ -409,6 +420,11 @@ def run_ours(args, world, rank, local):
     del captured, sets, k_caches, v_caches, step
     torch.cuda.empty_cache()
     bw = None if args.no_bw_probe else bandwidth_probe(world, rank, device, args.seed, peak)
+    tp = None if args.no_bw_probe else single_layer_probe("llama3_70b_tp", world, rank, device,
+                                                          args.seed, peak)
+    partial = None
+    if not args.no_bw_probe and world == 1:
+        partial = single_layer_probe("phi2_partial", world, rank, device, args.seed, peak)
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -433,7 +449,7 @@ def run_ours(args, world, rank, local):
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": args.steps * w.layers, "launch_floor": floor,
             "operator_ladder": ladder,
-            "bandwidth_config": bw,
+            "bandwidth_config": bw, "tp_config": tp, "partial_rotary_config": partial,
         }
         print(json.dumps(line), flush=True)
 
