@@ -36,6 +36,9 @@ if ROOT not in sys.path:
 from decode_llm_kernel_b200.harness.configs import WORKLOADS, make_positions  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
+# ncu captures (profiles/): DRAM bytes read + written per launch
+DECODE32_NCU_DRAM_BYTES = 878848 + 0
+MISTRAL_NCU_DRAM_BYTES = 51522560 + 5620480
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "achieved HBM GB/s per decode step (algorithmic bytes / device time), with us/call"
 
@@ -324,6 +327,11 @@ def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters
            "bytes_per_launch": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
            "achieved_gbs_per_gpu": gbs_rank, "frac_of_peak": gbs_rank / peak,
            "aggregate_gbs": gbs_rank * world, "input_sets": nsets}
+    if name == "mistral_b4096" and world == 1:
+        out["traffic"] = MISTRAL_NCU_DRAM_BYTES
+        out["traffic_note"] = ("ncu, caches cut to 128 positions: reads 51.5 MB = the "
+                               "algorithmic reads; 5.6 MB of the 51.4 MB of writes reach DRAM "
+                               "within the launch, the rest drains from L2 afterwards")
     del kc, vc, sets
     torch.cuda.empty_cache()
     return out
@@ -375,9 +383,16 @@ def run_ours(args, world, rank, local):
     value = world * bytes_step / per_step_s / 1e9
     per_launch_s = per_step_s / w.layers
     achieved = w.bytes_per_call() / per_launch_s / 1e9
+    # DRAM traffic of one launch from an ncu capture of this kernel on the same workload with
+    # caches cut to 256 positions (per-launch traffic does not depend on the cache size: one
+    # slot per token); profiles/rope_kv_kernel_decode32_bf16.md
+    traffic = DECODE32_NCU_DRAM_BYTES if args.workload == "llama3_8b_decode32" else None
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
-                "kernel": "drk::rope_kv_kernel<BF16, int, 16, kFused, kStrided>",
+                "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per launch "
+                                "(878,848 + 0): the reads of q/k/v plus table and slot lines; "
+                                "the launch's 0.8 MB of writes stay in L2 until later",
+                "kernel": "drk::rope_kv_kernel<BF16, int, 16, kFused, kStrided, 1 row/thread>",
                 "per_launch_bytes": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
                 "note": "average launch = graph step time / layers, so it includes the gaps "
                         "between the chained launches"}

@@ -243,7 +243,8 @@ struct Aligner {
 struct Shape {
   int vb;
   int nslots, nrot, G, threads;
-  int rows;   // head rows per thread in flight
+  int rows;    // head rows per thread in flight
+  int splits;  // CTAs sharing one token's rows
 };
 
 // Small batches run one head row per thread (more threads per token, shorter per-thread
@@ -251,8 +252,9 @@ struct Shape {
 #ifndef DRK_SMALL_BATCH_TOKENS
 #define DRK_SMALL_BATCH_TOKENS 256
 #endif
+constexpr int kRowsPerSplitCta = 20;
 
-Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens) {
+Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens, int32_t splits_hint) {
   Shape s{};
   s.vb = al.pick();
   if (s.vb == 0) throw Unsupported("tensors are not aligned to their element size");
@@ -269,6 +271,20 @@ Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens) {
   // `rows` rows per thread; a block holds whole row groups.
   const int want_groups = std::max(1, (nrows + s.rows - 1) / s.rows);
   s.G = std::max(1, std::min(want_groups, max_threads / s.nslots));
+  // With one row per thread, a token's rows are shared by several CTAs of about
+  // kRowsPerSplitCta rows each: smaller CTAs spread over more SMs finish a small launch sooner
+  // (measured on B200: 70B-shaped 80-row tokens 4.56 -> 3.41 us at 256 tokens).
+  int splits = 1;
+  if (splits_hint > 0) {
+    splits = splits_hint;
+  } else if (s.rows == 1 && tokens > 0) {
+    splits = std::max(1, nrows / kRowsPerSplitCta);
+  }
+  const int groups_needed = (nrows + s.rows - 1) / s.rows;
+  splits = std::max(1, std::min(splits, groups_needed));
+  if (splits > 1)
+    s.G = std::max(1, std::min((groups_needed + splits - 1) / splits, max_threads / s.nslots));
+  s.splits = splits;
   s.threads = s.G * s.nslots;
   return s;
 }
@@ -520,7 +536,7 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
       p.G = pl.groups;
       p.nslots = pl.nrot;
       DeviceGuard guard(device);
-      const drk::LaunchShape shape{0, pl.nrot, pl.groups, pdl};
+      const drk::LaunchShape shape{0, 1, pl.nrot, pl.groups, pdl};
       check_launch(drk::launch_rope_kv_staged(p, pl.sp, elem_code(q->dtype), index_bits, pl.vb,
                                               paged ? drk::kCachePaged : drk::kCacheStrided,
                                               shape, reinterpret_cast<cudaStream_t>(stream)));
@@ -536,12 +552,12 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
   for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
   const int nrows = static_cast<int>(Hq + 2 * Hkv);
-  const Shape s = plan(al, nrows, true, T);
+  const Shape s = plan(al, nrows, true, T, o.row_splits);
   p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
   p.pdl = pdl ? 1 : 0;
 
   DeviceGuard guard(device);
-  const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, pdl};
+  const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, pdl};
   check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeFused,
                                    paged ? drk::kCachePaged : drk::kCacheStrided, shape,
                                    reinterpret_cast<cudaStream_t>(stream)));
@@ -637,11 +653,11 @@ int drk_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor*
     for (const drk_tensor* t : {q, k, q_out, k_out}) al.ptr(t->data);
     al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
     al.stride(T, k->strides[0]); al.stride(Hkv, k->strides[1]);
-    const Shape s = plan(al, static_cast<int>(Hq + Hkv), true, T);
+    const Shape s = plan(al, static_cast<int>(Hq + Hkv), true, T, o.row_splits);
     p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
     p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
     DeviceGuard guard(device);
-    const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
+    const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
     const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
     check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeRope,
                                      drk::kCacheStrided, shape,
@@ -702,11 +718,11 @@ int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor
     al.stride(T, k_rot->strides[0]); al.stride(Hkv, k_rot->strides[1]);
     al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
     for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
-    const Shape s = plan(al, static_cast<int>(2 * Hkv), false, T);
+    const Shape s = plan(al, static_cast<int>(2 * Hkv), false, T, o.row_splits);
     p.nslots = s.nslots; p.nrot = 0; p.G = s.G; p.rows_per_thread = s.rows;
     p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
     DeviceGuard guard(device);
-    const drk::LaunchShape shape{grid_for(T), s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
+    const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
     const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
     check_launch(drk::launch_rope_kv(p, elem_code(k_rot->dtype), index_bits, s.vb,
                                      drk::kModeAppend, drk::kCacheStrided, shape,

@@ -244,10 +244,12 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
   const int qk_off2 = lane_rotates ? (p.R >> 1) + lane * VEC : qk_off1 + ((p.D - qk_base) >> 1);
   const int v_off1 = lane * VEC;
   const int v_off2 = v_off1 + (p.D >> 1);
-  const bool lead = threadIdx.x == 0 && threadIdx.y == 0;
+  const bool lead = threadIdx.x == 0 && threadIdx.y == 0 && blockIdx.y == 0;
   bool waited = false;
 
-  for (int r0 = grp; r0 < nrows; r0 += p.G * NR) {
+  // gridDim.y CTAs share a token's rows: CTA y takes row groups y*G .. y*G + G-1.
+  const int groups_total = p.G * static_cast<int>(gridDim.y);
+  for (int r0 = static_cast<int>(blockIdx.y) * p.G + grp; r0 < nrows; r0 += groups_total * NR) {
     // Per-row constants of this batch of rows: which tensor, the byte offset of the lane's
     // first vector inside a token's source row and inside its destination row, the distance
     // to the second vector.
@@ -256,7 +258,7 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
     int gap[NR];
 #pragma unroll
     for (int i = 0; i < NR; ++i) {
-      const int r = r0 + i * p.G;
+      const int r = r0 + i * groups_total;
       int k = kRowV, head = 0;
       if (r < nrows) row_kind<M>(p, r, k, head);
       kind[i] = r < nrows ? k : -1;

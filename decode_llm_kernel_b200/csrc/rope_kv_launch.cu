@@ -20,11 +20,11 @@ cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStre
   if (!shape.pdl) {
     // The plain launch path: no attributes to process on the host.
     rope_kv_kernel<E, Idx, VB, M, C, NR>
-        <<<dim3(shape.grid, 1, 1), dim3(shape.lanes, shape.groups, 1), 0, stream>>>(p);
+        <<<dim3(shape.grid, shape.splits, 1), dim3(shape.lanes, shape.groups, 1), 0, stream>>>(p);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(shape.grid, 1, 1);
+  cfg.gridDim = dim3(shape.grid, shape.splits, 1);
   cfg.blockDim = dim3(shape.lanes, shape.groups, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;

@@ -53,7 +53,8 @@ enum { kModeFused = 0, kModeRope = 1, kModeAppend = 2 };
 enum { kCacheStrided = 0, kCachePaged = 1 };
 
 struct LaunchShape {
-  int grid;      // CTAs; each walks tokens blockIdx.x, blockIdx.x + grid, ...
+  int grid;      // CTAs along x; each walks tokens blockIdx.x, blockIdx.x + grid, ...
+  int splits;    // gridDim.y: CTAs sharing one token's head rows (register kernel)
   int lanes;     // blockDim.x: lanes per head row (nslots)
   int groups;    // blockDim.y: row groups (G)
   bool pdl;

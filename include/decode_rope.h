@@ -106,7 +106,10 @@ typedef struct drk_options {
   int32_t rotary_dim;     /* 0: the table width must equal head_dim (reference). Otherwise the
                              table width, even and <= head_dim; dims past it are copied raw. */
   const float* inv_freq;  /* [rotary_dim/2] fp32 device array, only for DRK_FLAG_INREG_TRIG */
-  int64_t reserved[4];
+  int32_t row_splits;     /* register kernel: CTAs sharing one token's head rows (0 = chosen
+                             by the library from the token count and the SM count) */
+  int32_t reserved0;
+  int64_t reserved[3];
 } drk_options;
 
 /*
