@@ -47,6 +47,10 @@ def _load():
         lib.orc_kv_append.restype = i32
         lib.orc_kv_append.argtypes = (
             [i32, vp, vp, i64, i32, i32] + [i64] * 4 + [vp, vp, vp, vp] + [i64] * 5)
+        lib.orc_decode_attention.restype = i32
+        lib.orc_decode_attention.argtypes = (
+            [i32, vp, i64, i32, i32, i32, vp, vp] + [i64] * 5
+            + [vp, vp, ctypes.c_double, vp, i32])
         lib.orc_max_threads.restype = i32
         lib.orc_f32_to_bf16.restype = ctypes.c_uint16
         lib.orc_f32_to_bf16.argtypes = [ctypes.c_float]
@@ -155,6 +159,33 @@ def kv_append(k_rot, v, positions, request_indices, k_cache, v_cache):
         ri.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
         k_cache.shape[1], k_cache.stride(0), k_cache.stride(1), k_cache.stride(2))
     _raise(rc)
+
+
+def decode_attention(q_rot, k_cache, v_cache, positions, request_indices, scale=None,
+                     nthreads=1):
+    """Grouped-query decode attention of each token's rotated query over its request's cache
+    positions [0, pos], evaluated in double and rounded once to the storage dtype. D <= 1024."""
+    _check_cpu(q_rot, k_cache, v_cache, positions, request_indices)
+    T, Hq, D = q_rot.shape
+    Hkv = k_cache.shape[2]
+    if scale is None:
+        scale = D ** -0.5
+    q_c = q_rot.contiguous()
+    out = torch.empty((T, Hq, D), dtype=q_rot.dtype)
+    if T == 0:
+        return out
+    if k_cache.stride(3) != 1 or v_cache.stride() != k_cache.stride() or D > 1024:
+        raise ValueError("caches need a contiguous last dim, identical strides, head_dim <= 1024")
+    pos, ri = _i64(positions), _i64(request_indices)
+    rc = _load().orc_decode_attention(
+        _DTYPE_CODES[q_rot.dtype], q_c.data_ptr(), T, Hq, Hkv, D, k_cache.data_ptr(),
+        v_cache.data_ptr(), k_cache.shape[0], k_cache.shape[1], k_cache.stride(0),
+        k_cache.stride(1), k_cache.stride(2), pos.data_ptr(), ri.data_ptr(), float(scale),
+        out.data_ptr(), int(nthreads))
+    if rc == -4:
+        raise ValueError("num_q_heads must be a multiple of num_kv_heads")
+    _raise(rc)
+    return out
 
 
 def f32_to_bf16_bits(x):

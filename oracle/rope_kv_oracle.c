@@ -255,6 +255,55 @@ int orc_kv_append(int dtype, const void* k_rot, const void* v, int64_t T, int Hk
   return 0;
 }
 
+/*
+ * Decode attention over the cache after the append (the consumer of this path's writes; the
+ * reference prices it with torch SDPA, benchmarks/probe_cache_read.py:26-172):
+ *   out[t, h] = sum_p softmax_p(scale * q[t, h] . K[ri, p, g]) V[ri, p, g],  p in [0, pos[t]]
+ * with g = h / (Hq / Hkv) (grouped-query attention). q is the rotated query in the storage
+ * dtype (what the fused op returns); the dot products, the softmax and the weighted sum are
+ * evaluated in double from the stored values, then rounded once to the storage dtype.
+ * Returns 0, or -1 / -2 for an out-of-range position / request index.
+ */
+int orc_decode_attention(int dtype, const void* q, int64_t T, int Hq, int Hkv, int D,
+                         const void* k_cache, const void* v_cache, int64_t B, int64_t S,
+                         int64_t c_sb, int64_t c_ss, int64_t c_sh, const int64_t* positions,
+                         const int64_t* request_indices, double scale, void* out,
+                         int nthreads) {
+  int rc = check_indices(T, positions, request_indices, B, S, S);
+  if (rc) return rc;
+  if (Hq % Hkv) return -4;
+  set_threads(nthreads);
+  const int group = Hq / Hkv;
+#pragma omp parallel for schedule(dynamic)
+  for (int64_t th = 0; th < T * Hq; ++th) {
+    const int64_t t = th / Hq;
+    const int h = (int)(th % Hq);
+    const int g = h / group;
+    const int64_t npos = positions[t] + 1;
+    const int64_t base = request_indices[t] * c_sb + (int64_t)g * c_sh;
+    double m = -1e300, l = 0.0;
+    double acc[1024];
+    for (int d = 0; d < D; ++d) acc[d] = 0.0;
+    for (int64_t p = 0; p < npos; ++p) {
+      double dot = 0.0;
+      for (int d = 0; d < D; ++d)
+        dot += (double)load_f32(q, dtype, (t * Hq + h) * (int64_t)D + d) *
+               (double)load_f32(k_cache, dtype, base + p * c_ss + d);
+      const double sc = dot * scale;
+      const double m_new = sc > m ? sc : m;
+      const double corr = exp(m - m_new);
+      const double w = exp(sc - m_new);
+      l = l * corr + w;
+      for (int d = 0; d < D; ++d)
+        acc[d] = acc[d] * corr + w * (double)load_f32(v_cache, dtype, base + p * c_ss + d);
+      m = m_new;
+    }
+    for (int d = 0; d < D; ++d)
+      store_f32(out, dtype, (t * Hq + h) * (int64_t)D + d, (float)(acc[d] / l));
+  }
+  return 0;
+}
+
 /* Exposed for the conversion tests. */
 uint16_t orc_f32_to_bf16(float f) { return f32_to_bf16(f); }
 uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
