@@ -29,7 +29,8 @@ GENCODE = "-gencode=arch=compute_100a,code=sm_100a"
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", GENCODE, "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]
 EXTRA_NVCC_FLAGS = os.environ.get("DECODE_NVCC_EXTRA_FLAGS", "").split()
-LIB_SOURCES = ["abi.cu", "rope_kv_launch.cu", "smoke.cu", "noalloc.cu", "positions.cu"]
+LIB_SOURCES = ["abi.cu", "rope_kv_launch.cu", "rope_kv_attention.cu", "rope_kv_attention_tc.cu",
+               "smoke.cu", "noalloc.cu", "positions.cu"]
 BINDING_SOURCE = "bindings.cpp"
 EXT_NAME = "_ext"
 

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -563,6 +564,210 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
                                    reinterpret_cast<cudaStream_t>(stream)));
 }
 
+// ---- fused append + decode attention: the plan both the workspace query and the launch use ----
+
+struct AttentionPlan {
+  bool tc = false;              // the tensor-core kernel (16 heads per unit)
+  int64_t chunk = 0, max_chunks = 0;
+  int hpb = 0, nhb = 0, lpr = 0;
+  int64_t counter_bytes = 0;    // arrival counters, rounded up to 256 bytes
+  int64_t partial_bytes = 0;    // fp32 [T, Hq, max_chunks, D + 2]
+};
+
+// CTAs of one attention instantiation resident per SM, from its register use (128 threads).
+int attention_ctas_per_sm(int hpb, int64_t es) {
+  if (es == 4) return hpb >= 8 ? 4 : 8;
+  return hpb >= 8 ? 2 : (hpb == 4 ? 4 : 8);
+}
+
+AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t S,
+                             int32_t dtype, const drk_attention_options& ao, int device) {
+  if (dtype != DRK_F32 && dtype != DRK_F16 && dtype != DRK_BF16)
+    throw Unsupported(cat("fused attention supports fp32, fp16 and bf16, got ", dtype_name(dtype)));
+  if (T < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || S < 0)
+    invalid("fused attention: sizes must be positive");
+  if (Hq % Hkv) invalid("num_q_heads (", Hq, ") must be a multiple of num_kv_heads (", Hkv, ")");
+  const int64_t es = elem_size(dtype);
+  const int64_t vl = 16 / es;
+  if (D % vl) throw Unsupported(cat("fused attention needs head_dim * element size to be a ",
+                                    "multiple of 16 bytes, got head_dim ", D));
+  if (D > 32 * vl)
+    throw Unsupported(cat("fused attention supports head_dim <= ", 32 * vl, " for ",
+                          dtype_name(dtype), ", got ", D));
+  if (T > 65535 || Hkv > 65535) throw Unsupported("fused attention: at most 65535 tokens and kv heads");
+  AttentionPlan pl;
+  if (ao.path < DRK_ATTN_PATH_AUTO || ao.path > DRK_ATTN_PATH_TENSOR_CORES)
+    invalid("path must be DRK_ATTN_PATH_AUTO, _CUDA_CORES or _TENSOR_CORES, got ", ao.path);
+  const bool tc_shape = es == 2 && D == 128;
+  if (ao.path == DRK_ATTN_PATH_TENSOR_CORES && !tc_shape)
+    throw Unsupported("the tensor-core attention kernel takes fp16/bf16 with head_dim 128");
+  if (tc_shape && ao.path != DRK_ATTN_PATH_CUDA_CORES) {
+    pl.tc = true;
+    pl.hpb = 16;
+    pl.nhb = static_cast<int>((Hq / Hkv + 15) / 16);
+    int64_t chunk = ao.chunk;
+    if (chunk < 0) invalid("chunk must be >= 0, got ", chunk);
+    if (chunk == 0) {
+      // Enough units for about four per SM, so the static walk balances; at most 4096.
+      const int64_t heads = std::max<int64_t>(1, T * Hkv * pl.nhb);
+      const int64_t target = 4LL * drk::device_sm_count(device);
+      chunk = 128;
+      while (chunk < 4096 && heads * ((S + 2 * chunk - 1) / (2 * chunk)) >= target) chunk <<= 1;
+    }
+    pl.chunk = (chunk + 127) / 128 * 128;
+    pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);
+    pl.counter_bytes = (T * Hkv * pl.nhb * 4 + 255) / 256 * 256;
+    pl.partial_bytes = T * Hq * pl.max_chunks * (D + 2) * 4;
+    return pl;
+  }
+  int lanes = 8;
+  while (lanes * vl < D) lanes <<= 1;
+  pl.lpr = lanes;
+  const int64_t group = Hq / Hkv;
+  int hpb = ao.heads_per_cta;
+  if (hpb == 0) {
+    hpb = 1;
+    while (hpb < group && hpb < 8) hpb <<= 1;
+    // Eight 16-bit heads per CTA need ~250 registers a thread; two blocks of four re-read each
+    // chunk (from L2) but keep twice the CTAs resident.
+    if (hpb == 8 && es == 2) hpb = 4;
+  }
+  if (hpb != 1 && hpb != 2 && hpb != 4 && hpb != 8)
+    invalid("heads_per_cta must be 0, 1, 2, 4 or 8, got ", hpb);
+  pl.hpb = hpb;
+  pl.nhb = static_cast<int>((group + hpb - 1) / hpb);
+  int64_t chunk = ao.chunk;
+  if (chunk < 0) invalid("chunk must be >= 0, got ", chunk);
+  if (chunk == 0) {
+    const int64_t units = std::max<int64_t>(1, T * Hkv * pl.nhb);
+    const int64_t slots =
+        2LL * drk::device_sm_count(device) * attention_ctas_per_sm(hpb, es);
+    const int64_t want = std::max<int64_t>(1, units * std::max<int64_t>(S, 1) / slots);
+    chunk = 64;
+    while (chunk * 2 <= want && chunk < 1024) chunk <<= 1;
+  }
+  pl.chunk = chunk;
+  pl.max_chunks = std::max<int64_t>(1, (S + chunk - 1) / chunk);
+  if (pl.max_chunks * pl.nhb > 0x7fffffffLL) throw Unsupported("fused attention: grid too large");
+  pl.counter_bytes = (T * Hkv * pl.nhb * 4 + 255) / 256 * 256;
+  pl.partial_bytes = T * Hq * pl.max_chunks * (D + 2) * 4;
+  return pl;
+}
+
+drk_attention_options attention_or_default(const drk_attention_options* a) {
+  drk_attention_options o{};
+  if (a) o = *a;
+  return o;
+}
+
+void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
+                    const drk_tensor* positions, const drk_tensor* cos, const drk_tensor* sin,
+                    const drk_tensor* k_cache, const drk_tensor* v_cache,
+                    const drk_tensor* request_indices, const drk_tensor* q_out,
+                    const drk_tensor* attn_out, const drk_attention_options* attn,
+                    void* workspace, size_t workspace_bytes, const drk_options* opts,
+                    uint32_t* status, drk_stream_t stream) {
+  const drk_options o = options_or_default(opts);
+  const drk_attention_options ao = attention_or_default(attn);
+  if (o.flags & ~static_cast<uint32_t>(DRK_FLAG_PDL | DRK_FLAG_STRIDED_CACHE))
+    throw Unsupported("fused attention accepts only DRK_FLAG_PDL and DRK_FLAG_STRIDED_CACHE");
+  require(q, "q");
+  if (q->ndim != 3) invalid("q must be [num_tokens, num_q_heads, head_dim]");
+  const int64_t T = q->sizes[0], Hq = q->sizes[1], D = q->sizes[2];
+  if (D % 2) invalid("head_dim must be even for split-half RoPE, got ", D);
+  const int32_t device = q->device;
+  check_qkv(q, "q", T, D, device);
+  check_qkv(k, "k", T, D, device);
+  check_qkv(v, "v", T, D, device);
+  const int64_t Hkv = k->sizes[1];
+  if (v->sizes[1] != Hkv) invalid("v has ", v->sizes[1], " kv heads, expected ", Hkv);
+  if (q->dtype != k->dtype || q->dtype != v->dtype) invalid("q, k and v must share a dtype");
+  check_index_tensor(positions, "positions", T, device);
+  check_index_tensor(request_indices, "request_indices", T, device);
+  if (positions->dtype != request_indices->dtype)
+    invalid("positions and request_indices must share a dtype, got ",
+            dtype_name(positions->dtype), "/", dtype_name(request_indices->dtype));
+  const int32_t rot = resolve_rotary(o, D);
+  check_rope_tables(cos, sin, D, rot, device);
+  const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0;
+  check_cache(k_cache, "k_cache", k->dtype, Hkv, D, device, strided_ok);
+  check_cache(v_cache, "v_cache", v->dtype, Hkv, D, device, strided_ok);
+  check_caches_are_distinct(k_cache, v_cache);
+  if (q_out != nullptr) check_output(q_out, "q_out", q->dtype, T, Hq, D, device);
+  check_output(attn_out, "attn_out", q->dtype, T, Hq, D, device);
+  check_float_dtype(q->dtype, "fused_rope_kv_append_attention");
+  const int64_t S = k_cache->sizes[1];
+  const AttentionPlan pl = plan_attention(T, Hq, Hkv, D, S, q->dtype, ao, device);
+  if (T == 0) return;
+  const int64_t es = elem_size(q->dtype);
+  uintptr_t addr = reinterpret_cast<uintptr_t>(k_cache->data) |
+                   reinterpret_cast<uintptr_t>(v_cache->data);
+  int64_t strides = 0;
+  for (int i = 0; i < 3; ++i)
+    if (k_cache->sizes[i] > 1) strides |= k_cache->strides[i];
+  if (addr % 16 || (strides * es) % 16)
+    throw Unsupported("fused attention needs 16-byte aligned cache rows (base and strides)");
+  if (workspace == nullptr ||
+      workspace_bytes < static_cast<size_t>(pl.counter_bytes + pl.partial_bytes))
+    invalid("workspace needs ", pl.counter_bytes + pl.partial_bytes, " bytes, got ",
+            workspace == nullptr ? 0 : workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 16) invalid("workspace must be 16-byte aligned");
+  if (ao.scale < 0) invalid("scale must be >= 0 (0 = 1/sqrt(head_dim))");
+
+  const int64_t R = rot ? rot : D;
+  drk::KernelParams p{};
+  p.q = static_cast<const char*>(q->data);
+  p.k = static_cast<const char*>(k->data);
+  p.v = static_cast<const char*>(v->data);
+  p.k_dst = static_cast<char*>(k_cache->data);
+  p.v_dst = static_cast<char*>(v_cache->data);
+  p.positions = positions->data;
+  p.request_indices = request_indices->data;
+  p.status = status;
+  p.T = T;
+  p.q_ts = q->strides[0]; p.q_hs = q->strides[1];
+  p.k_ts = k->strides[0]; p.k_hs = k->strides[1];
+  p.v_ts = v->strides[0]; p.v_hs = v->strides[1];
+  p.c_bs = k_cache->strides[0]; p.c_ss = k_cache->strides[1]; p.c_hs = k_cache->strides[2];
+  p.B = k_cache->sizes[0];
+  p.S = S;
+  p.Hq = static_cast<int32_t>(Hq);
+  p.Hkv = static_cast<int32_t>(Hkv);
+  p.D = static_cast<int32_t>(D);
+  p.R = static_cast<int32_t>(R);
+  fill_table(p, cos, sin, o, R);
+
+  drk::AttentionParams a{};
+  char* ws = static_cast<char*>(workspace);
+  a.counters = reinterpret_cast<int*>(ws);
+  a.workspace = reinterpret_cast<float*>(ws + pl.counter_bytes);
+  a.attn_out = attn_out->data;
+  a.q_out = q_out ? static_cast<char*>(q_out->data) : nullptr;
+  const double scale = ao.scale > 0 ? ao.scale : 1.0 / std::sqrt(static_cast<double>(D));
+  a.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  a.chunk = static_cast<int32_t>(pl.chunk);
+  a.max_chunks = static_cast<int32_t>(pl.max_chunks);
+  a.group = static_cast<int32_t>(Hq / Hkv);
+  a.nhb = pl.nhb;
+
+  DeviceGuard guard(device);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(workspace, 0, static_cast<size_t>(pl.counter_bytes), s) != cudaSuccess)
+    throw CudaFailure("cudaMemsetAsync of the attention counters failed");
+  const int index_bits_tc = positions->dtype == DRK_I32 ? 32 : 64;
+  if (pl.tc) {
+    const int64_t units = T * Hkv * pl.nhb * pl.max_chunks;
+    check_launch(drk::launch_rope_kv_attention_tc(p, a, elem_code(q->dtype), index_bits_tc, units,
+                                                  (o.flags & DRK_FLAG_PDL) != 0, s));
+    return;
+  }
+  const drk::AttentionShape shape{static_cast<int>(pl.max_chunks * pl.nhb),
+                                  static_cast<int>(Hkv), static_cast<int>(T), pl.lpr, pl.hpb,
+                                  (o.flags & DRK_FLAG_PDL) != 0};
+  const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+  check_launch(drk::launch_rope_kv_attention(p, a, elem_code(q->dtype), index_bits, shape, s));
+}
+
 }  // namespace
 
 namespace drk {
@@ -788,6 +993,32 @@ int drk_build_info(char* buf, size_t len, drk_stream_t stream) {
             __CUDACC_VER_BUILD__, "\nfast_math=", fast_math, "\n");
     if (text.size() + 1 > len) invalid("buf too small: need ", text.size() + 1, " bytes");
     std::memcpy(buf, text.c_str(), text.size() + 1);
+  });
+}
+
+int64_t drk_attention_workspace_bytes(int64_t num_tokens, int32_t num_q_heads,
+                                      int32_t num_kv_heads, int32_t head_dim,
+                                      int64_t cache_alloc_len, int32_t dtype,
+                                      const drk_attention_options* attn, int32_t device) {
+  int64_t bytes = 0;
+  const int rc = guarded([&] {
+    const AttentionPlan pl = plan_attention(num_tokens, num_q_heads, num_kv_heads, head_dim,
+                                            cache_alloc_len, dtype, attention_or_default(attn),
+                                            device);
+    bytes = pl.counter_bytes + pl.partial_bytes;
+  });
+  return rc == DRK_OK ? bytes : rc;
+}
+
+int drk_fused_rope_kv_append_attention(
+    const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,
+    const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* k_cache,
+    const drk_tensor* v_cache, const drk_tensor* request_indices, const drk_tensor* q_out,
+    const drk_tensor* attn_out, const drk_attention_options* attn, void* workspace,
+    size_t workspace_bytes, const drk_options* opts, uint32_t* status, drk_stream_t stream) {
+  return guarded([&] {
+    attention_impl(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices, q_out,
+                   attn_out, attn, workspace, workspace_bytes, opts, status, stream);
   });
 }
 

@@ -118,6 +118,13 @@ uint32_t path_flags(const std::string& path) {
   TORCH_CHECK(false, "path must be 'auto', 'register' or 'staged', got '", path, "'");
 }
 
+int32_t attention_path(const std::string& path) {
+  if (path == "auto") return DRK_ATTN_PATH_AUTO;
+  if (path == "cuda_cores") return DRK_ATTN_PATH_CUDA_CORES;
+  if (path == "tensor_cores") return DRK_ATTN_PATH_TENSOR_CORES;
+  TORCH_CHECK(false, "path must be 'auto', 'cuda_cores' or 'tensor_cores', got '", path, "'");
+}
+
 at::Tensor empty_like_rows(const at::Tensor& src, int64_t heads) {
   return at::empty({src.size(0), heads, src.size(2)}, src.options());
 }
@@ -269,6 +276,68 @@ void kv_append_ex(at::Tensor k_rot, at::Tensor v, at::Tensor positions,
                                stream_for(k_rot)));
 }
 
+// Fused append + decode attention. attn_out (and the workspace) come from the caching
+// allocator unless given; q_out is written only when given.
+at::Tensor fused_rope_kv_append_attention(
+    at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor positions, at::Tensor cos,
+    at::Tensor sin, at::Tensor k_cache, at::Tensor v_cache, at::Tensor request_indices,
+    double scale, c10::optional<at::Tensor> q_out_opt, c10::optional<at::Tensor> attn_out_opt,
+    int64_t chunk, int64_t heads_per_cta, int64_t rotary_dim, bool pdl, bool strided_cache,
+    c10::optional<at::Tensor> workspace_opt, const std::string& path) {
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && k_cache.dim() == 4,
+              "q must be [num_tokens, num_q_heads, head_dim], k [num_tokens, num_kv_heads, "
+              "head_dim] and k_cache [batch, cache_alloc_len, num_kv_heads, head_dim]");
+  at::Tensor attn_out;
+  if (attn_out_opt.has_value() && attn_out_opt->defined()) attn_out = *attn_out_opt;
+  else attn_out = empty_like_rows(q, q.size(1));
+  drk_attention_options ao{};
+  ao.scale = scale;
+  ao.chunk = static_cast<int32_t>(chunk);
+  ao.heads_per_cta = static_cast<int32_t>(heads_per_cta);
+  ao.path = attention_path(path);
+  const int32_t device = q.is_cuda() ? q.get_device() : -1;
+  const int64_t need = drk_attention_workspace_bytes(
+      q.size(0), static_cast<int32_t>(q.size(1)), static_cast<int32_t>(k.size(1)),
+      static_cast<int32_t>(q.size(2)), k_cache.size(1), dtype_code(q.scalar_type()), &ao,
+      device < 0 ? 0 : device);
+  if (need < 0) raise_on_error(static_cast<int>(need));
+  at::Tensor workspace;
+  if (workspace_opt.has_value() && workspace_opt->defined()) workspace = *workspace_opt;
+  else workspace = at::empty({std::max<int64_t>(need, 16)}, q.options().dtype(at::kByte));
+  TORCH_CHECK(workspace.is_contiguous(), "workspace must be contiguous");
+  const drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
+                                         (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
+                                     rotary_dim, c10::nullopt);
+  const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
+                   dp = describe(positions), dc = describe(cos), ds = describe(sin),
+                   dkc = describe(k_cache), dvc = describe(v_cache),
+                   dri = describe(request_indices), dao = describe(attn_out);
+  drk_tensor dqo{};
+  const bool has_q_out = q_out_opt.has_value() && q_out_opt->defined();
+  if (has_q_out) dqo = describe(*q_out_opt);
+  raise_on_error(drk_fused_rope_kv_append_attention(
+      &dq, &dk, &dv, &dp, &dc, &ds, &dkc, &dvc, &dri, has_q_out ? &dqo : nullptr, &dao, &ao,
+      workspace.data_ptr(), static_cast<size_t>(workspace.numel() * workspace.element_size()),
+      &o, status_for(q), stream_for(q)));
+  return attn_out;
+}
+
+int64_t attention_workspace_bytes(int64_t num_tokens, int64_t num_q_heads, int64_t num_kv_heads,
+                                  int64_t head_dim, int64_t cache_alloc_len,
+                                  at::ScalarType dtype, int64_t chunk, int64_t heads_per_cta,
+                                  int64_t device, const std::string& path) {
+  drk_attention_options ao{};
+  ao.chunk = static_cast<int32_t>(chunk);
+  ao.heads_per_cta = static_cast<int32_t>(heads_per_cta);
+  ao.path = attention_path(path);
+  const int64_t need = drk_attention_workspace_bytes(
+      num_tokens, static_cast<int32_t>(num_q_heads), static_cast<int32_t>(num_kv_heads),
+      static_cast<int32_t>(head_dim), cache_alloc_len, dtype_code(dtype), &ao,
+      static_cast<int32_t>(device));
+  if (need < 0) raise_on_error(static_cast<int>(need));
+  return need;
+}
+
 // Reads (and by default clears) the device's status word. Synchronises the current stream:
 // call it outside timed regions.
 int64_t read_status(int64_t device, bool clear) {
@@ -339,6 +408,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_append_ex", &kv_append_ex, py::arg("k_rot"), py::arg("v"), py::arg("positions"),
         py::arg("request_indices"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("pdl") = false, py::arg("strided_cache") = false);
+  m.def("fused_rope_kv_append_attention", &fused_rope_kv_append_attention, py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("request_indices"),
+        py::arg("scale") = 0.0, py::arg("q_out") = py::none(), py::arg("attn_out") = py::none(),
+        py::arg("chunk") = 0, py::arg("heads_per_cta") = 0, py::arg("rotary_dim") = 0,
+        py::arg("pdl") = false, py::arg("strided_cache") = false,
+        py::arg("workspace") = py::none(), py::arg("path") = "auto",
+        "Fused RoPE + KV append + decode attention over positions [0, pos]; returns attn_out.");
+  m.def("attention_workspace_bytes", &attention_workspace_bytes, py::arg("num_tokens"),
+        py::arg("num_q_heads"), py::arg("num_kv_heads"), py::arg("head_dim"),
+        py::arg("cache_alloc_len"), py::arg("dtype"), py::arg("chunk") = 0,
+        py::arg("heads_per_cta") = 0, py::arg("device") = 0, py::arg("path") = "auto");
   m.def("read_status", &read_status, py::arg("device"), py::arg("clear") = true);
   m.def("status_address", &status_address, py::arg("device"));
   m.def("status_string", &status_string, py::arg("status"));

@@ -1,0 +1,111 @@
+// Host side of the tensor-core attention kernel (rope_kv_attention_tc.cuh): the TMA tensor
+// maps of the two caches and the persistent launch.
+//
+// The caches are described to TMA as 4-D tensors (dims, kv heads, positions, batch rows) with
+// their own element strides, so token-major and head-major caches take the same kernel; a box
+// is [1 row][128 positions][1 head][64 dims] with the 128-byte swizzle the tcgen05 shared-memory
+// descriptors expect. cuTensorMapEncodeTiled is reached through the runtime's driver entry
+// point, so the library does not link the driver API.
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+
+#include "rope_kv_attention_tc.cuh"
+#include "rope_kv_launch.h"
+
+namespace drk {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+cudaError_t encode_cache_map(CUtensorMap* map, const void* base, bool bf16,
+                             const KernelParams& p) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.D), static_cast<cuuint64_t>(p.Hkv),
+                              static_cast<cuuint64_t>(p.S), static_cast<cuuint64_t>(p.B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.c_hs) * 2,
+                                 static_cast<cuuint64_t>(p.c_ss) * 2,
+                                 static_cast<cuuint64_t>(p.c_bs) * 2};
+  const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kTcTile), 1};
+  const cuuint32_t estride[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        4, const_cast<void*>(base), dims, strides, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <typename E, typename Idx>
+cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t units, bool pdl,
+                      cudaStream_t stream) {
+  auto kernel = rope_kv_attention_tc_kernel<E, Idx>;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  {
+    static std::mutex mu;
+    static std::map<int, bool> opted_in;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!opted_in[device]) {
+      err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kTcSmemBytes));
+      if (err != cudaSuccess) return err;
+      opted_in[device] = true;
+    }
+  }
+  CUtensorMap kmap, vmap;
+  constexpr bool bf16 = std::is_same<E, BF16>::value;
+  err = encode_cache_map(&kmap, p.k_dst, bf16, p);
+  if (err != cudaSuccess) return err;
+  err = encode_cache_map(&vmap, p.v_dst, bf16, p);
+  if (err != cudaSuccess) return err;
+  const int64_t sms = device_sm_count(device);
+  const int grid = static_cast<int>(units < sms ? units : sms);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = kTcSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, p, a, kmap, vmap, units);
+}
+
+}  // namespace
+
+cudaError_t launch_rope_kv_attention_tc(const KernelParams& p, const AttentionParams& a,
+                                        int elem_code, int index_bits, int64_t units, bool pdl,
+                                        cudaStream_t stream) {
+  if (units <= 0) return cudaSuccess;
+  switch (elem_code) {
+    case kElemF16:
+      return index_bits == 32 ? launch_tc<F16, int>(p, a, units, pdl, stream)
+                              : launch_tc<F16, long long>(p, a, units, pdl, stream);
+    case kElemBF16:
+      return index_bits == 32 ? launch_tc<BF16, int>(p, a, units, pdl, stream)
+                              : launch_tc<BF16, long long>(p, a, units, pdl, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace drk

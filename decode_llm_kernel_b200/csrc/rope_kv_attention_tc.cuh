@@ -1,0 +1,528 @@
+// Fused RoPE + KV append + decode attention on the 5th-generation tensor cores (tcgen05), for
+// 16-bit caches with head_dim 128: the bandwidth form of rope_kv_attention.cuh.
+//
+// Work unit: (token t, KV head g, head block hb of up to 16 query heads, chunk of positions).
+// A persistent grid (one CTA per SM, 128 threads) walks units u = blockIdx.x, +gridDim.x, ...
+// and streams each unit's positions in tiles of 128 through a kTcStages-deep ring of shared
+// memory stages. Per tile:
+//   1. TMA (cp.async.bulk.tensor, 128-byte swizzle) brings K[128 positions][128 dims] and V of
+//      the same rows, as two 64-dim boxes each (64 KB), completing on the stage's mbarrier;
+//   2. one thread issues S^T = K_tile . Q^T on the tensor cores (M = 128 positions, N = 16
+//      heads, K = 128 dims: 8 tcgen05.mma of K = 16; A = K tile, K-major; B = the unit's
+//      rotated queries, K-major), accumulating in TMEM columns [0, 16);
+//   3. each thread reads its position's 16 scores from TMEM (thread = TMEM lane = position),
+//      scales them, masks positions past the unit's end, takes the per-head tile maximum across
+//      the CTA, and writes p = 2^(s - m) to shared memory in the storage type (the B operand of
+//      the next product, K-major); per-thread partial row sums stay in registers;
+//   4. one thread issues O^T = V^T . P^T (M = 128 dims, N = 16 heads, K = 128 positions; A = the
+//      V tile read MN-major, B = P) into TMEM columns [16, 32);
+//   5. each thread (= one dim) reads its 16 head values and folds them into its fp32
+//      accumulator with the online-softmax correction; the stage is refilled with the tile
+//      kTcStages ahead in the CTA's walk (which may belong to a later unit).
+// At a unit's end the partial (acc, m, l) per head goes to the workspace; the last chunk of a
+// (token, KV head, head block) to arrive merges them, exactly as in rope_kv_attention.cuh.
+//
+// The new token's rotated K and raw V row is written to the cache slot by head block 0 of the
+// unit holding pos and patched into the shared-memory tile that holds pos by every unit that
+// reads it, so no unit depends on another's global write (the tile may have been fetched before
+// the slot was written).
+//
+// Waits are bounded (kWaitLimit polls); a wait that runs out -- no valid input causes one --
+// sets DRK_STATUS_TIMEOUT, stops the CTA's walk, waits (bounded) for its copies in flight,
+// frees its TMEM and returns. No thread-block clusters and no cross-CTA waits.
+#pragma once
+
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "rope_kv_attention.cuh"
+#include "rope_kv_staged.cuh"
+
+namespace drk {
+
+constexpr int kTcThreads = 128;
+constexpr int kTcTile = 128;                       // positions per tile (MMA M of S^T)
+constexpr int kTcHeads = 16;                       // query heads per unit (MMA N)
+constexpr int kTcDim = 128;                        // head_dim
+constexpr int kTcStages = 3;
+constexpr uint32_t kTcBoxBytes = kTcTile * 128;    // [128 rows][64 dims] of 2 bytes: 16 KB
+constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
+constexpr uint32_t kTcQBytes = 2 * kTcHeads * 128; // [2 dim halves][16 heads][128 B]
+constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 heads][128 B]
+constexpr uint32_t kTcTmemCols = 32;               // S^T in [0, 16), O^T in [16, 32)
+
+struct TcShared {
+  uint8_t stage[kTcStages][kTcStageBytes];         // K lo, K hi, V lo, V hi boxes
+  uint8_t q[kTcQBytes];
+  uint8_t pm[kTcPBytes];
+  float red[kTcThreads / 32][kTcHeads];
+  uint4 kn[16];                                    // the new token's K row (storage type)
+  uint4 vn[16];
+  uint64_t full[kTcStages];
+  uint64_t s_bar;
+  uint64_t o_bar;
+  uint32_t tmem_base;
+  int last;
+};
+constexpr size_t kTcSmemBytes = sizeof(TcShared) + 1024;   // + alignment slack
+
+// Shared-memory matrix descriptor (tcgen05): start, leading and stride byte offsets (16-byte
+// units), descriptor version 1, swizzle layout in bits 61-63 (2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t tc_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, A/B format (0 fp16, 1 bf16), operand
+// majors (0 K-major, 1 MN-major), N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t tc_idesc(uint32_t ab, uint32_t a_mn, uint32_t b_mn,
+                                                uint32_t m, uint32_t n) {
+  return (1u << 4) | (ab << 7) | (ab << 10) | (a_mn << 15) | (b_mn << 16) | ((n >> 3) << 17) |
+         ((m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void proxy_fence_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled box (box base 1024-aligned).
+__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
+  return r * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+// One work unit of the CTA's walk, resolved from its linear index.
+struct TcUnit {
+  int64_t t, ri, pos;
+  int g, hb, chunk;
+  int64_t p0, p1;      // positions [p0, p1) of this unit
+  int ntiles;          // 0: nothing to do (chunk past pos, or invalid indices)
+  bool bad;            // invalid position or request index
+};
+
+template <typename Idx>
+__device__ __forceinline__ TcUnit tc_unit(const KernelParams& p, const AttentionParams& a,
+                                          int64_t u) {
+  TcUnit w;
+  const int64_t per_token_head = static_cast<int64_t>(a.max_chunks) * a.nhb;
+  const int64_t tg = u / per_token_head;
+  const int64_t rest = u - tg * per_token_head;
+  w.chunk = static_cast<int>(rest / a.nhb);
+  w.hb = static_cast<int>(rest - static_cast<int64_t>(w.chunk) * a.nhb);
+  w.t = tg / p.Hkv;
+  w.g = static_cast<int>(tg - w.t * p.Hkv);
+  w.pos = load_index<Idx>(p.positions, w.t);
+  w.ri = load_index<Idx>(p.request_indices, w.t);
+  w.bad = w.pos < 0 || w.pos >= p.S || w.pos >= p.table_rows || w.ri < 0 || w.ri >= p.B;
+  w.p0 = static_cast<int64_t>(w.chunk) * a.chunk;
+  w.p1 = w.bad ? w.p0 : min(w.pos + 1, w.p0 + a.chunk);
+  w.ntiles = w.p1 > w.p0 ? static_cast<int>((w.p1 - w.p0 + kTcTile - 1) / kTcTile) : 0;
+  return w;
+}
+
+// The producer's cursor over the CTA's flat sequence of (unit, tile).
+struct TcCursor {
+  int64_t u;
+  int tile;
+  TcUnit w;
+};
+
+template <typename Idx>
+__device__ __forceinline__ bool tc_cursor_valid(const KernelParams& p, const AttentionParams& a,
+                                                int64_t units, TcCursor& c) {
+  while (c.u < units) {
+    if (c.tile < c.w.ntiles) return true;
+    c.u += gridDim.x;
+    c.tile = 0;
+    if (c.u < units) c.w = tc_unit<Idx>(p, a, c.u);
+  }
+  return false;
+}
+
+template <typename E, typename Idx>
+__global__ void __launch_bounds__(kTcThreads, 1)
+rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
+                            const __grid_constant__ AttentionParams a,
+                            const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap, const int64_t units) {
+  using raw = typename E::raw;
+  constexpr uint32_t kAB = std::is_same<E, BF16>::value ? 1u : 0u;
+  static_assert(sizeof(raw) == 2, "the tensor-core path takes 16-bit caches");
+  constexpr uint32_t kIdescQK = tc_idesc(kAB, 0, 0, kTcTile, kTcHeads);
+  constexpr uint32_t kIdescPV = tc_idesc(kAB, 1, 0, kTcDim, kTcHeads);
+
+  extern __shared__ uint8_t smem_raw[];
+  TcShared& sh = *reinterpret_cast<TcShared*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = static_cast<int>(threadIdx.x);
+  const int warp = tid >> 5, lane = tid & 31;
+
+  pdl_launch_dependents();
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; ++s) mbar_init(&sh.full[s], 1);
+    mbar_init(&sh.s_bar, 1);
+    mbar_init(&sh.o_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(&sh.tmem_base)), "r"(kTcTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const uint32_t tmem_lane = static_cast<uint32_t>(warp * 32) << 16;
+  pdl_wait();
+
+  // ---- producer (thread 0): prefill the ring with the first kTcStages tiles of the walk ----
+  TcCursor prod{static_cast<int64_t>(blockIdx.x), 0, {}};
+  if (prod.u < units) prod.w = tc_unit<Idx>(p, a, prod.u);
+  int64_t issued = 0;
+  auto issue_next = [&]() {
+    if (!tc_cursor_valid<Idx>(p, a, units, prod)) return;
+    const int s = static_cast<int>(issued % kTcStages);
+    uint8_t* st = sh.stage[s];
+    const int z = static_cast<int>(prod.w.p0 + static_cast<int64_t>(prod.tile) * kTcTile);
+    const int ri = static_cast<int>(prod.w.ri);
+    mbar_expect_tx(&sh.full[s], kTcStageBytes);
+    tma_load_4d(st, &kmap, 0, prod.w.g, z, ri, &sh.full[s]);
+    tma_load_4d(st + kTcBoxBytes, &kmap, 64, prod.w.g, z, ri, &sh.full[s]);
+    tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, prod.w.g, z, ri, &sh.full[s]);
+    tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, prod.w.g, z, ri, &sh.full[s]);
+    ++issued;
+    ++prod.tile;
+  };
+  if (tid == 0)
+    for (int s = 0; s < kTcStages; ++s) issue_next();
+
+  int64_t consumed = 0;          // tiles consumed (ring position)
+  uint32_t mma_phase = 0;        // parity of s_bar / o_bar
+  bool timed_out = false;
+  const float scale = a.scale_log2;
+  const int half_r = p.R >> 1;
+  const int row = p.D + 2;
+
+  for (int64_t u = blockIdx.x; u < units && !timed_out; u += gridDim.x) {
+    const TcUnit w = tc_unit<Idx>(p, a, u);
+    if (w.bad) {
+      if (tid == 0 && w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
+        uint32_t bad = 0;
+        if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
+        if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
+        if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
+        atomicOr(p.status, bad);
+      }
+      continue;
+    }
+    if (w.ntiles == 0) continue;
+    const int h0 = w.g * a.group + w.hb * kTcHeads;
+    const int nh = min(kTcHeads, a.group - w.hb * kTcHeads);
+    const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
+    const float* crow = p.cos_t + w.pos * p.table_stride;
+    const float* srow = p.sin_t + w.pos * p.table_stride;
+
+    // ---- the unit's rotated queries -> Q^T operand (K-major, 128-byte swizzle) ----
+    for (int idx = tid; idx < kTcHeads * (kTcDim / 2); idx += kTcThreads) {
+      const int hh = idx / (kTcDim / 2);
+      const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
+      raw y0 = 0, y1 = 0;
+      if (hh < nh) {
+        const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
+                          static_cast<int64_t>(h0 + hh) * p.q_hs;
+        raw ys[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int dd = d + e;
+          if (dd < p.R) {
+            const int i = dd < half_r ? dd : dd - half_r;
+            ys[e] = E::from_f(rotate_one(E::to_f(qrow[i]), E::to_f(qrow[i + half_r]),
+                                         __ldg(crow + i), __ldg(srow + i), dd < half_r));
+          } else {
+            ys[e] = qrow[dd];
+          }
+        }
+        y0 = ys[0];
+        y1 = ys[1];
+        if (a.q_out != nullptr && w.chunk == 0) {
+          raw* qo = reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+          qo[d] = y0;
+          qo[d + 1] = y1;
+        }
+      }
+      const int box = d >> 6, db = (d & 63) * 2;     // byte within the 128-byte row
+      uint8_t* dst = sh.q + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
+      const uint32_t packed = static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16);
+      *reinterpret_cast<uint32_t*>(dst) = packed;
+    }
+    // ---- the new token's K/V rows; head block 0 appends them to the cache ----
+    const bool holds_pos = w.pos < w.p1;
+    if (holds_pos) {
+      const raw* krow = reinterpret_cast<const raw*>(p.k) + w.t * p.k_ts + w.g * p.k_hs;
+      const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
+      raw* kn = reinterpret_cast<raw*>(sh.kn);
+      raw* vn = reinterpret_cast<raw*>(sh.vn);
+      const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
+      for (int d = tid; d < kTcDim; d += kTcThreads) {
+        raw kr = krow[d];
+        if (d < p.R) {
+          const int i = d < half_r ? d : d - half_r;
+          kr = E::from_f(rotate_one(E::to_f(krow[i]), E::to_f(krow[i + half_r]),
+                                    __ldg(crow + i), __ldg(srow + i), d < half_r));
+        }
+        const raw vr = vrow[d];
+        kn[d] = kr;
+        vn[d] = vr;
+        if (w.hb == 0) {
+          reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
+          reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
+        }
+      }
+    }
+    proxy_fence_shared();
+    __syncthreads();
+
+    float m_run[kTcHeads], lp[kTcHeads], acc[kTcHeads];
+#pragma unroll
+    for (int h = 0; h < kTcHeads; ++h) {
+      m_run[h] = -INFINITY;
+      lp[h] = 0.f;
+      acc[h] = 0.f;
+    }
+
+    for (int j = 0; j < w.ntiles; ++j) {
+      const int s = static_cast<int>(consumed % kTcStages);
+      const uint32_t par = static_cast<uint32_t>((consumed / kTcStages) & 1);
+      uint8_t* st = sh.stage[s];
+      const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
+      // Every wait ends in a CTA-wide vote, so a timeout leaves the loop in all threads.
+      if (__syncthreads_or(!mbar_wait(&sh.full[s], par))) {
+        timed_out = true;
+        break;
+      }
+      if (holds_pos && w.pos >= tp0 && w.pos < tp0 + kTcTile) {
+        // Patch the new token's row into the tile: 16 chunks of K, 16 of V.
+        if (tid < 32) {
+          const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
+          const int c = tid & 15;
+          const bool is_v = tid >= 16;
+          uint8_t* base = st + (is_v ? 2 : 0) * kTcBoxBytes + (c >> 3) * kTcBoxBytes;
+          *reinterpret_cast<uint4*>(base + sw128(r, c & 7)) = is_v ? sh.vn[c] : sh.kn[c];
+        }
+        proxy_fence_shared();
+        __syncthreads();
+      }
+      // S^T = K_tile . Q^T
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t kb = smem_u32(st), qb = smem_u32(sh.q);
+#pragma unroll
+        for (int ks = 0; ks < kTcDim / 16; ++ks) {
+          const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
+          const uint64_t ad = tc_sdesc(kb + (ks >> 2) * kTcBoxBytes + off, 16, 1024);
+          const uint64_t bd = tc_sdesc(qb + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
+          tc_mma(tmem, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&sh.s_bar);
+      }
+      if (__syncthreads_or(!mbar_wait(&sh.s_bar, mma_phase))) {
+        timed_out = true;
+        break;
+      }
+      tc_fence_after();
+      float sc[kTcHeads];
+      tc_ld16(tmem + tmem_lane, sc);
+      const int64_t mypos = tp0 + tid;
+      const bool live = mypos < w.p1;
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h)
+        sc[h] = h < nh ? (live ? sc[h] * scale : -INFINITY) : 0.f;
+      // Per-head maximum over the tile's 128 positions.
+      float mx[kTcHeads];
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h) mx[h] = sc[h];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+        for (int h = 0; h < kTcHeads; ++h)
+          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+      if (lane == 0)
+#pragma unroll
+        for (int h = 0; h < kTcHeads; ++h) sh.red[warp][h] = mx[h];
+      __syncthreads();
+      float corr[kTcHeads];
+      raw pr[kTcHeads];
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h) {
+        const float mt = fmaxf(fmaxf(sh.red[0][h], sh.red[1][h]),
+                               fmaxf(sh.red[2][h], sh.red[3][h]));
+        const float m_new = fmaxf(m_run[h], mt);
+        corr[h] = exp2f(m_run[h] - m_new);
+        const float e = exp2f(sc[h] - m_new);
+        lp[h] = fmaf(lp[h], corr[h], e);
+        pr[h] = E::from_f(e);
+        m_run[h] = m_new;
+      }
+      // P (B operand, K-major: rows = heads, 64 positions per 128-byte row, two halves).
+      {
+        const int half = tid >> 6, pc = tid & 63;
+        uint8_t* pb = sh.pm + half * (kTcHeads * 128);
+#pragma unroll
+        for (int h = 0; h < kTcHeads; ++h)
+          *reinterpret_cast<raw*>(pb + sw128(h, (pc * 2) >> 4) + ((pc * 2) & 15)) = pr[h];
+      }
+      proxy_fence_shared();
+      tc_fence_before();
+      __syncthreads();
+      // O^T = V^T . P^T
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t vb = smem_u32(st + 2 * kTcBoxBytes), pb = smem_u32(sh.pm);
+#pragma unroll
+        for (int ks = 0; ks < kTcTile / 16; ++ks) {
+          const uint64_t ad = tc_sdesc(vb + ks * 2048, kTcBoxBytes, 1024);
+          const uint64_t bd = tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
+          tc_mma(tmem + kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&sh.o_bar);
+      }
+      if (__syncthreads_or(!mbar_wait(&sh.o_bar, mma_phase))) {
+        timed_out = true;
+        break;
+      }
+      mma_phase ^= 1u;
+      tc_fence_after();
+      float o[kTcHeads];
+      tc_ld16(tmem + tmem_lane + kTcHeads, o);
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h) acc[h] = fmaf(acc[h], corr[h], o[h]);
+      tc_fence_before();
+      __syncthreads();
+      ++consumed;
+      if (tid == 0) issue_next();
+    }
+    if (timed_out) break;
+
+    // ---- the unit's partial: l per head (sum over positions), then out or workspace ----
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
+    if (lane == 0)
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h) sh.red[warp][h] = lp[h];
+    __syncthreads();
+    float L[kTcHeads];
+#pragma unroll
+    for (int h = 0; h < kTcHeads; ++h)
+      L[h] = (sh.red[0][h] + sh.red[1][h]) + (sh.red[2][h] + sh.red[3][h]);
+    __syncthreads();   // sh.red is reused by the next unit
+    raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+    float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
+    const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
+    const int d = tid;   // this thread's dim of O^T
+    if (nchunks == 1) {
+#pragma unroll
+      for (int h = 0; h < kTcHeads; ++h)
+        if (h < nh) out[h * int64_t{kTcDim} + d] = E::from_f(acc[h] / L[h]);
+      continue;
+    }
+#pragma unroll
+    for (int h = 0; h < kTcHeads; ++h) {
+      if (h >= nh) continue;
+      float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
+      dst[d] = acc[h];
+      if (d == 0) {
+        dst[kTcDim] = m_run[h];
+        dst[kTcDim + 1] = L[h];
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
+    if (tid == 0) sh.last = atomicAdd(counter, 1) == nchunks - 1;
+    __syncthreads();
+    if (sh.last) {
+      __threadfence();
+      for (int h = 0; h < nh; ++h) {
+        const float* hw = ws + h * ws_head;
+        float M = -INFINITY;
+        for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(hw + c * row + kTcDim));
+        float Ls = 0.f, O = 0.f;
+        for (int c = 0; c < nchunks; ++c) {
+          const float wgt = exp2f(__ldcg(hw + c * row + kTcDim) - M);
+          Ls = fmaf(__ldcg(hw + c * row + kTcDim + 1), wgt, Ls);
+          O = fmaf(__ldcg(hw + c * row + d), wgt, O);
+        }
+        out[h * int64_t{kTcDim} + d] = E::from_f(O / Ls);
+      }
+      if (tid == 0) *counter = 0;
+    }
+    __syncthreads();   // sh.last is reused by the next unit
+  }
+
+  if (timed_out) {
+    if (tid == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+    // Let the copies this CTA issued land before its shared memory goes away.
+    if (tid == 0)
+      for (int64_t i = consumed; i < issued; ++i)
+        (void)mbar_wait(&sh.full[i % kTcStages], static_cast<uint32_t>((i / kTcStages) & 1));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTcTmemCols) : "memory");
+  }
+}
+
+}  // namespace drk

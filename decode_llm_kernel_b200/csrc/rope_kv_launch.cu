@@ -193,6 +193,8 @@ cudaError_t launch_staged_idx(const KernelParams& p, const StagedParams& sp, int
 
 }  // namespace
 
+int device_sm_count(int device) { return sm_count(device); }
+
 cudaError_t launch_rope_kv_staged(const KernelParams& p, const StagedParams& sp, int elem_code,
                                   int index_bits, int vb, int cache, const LaunchShape& shape,
                                   cudaStream_t stream) {

@@ -77,6 +77,40 @@ cudaError_t launch_rope_kv_staged(const KernelParams& p, const StagedParams& sp,
                                   int index_bits, int vb, int cache, const LaunchShape& shape,
                                   cudaStream_t stream);
 
+// Streaming multiprocessors of a device (cached per device).
+int device_sm_count(int device);
+
+// rope_kv_attention.cu: the fused RoPE + append + decode attention kernel.
+struct AttentionParams {
+  float* workspace;      // [T, Hq, max_chunks, D + 2] fp32: acc[D], m, l of each chunk
+  int* counters;         // [T, Hkv, nhb], zero on entry, zero again on exit
+  void* attn_out;        // contiguous [T, Hq, D] of the storage type
+  char* q_out;           // contiguous [T, Hq, D] or null
+  float scale_log2;      // softmax scale * log2(e)
+  int32_t chunk;         // positions per CTA
+  int32_t max_chunks;    // ceil(S / chunk)
+  int32_t group;         // Hq / Hkv
+  int32_t nhb;           // head blocks per KV head
+};
+
+struct AttentionShape {
+  int grid_x;   // max_chunks * nhb
+  int grid_y;   // Hkv
+  int grid_z;   // T
+  int lpr;      // lanes per K/V row: 8, 16 or 32
+  int hpb;      // query heads per CTA: 1, 2, 4 or 8
+  bool pdl;
+};
+cudaError_t launch_rope_kv_attention(const KernelParams& p, const AttentionParams& a,
+                                     int elem_code, int index_bits, const AttentionShape& s,
+                                     cudaStream_t stream);
+
+// rope_kv_attention_tc.cu: the tcgen05 form (16-bit, head_dim 128), a persistent grid over
+// `units` = T * Hkv * nhb * max_chunks work units of up to 16 query heads.
+cudaError_t launch_rope_kv_attention_tc(const KernelParams& p, const AttentionParams& a,
+                                        int elem_code, int index_bits, int64_t units, bool pdl,
+                                        cudaStream_t stream);
+
 // positions.cu
 cudaError_t launch_advance_positions(void* data, int index_bits, int64_t n, int64_t delta,
                                      bool pdl, cudaStream_t stream);

@@ -82,5 +82,36 @@ def advance_positions(positions, delta=1, *, pdl=False):
     require().advance_positions(positions, delta, pdl)
 
 
-__all__ = ["advance_positions", "fused_rope_kv_append", "fused_rope_kv_append_ex", "kv_append", "kv_append_ex",
-           "paged_rope_kv_append", "rope_forward", "rope_forward_ex", "separate_rope_kv_append"]
+def fused_rope_kv_append_attention(q, k, v, positions, cos, sin, k_cache, v_cache,
+                                   request_indices, *, scale=None, q_out=None, attn_out=None,
+                                   chunk=0, heads_per_cta=0, rotary_dim=0, pdl=False,
+                                   strided_cache=False, workspace=None, path="auto"):
+    """The fused append followed by the decode attention that reads the cache, one launch.
+
+    Appends exactly as fused_rope_kv_append (K slot = RoPE(k), V slot = v), then returns
+    attn_out [T, Hq, D] (q's dtype): for each token t and query head h, softmax over cache
+    positions 0..pos[t] of request ri[t] of scale * q_rot . K, applied to V, with KV head
+    h // (Hq // Hkv) (grouped-query attention). scale defaults to 1/sqrt(head_dim). Each request
+    appears at most once per call. q_out, when given, also receives q_rot. chunk and
+    heads_per_cta tune the grid (0 = chosen by the library); workspace, when given, is a
+    contiguous uint8 device tensor of at least attention_workspace_bytes(...) bytes (same
+    tuning and path). path: "auto" (tensor cores for fp16/bf16 with head_dim 128, CUDA cores
+    otherwise), "tensor_cores" or "cuda_cores"."""
+    return require().fused_rope_kv_append_attention(
+        q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
+        0.0 if scale is None else float(scale), q_out, attn_out, chunk, heads_per_cta,
+        rotary_dim, pdl, strided_cache, workspace, path)
+
+
+def attention_workspace_bytes(num_tokens, num_q_heads, num_kv_heads, head_dim, cache_alloc_len,
+                              dtype, *, chunk=0, heads_per_cta=0, device=0, path="auto"):
+    """Workspace bytes fused_rope_kv_append_attention needs for this shape and tuning."""
+    return require().attention_workspace_bytes(num_tokens, num_q_heads, num_kv_heads, head_dim,
+                                               cache_alloc_len, dtype, chunk, heads_per_cta,
+                                               device, path)
+
+
+__all__ = ["advance_positions", "attention_workspace_bytes", "fused_rope_kv_append",
+           "fused_rope_kv_append_attention", "fused_rope_kv_append_ex", "kv_append",
+           "kv_append_ex", "paged_rope_kv_append", "rope_forward", "rope_forward_ex",
+           "separate_rope_kv_append"]

@@ -192,6 +192,66 @@ DRK_API int drk_separate_rope_kv_append_noalloc(
     const drk_tensor* v_cache, const drk_tensor* request_indices, const drk_tensor* q_out,
     uint32_t* status, drk_stream_t stream);
 
+/* Tuning and semantics of drk_fused_rope_kv_append_attention; zero-initialised = defaults. */
+typedef struct drk_attention_options {
+  double scale;           /* softmax scale; 0 means 1 / sqrt(head_dim) */
+  int32_t chunk;          /* cache positions per work unit; 0 = chosen from the shape and SM
+                             count (the tensor-core kernel rounds it up to a multiple of 128) */
+  int32_t heads_per_cta;  /* CUDA-core kernel: query heads per CTA, 0 (chosen), 1, 2, 4 or 8 */
+  int32_t path;           /* DRK_ATTN_PATH_* */
+  int32_t reserved0;
+  int64_t reserved;
+} drk_attention_options;
+
+/* Kernel choice of drk_fused_rope_kv_append_attention (drk_attention_options.path). AUTO takes
+ * the tensor-core (tcgen05 + TMA) kernel for fp16/bf16 with head_dim 128 and the CUDA-core
+ * kernel otherwise; forcing the tensor-core kernel on another shape returns
+ * DRK_ERR_UNSUPPORTED. */
+enum {
+  DRK_ATTN_PATH_AUTO = 0,
+  DRK_ATTN_PATH_CUDA_CORES = 1,
+  DRK_ATTN_PATH_TENSOR_CORES = 2
+};
+
+/*
+ * Bytes of device workspace drk_fused_rope_kv_append_attention needs for this shape, with the
+ * same options and device; negative (a DRK_ERR_* code) if the shape is rejected. dtype is the
+ * element type code of q/k/v. The workspace holds per-chunk partial results (fp32) and the
+ * arrival counters of the cross-chunk merge.
+ */
+DRK_API int64_t drk_attention_workspace_bytes(int64_t num_tokens, int32_t num_q_heads,
+                                              int32_t num_kv_heads, int32_t head_dim,
+                                              int64_t cache_alloc_len, int32_t dtype,
+                                              const drk_attention_options* attn,
+                                              int32_t device);
+
+/*
+ * The fused append followed by the decode attention that consumes the cache, in one launch:
+ * the write side of drk_fused_rope_kv_append and the read side the reference prices separately
+ * (SDPA over the token-major cache viewed head-major, benchmarks/probe_cache_read.py:26-172 and
+ * results/LIMITATIONS.md:153-157 of the reference). No counterpart kernel in the reference.
+ *
+ * For each token t it performs the fused op's append exactly (K slot = RoPE(k[t]), V slot =
+ * v[t], bit-identical to drk_fused_rope_kv_append), optionally writes q_out = RoPE(q) (NULL to
+ * skip), and writes attn_out[t, h] = softmax(scale * q_rot[t, h] . K[ri, p, g]) V[ri, p, g]
+ * over cache positions p = 0..pos[t] of request ri[t] and KV head g = h / (Hq / Hkv), with the
+ * new token's own K/V at p = pos[t]. Softmax and accumulation run in fp32; attn_out
+ * ([T, Hq, D] contiguous, q's dtype) is rounded once.
+ *
+ * Each request appears at most once per call (one new token per sequence, the decode
+ * contract). fp32, fp16 and bf16; head_dim * element size a multiple of 16 bytes and head_dim
+ * <= 256 (16-bit) or 128 (fp32); cache base and strides 16-byte aligned; T <= 65535. opts
+ * accepts DRK_FLAG_PDL, DRK_FLAG_STRIDED_CACHE and rotary_dim. workspace is device memory of
+ * at least drk_attention_workspace_bytes for the same arguments; calls that overlap on the
+ * GPU need separate workspaces. Other shapes return DRK_ERR_UNSUPPORTED.
+ */
+DRK_API int drk_fused_rope_kv_append_attention(
+    const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,
+    const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* k_cache,
+    const drk_tensor* v_cache, const drk_tensor* request_indices, const drk_tensor* q_out,
+    const drk_tensor* attn_out, const drk_attention_options* attn, void* workspace,
+    size_t workspace_bytes, const drk_options* opts, uint32_t* status, drk_stream_t stream);
+
 /*
  * positions[t] += delta for every token: the device-side step of a decode loop, so a captured
  * step ending with this call replays without a host-side position copy. No counterpart in the
