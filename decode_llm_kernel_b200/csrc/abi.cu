@@ -757,6 +757,12 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
   const int index_bits_tc = positions->dtype == DRK_I32 ? 32 : 64;
   if (pl.tc) {
     const int64_t units = T * Hkv * pl.nhb * pl.max_chunks;
+    // One round of 16-byte loads for the query rotation: full rotary, aligned q rows, q_out and
+    // table rows.
+    const uintptr_t qa = reinterpret_cast<uintptr_t>(q->data) |
+                         (q_out ? reinterpret_cast<uintptr_t>(q_out->data) : 0);
+    const int64_t qs = (T > 1 ? q->strides[0] : 0) | (Hq > 1 ? q->strides[1] : 0);
+    a.q_vec = (R == D && qa % 16 == 0 && (qs * es) % 16 == 0 && p.table_vec4) ? 1 : 0;
     check_launch(drk::launch_rope_kv_attention_tc(p, a, elem_code(q->dtype), index_bits_tc, units,
                                                   (o.flags & DRK_FLAG_PDL) != 0, s));
     return;

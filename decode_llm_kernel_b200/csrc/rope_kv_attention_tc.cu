@@ -49,10 +49,10 @@ cudaError_t encode_cache_map(CUtensorMap* map, const void* base, bool bf16,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <typename E, typename Idx>
+template <typename E, typename Idx, int HR>
 cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t units, bool pdl,
                       cudaStream_t stream) {
-  auto kernel = rope_kv_attention_tc_kernel<E, Idx>;
+  auto kernel = rope_kv_attention_tc_kernel<E, Idx, HR>;
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
@@ -77,7 +77,7 @@ cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t u
   const int grid = static_cast<int>(units < sms ? units : sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.blockDim = dim3(kTcBlock, 1, 1);
   cfg.dynamicSmemBytes = kTcSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -90,6 +90,18 @@ cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t u
   return cudaLaunchKernelEx(&cfg, kernel, p, a, kmap, vmap, units);
 }
 
+template <typename E, typename Idx>
+cudaError_t launch_tc_hr(const KernelParams& p, const AttentionParams& a, int64_t units, bool pdl,
+                         cudaStream_t stream) {
+  // Real query heads per unit: the group size rounded up to a power of two, at most 16.
+  const int g = a.group < kTcHeads ? a.group : kTcHeads;
+  if (g <= 1) return launch_tc<E, Idx, 1>(p, a, units, pdl, stream);
+  if (g <= 2) return launch_tc<E, Idx, 2>(p, a, units, pdl, stream);
+  if (g <= 4) return launch_tc<E, Idx, 4>(p, a, units, pdl, stream);
+  if (g <= 8) return launch_tc<E, Idx, 8>(p, a, units, pdl, stream);
+  return launch_tc<E, Idx, 16>(p, a, units, pdl, stream);
+}
+
 }  // namespace
 
 cudaError_t launch_rope_kv_attention_tc(const KernelParams& p, const AttentionParams& a,
@@ -98,11 +110,11 @@ cudaError_t launch_rope_kv_attention_tc(const KernelParams& p, const AttentionPa
   if (units <= 0) return cudaSuccess;
   switch (elem_code) {
     case kElemF16:
-      return index_bits == 32 ? launch_tc<F16, int>(p, a, units, pdl, stream)
-                              : launch_tc<F16, long long>(p, a, units, pdl, stream);
+      return index_bits == 32 ? launch_tc_hr<F16, int>(p, a, units, pdl, stream)
+                              : launch_tc_hr<F16, long long>(p, a, units, pdl, stream);
     case kElemBF16:
-      return index_bits == 32 ? launch_tc<BF16, int>(p, a, units, pdl, stream)
-                              : launch_tc<BF16, long long>(p, a, units, pdl, stream);
+      return index_bits == 32 ? launch_tc_hr<BF16, int>(p, a, units, pdl, stream)
+                              : launch_tc_hr<BF16, long long>(p, a, units, pdl, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -2,23 +2,34 @@
 // 16-bit caches with head_dim 128: the bandwidth form of rope_kv_attention.cuh.
 //
 // Work unit: (token t, KV head g, head block hb of up to 16 query heads, chunk of positions).
-// A persistent grid (one CTA per SM, 128 threads) walks units u = blockIdx.x, +gridDim.x, ...
-// and streams each unit's positions in tiles of 128 through a kTcStages-deep ring of shared
-// memory stages. Per tile:
+// A persistent grid (one CTA per SM) walks units u = blockIdx.x, +gridDim.x, ... and streams
+// each unit's positions in tiles of 128 through a kTcStages-deep ring of shared-memory stages.
+// Three roles, synchronised by mbarriers only:
+//   - warp 4, the producer, walks the CTA's sequence of tiles and refills a stage as soon as the
+//     tensor core has finished reading it (an "empty" mbarrier that tcgen05.commit arrives on
+//     after the tile's last MMA), so the ring stays full;
+//   - warp 5 issues the MMAs (one lane) and patches the new token's row into the tile holding
+//     it, so no softmax thread ever waits on an MMA issue;
+//   - warps 0-3 (the 128 TMEM lanes) run the softmax, the output correction and the chunk
+//     merge, synchronising among themselves with a named barrier.
+// Per tile:
 //   1. TMA (cp.async.bulk.tensor, 128-byte swizzle) brings K[128 positions][128 dims] and V of
 //      the same rows, as two 64-dim boxes each (64 KB), completing on the stage's mbarrier;
 //   2. one thread issues S^T = K_tile . Q^T on the tensor cores (M = 128 positions, N = 16
 //      heads, K = 128 dims: 8 tcgen05.mma of K = 16; A = K tile, K-major; B = the unit's
-//      rotated queries, K-major), accumulating in TMEM columns [0, 16);
-//   3. each thread reads its position's 16 scores from TMEM (thread = TMEM lane = position),
+//      rotated queries, K-major) into a TMEM accumulator;
+//   3. each thread reads its position's scores from TMEM (thread = TMEM lane = position),
 //      scales them, masks positions past the unit's end, takes the per-head tile maximum across
-//      the CTA, and writes p = 2^(s - m) to shared memory in the storage type (the B operand of
-//      the next product, K-major); per-thread partial row sums stay in registers;
+//      the consumers, and writes p = 2^(s - m) to shared memory in the storage type (the B
+//      operand of the next product, K-major); per-thread partial row sums stay in registers;
 //   4. one thread issues O^T = V^T . P^T (M = 128 dims, N = 16 heads, K = 128 positions; A = the
-//      V tile read MN-major, B = P) into TMEM columns [16, 32);
-//   5. each thread (= one dim) reads its 16 head values and folds them into its fp32
-//      accumulator with the online-softmax correction; the stage is refilled with the tile
-//      kTcStages ahead in the CTA's walk (which may belong to a later unit).
+//      V tile read MN-major, B = P) into a second TMEM accumulator;
+//   5. each thread (= one dim) reads its head values and folds them into its fp32 accumulator
+//      with the online-softmax correction.
+// S^T, O^T and P are double-buffered: the next tile's QK is issued with this tile's PV, and this
+// tile's O^T is read after the next tile's softmax. Only the HR real heads of a unit (the group
+// size rounded up to a power of two, at most 16) go through the softmax; the MMA always runs
+// N = 16 with zero query rows.
 // At a unit's end the partial (acc, m, l) per head goes to the workspace; the last chunk of a
 // (token, KV head, head block) to arrive merges them, exactly as in rope_kv_attention.cuh.
 //
@@ -28,8 +39,9 @@
 // the slot was written).
 //
 // Waits are bounded (kWaitLimit polls); a wait that runs out -- no valid input causes one --
-// sets DRK_STATUS_TIMEOUT, stops the CTA's walk, waits (bounded) for its copies in flight,
-// frees its TMEM and returns. No thread-block clusters and no cross-CTA waits.
+// sets DRK_STATUS_TIMEOUT and ends the CTA's walk; the producer waits (bounded) for the copies it
+// issued, and the CTA frees its TMEM and returns. No thread-block clusters and no cross-CTA
+// waits.
 #pragma once
 
 #include <cuda.h>
@@ -41,7 +53,10 @@
 
 namespace drk {
 
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 128;                    // consumers: warps 0-3
+constexpr int kTcProducerWarp = 4;
+constexpr int kTcMmaWarp = 5;
+constexpr int kTcBlock = kTcThreads + 64;          // + the producer and MMA warps
 constexpr int kTcTile = 128;                       // positions per tile (MMA M of S^T)
 constexpr int kTcHeads = 16;                       // query heads per unit (MMA N)
 constexpr int kTcDim = 128;                        // head_dim
@@ -50,18 +65,23 @@ constexpr uint32_t kTcBoxBytes = kTcTile * 128;    // [128 rows][64 dims] of 2 b
 constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
 constexpr uint32_t kTcQBytes = 2 * kTcHeads * 128; // [2 dim halves][16 heads][128 B]
 constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 heads][128 B]
-constexpr uint32_t kTcTmemCols = 32;               // S^T in [0, 16), O^T in [16, 32)
+constexpr uint32_t kTcTmemCols = 64;               // S^T buffers at 0, 16; O^T at 32, 48
 
 struct TcShared {
   uint8_t stage[kTcStages][kTcStageBytes];         // K lo, K hi, V lo, V hi boxes
   uint8_t q[kTcQBytes];
-  uint8_t pm[kTcPBytes];
-  float red[kTcThreads / 32][kTcHeads];
+  uint8_t pm[2][kTcPBytes];                        // P, double-buffered across tiles
+  float red[2][kTcThreads / 32][kTcHeads];         // per-warp tile maxima, double-buffered
+  float lsum[kTcThreads / 32][kTcHeads];           // per-warp row sums at a unit's end
+  float mrg[2][kTcHeads][32];                      // merge: (m, l) of up to 32 chunks per head
   uint4 kn[16];                                    // the new token's K row (storage type)
   uint4 vn[16];
   uint64_t full[kTcStages];
-  uint64_t s_bar;
-  uint64_t o_bar;
+  uint64_t empty[kTcStages];
+  uint64_t s_bar[2];                               // QK done (tcgen05.commit)
+  uint64_t o_bar[2];                               // PV done (tcgen05.commit)
+  uint64_t p_bar[2];                               // P written (128 consumer arrivals)
+  uint64_t q_bar;                                  // unit's Q and new K/V rows written (128)
   uint32_t tmem_base;
   int last;
 };
@@ -106,6 +126,28 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 __device__ __forceinline__ void proxy_fence_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier 1 over the 128 consumer threads (the producer warp never joins it).
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kTcThreads) : "memory");
+}
+// consumer_sync that also ORs a predicate over the consumers.
+__device__ __forceinline__ bool consumer_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kTcThreads)
+      : "memory");
+  return r != 0;
 }
 
 // 16 consecutive fp32 columns of this thread's TMEM lane.
@@ -186,8 +228,8 @@ __device__ __forceinline__ bool tc_cursor_valid(const KernelParams& p, const Att
   return false;
 }
 
-template <typename E, typename Idx>
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <typename E, typename Idx, int HR>
+__global__ void __launch_bounds__(kTcBlock, 1)
 rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
                             const __grid_constant__ AttentionParams a,
                             const __grid_constant__ CUtensorMap kmap,
@@ -195,6 +237,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   using raw = typename E::raw;
   constexpr uint32_t kAB = std::is_same<E, BF16>::value ? 1u : 0u;
   static_assert(sizeof(raw) == 2, "the tensor-core path takes 16-bit caches");
+  static_assert(HR >= 1 && HR <= kTcHeads, "HR real heads per unit, at most the MMA N");
   constexpr uint32_t kIdescQK = tc_idesc(kAB, 0, 0, kTcTile, kTcHeads);
   constexpr uint32_t kIdescPV = tc_idesc(kAB, 1, 0, kTcDim, kTcHeads);
 
@@ -206,316 +249,452 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
 
   pdl_launch_dependents();
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) mbar_init(&sh.full[s], 1);
-    mbar_init(&sh.s_bar, 1);
-    mbar_init(&sh.o_bar, 1);
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.s_bar[b], 1);
+      mbar_init(&sh.o_bar[b], 1);
+      mbar_init(&sh.p_bar[b], kTcThreads);
+    }
+    mbar_init(&sh.q_bar, kTcThreads);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // P rows of heads past HR are never written per tile: zero both buffers once.
+  for (int i = tid; i < static_cast<int>(2 * kTcPBytes / 16); i += kTcBlock)
+    reinterpret_cast<uint4*>(sh.pm)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_u32(&sh.tmem_base)), "r"(kTcTmemCols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  proxy_fence_shared();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
-  const uint32_t tmem_lane = static_cast<uint32_t>(warp * 32) << 16;
   pdl_wait();
 
-  // ---- producer (thread 0): prefill the ring with the first kTcStages tiles of the walk ----
-  TcCursor prod{static_cast<int64_t>(blockIdx.x), 0, {}};
-  if (prod.u < units) prod.w = tc_unit<Idx>(p, a, prod.u);
-  int64_t issued = 0;
-  auto issue_next = [&]() {
-    if (!tc_cursor_valid<Idx>(p, a, units, prod)) return;
-    const int s = static_cast<int>(issued % kTcStages);
-    uint8_t* st = sh.stage[s];
-    const int z = static_cast<int>(prod.w.p0 + static_cast<int64_t>(prod.tile) * kTcTile);
-    const int ri = static_cast<int>(prod.w.ri);
-    mbar_expect_tx(&sh.full[s], kTcStageBytes);
-    tma_load_4d(st, &kmap, 0, prod.w.g, z, ri, &sh.full[s]);
-    tma_load_4d(st + kTcBoxBytes, &kmap, 64, prod.w.g, z, ri, &sh.full[s]);
-    tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, prod.w.g, z, ri, &sh.full[s]);
-    tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, prod.w.g, z, ri, &sh.full[s]);
-    ++issued;
-    ++prod.tile;
-  };
-  if (tid == 0)
-    for (int s = 0; s < kTcStages; ++s) issue_next();
+  auto stage_of = [&](int64_t c) { return sh.stage[static_cast<int>(c % kTcStages)]; };
+  auto full_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kTcStages) & 1); };
+  auto pair_parity = [&](int64_t c) { return static_cast<uint32_t>((c >> 1) & 1); };
 
-  int64_t consumed = 0;          // tiles consumed (ring position)
-  uint32_t mma_phase = 0;        // parity of s_bar / o_bar
-  bool timed_out = false;
-  const float scale = a.scale_log2;
-  const int half_r = p.R >> 1;
-  const int row = p.D + 2;
-
-  for (int64_t u = blockIdx.x; u < units && !timed_out; u += gridDim.x) {
-    const TcUnit w = tc_unit<Idx>(p, a, u);
-    if (w.bad) {
-      if (tid == 0 && w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
-        uint32_t bad = 0;
-        if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
-        if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
-        if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
-        atomicOr(p.status, bad);
+  if (warp == kTcProducerWarp) {
+    // ---- producer (one lane): refill each stage once its last MMA has read it ----
+    if (lane == 0) {
+      TcCursor prod{static_cast<int64_t>(blockIdx.x), 0, {}};
+      if (prod.u < units) prod.w = tc_unit<Idx>(p, a, prod.u);
+      int64_t issued = 0;
+      bool ok = true;
+      while (tc_cursor_valid<Idx>(p, a, units, prod)) {
+        const int s = static_cast<int>(issued % kTcStages);
+        if (issued >= kTcStages)
+          ok = mbar_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
+        if (!ok) break;
+        uint8_t* st = sh.stage[s];
+        const int z = static_cast<int>(prod.w.p0 + static_cast<int64_t>(prod.tile) * kTcTile);
+        const int ri = static_cast<int>(prod.w.ri);
+        mbar_expect_tx(&sh.full[s], kTcStageBytes);
+        tma_load_4d(st, &kmap, 0, prod.w.g, z, ri, &sh.full[s]);
+        tma_load_4d(st + kTcBoxBytes, &kmap, 64, prod.w.g, z, ri, &sh.full[s]);
+        tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, prod.w.g, z, ri, &sh.full[s]);
+        tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, prod.w.g, z, ri, &sh.full[s]);
+        ++issued;
+        ++prod.tile;
       }
-      continue;
+      if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+      // Every copy this CTA issued lands before its shared memory goes away.
+      for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i)
+        (void)mbar_wait(&sh.full[i % kTcStages], static_cast<uint32_t>((i / kTcStages) & 1));
     }
-    if (w.ntiles == 0) continue;
-    const int h0 = w.g * a.group + w.hb * kTcHeads;
-    const int nh = min(kTcHeads, a.group - w.hb * kTcHeads);
-    const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
-    const float* crow = p.cos_t + w.pos * p.table_stride;
-    const float* srow = p.sin_t + w.pos * p.table_stride;
-
-    // ---- the unit's rotated queries -> Q^T operand (K-major, 128-byte swizzle) ----
-    for (int idx = tid; idx < kTcHeads * (kTcDim / 2); idx += kTcThreads) {
-      const int hh = idx / (kTcDim / 2);
-      const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
-      raw y0 = 0, y1 = 0;
-      if (hh < nh) {
-        const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
-                          static_cast<int64_t>(h0 + hh) * p.q_hs;
-        raw ys[2];
+  } else if (warp == kTcMmaWarp) {
+    // ---- MMA issuer: per tile c, S^T(c) = K . Q^T once its data has landed, then
+    //      O^T(c - 1) = V^T . P^T(c - 1) once the consumers have written P(c - 1) ----
+    auto issue_qk = [&](const uint8_t* st, int b) {
+      const uint32_t kb = smem_u32(st), qb = smem_u32(sh.q);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int dd = d + e;
-          if (dd < p.R) {
-            const int i = dd < half_r ? dd : dd - half_r;
-            ys[e] = E::from_f(rotate_one(E::to_f(qrow[i]), E::to_f(qrow[i + half_r]),
-                                         __ldg(crow + i), __ldg(srow + i), dd < half_r));
-          } else {
-            ys[e] = qrow[dd];
+      for (int ks = 0; ks < kTcDim / 16; ++ks) {
+        const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
+        const uint64_t ad = tc_sdesc(kb + (ks >> 2) * kTcBoxBytes + off, 16, 1024);
+        const uint64_t bd = tc_sdesc(qb + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
+        tc_mma(tmem + b * kTcHeads, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+      }
+      tc_commit(&sh.s_bar[b]);
+    };
+    auto issue_pv = [&](int64_t c) {
+      const int b = static_cast<int>(c & 1);
+      const uint8_t* st = stage_of(c);
+      const uint32_t vb = smem_u32(st + 2 * kTcBoxBytes), pb = smem_u32(sh.pm[b]);
+#pragma unroll
+      for (int ks = 0; ks < kTcTile / 16; ++ks) {
+        const uint64_t ad = tc_sdesc(vb + ks * 2048, kTcBoxBytes, 1024);
+        const uint64_t bd =
+            tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
+        tc_mma(tmem + 2 * kTcHeads + b * kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
+      }
+      tc_commit(&sh.o_bar[b]);
+      tc_commit(&sh.empty[static_cast<int>(c % kTcStages)]);
+    };
+    int64_t cj = 0, nunits = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const TcUnit w = tc_unit<Idx>(p, a, u);
+      if (w.bad || w.ntiles == 0) continue;
+      // Wait results are made warp-uniform so the warp never splits at a __syncwarp.
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.q_bar, static_cast<uint32_t>(nunits & 1)));
+      ++nunits;
+      const bool holds_pos = w.pos < w.p1;
+      for (int j = 0; j <= w.ntiles && ok; ++j) {
+        const int64_t c = cj + j;
+        if (j < w.ntiles) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&sh.full[c % kTcStages], full_parity(c)));
+          if (!ok) break;
+          const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
+          if (holds_pos && w.pos >= tp0 && w.pos < tp0 + kTcTile) {
+            // The new token's K and V row, 16 chunks each, into the staged tile.
+            const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
+            const int ch = lane & 15;
+            const bool is_v = lane >= 16;
+            uint8_t* base = stage_of(c) + (is_v ? 2 : 0) * kTcBoxBytes + (ch >> 3) * kTcBoxBytes;
+            *reinterpret_cast<uint4*>(base + sw128(r, ch & 7)) = is_v ? sh.vn[ch] : sh.kn[ch];
+            proxy_fence_shared();
+          }
+          __syncwarp();
+          if (lane == 0) {
+            tc_fence_after();
+            issue_qk(stage_of(c), static_cast<int>(c & 1));
+          }
+          __syncwarp();
+        }
+        if (j >= 1) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&sh.p_bar[(c - 1) & 1], pair_parity(c - 1)));
+          if (!ok) break;
+          if (lane == 0) {
+            tc_fence_after();
+            issue_pv(c - 1);
+          }
+          __syncwarp();
+        }
+      }
+      cj += w.ntiles;
+    }
+    if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+  } else {
+    // ---- consumers (warps 0-3): softmax, output correction, chunk merge ----
+    const uint32_t tmem_lane = static_cast<uint32_t>(warp * 32) << 16;
+    int64_t cj = 0;                // tiles of the walk consumed so far
+    bool timed_out = false;
+    const float scale = a.scale_log2;
+    const int half_r = p.R >> 1;
+    const int row = p.D + 2;
+
+    for (int64_t u = blockIdx.x; u < units && !timed_out; u += gridDim.x) {
+      const TcUnit w = tc_unit<Idx>(p, a, u);
+      if (w.bad) {
+        if (tid == 0 && w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
+          uint32_t bad = 0;
+          if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
+          if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
+          if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
+          atomicOr(p.status, bad);
+        }
+        continue;
+      }
+      if (w.ntiles == 0) continue;
+      const int h0 = w.g * a.group + w.hb * kTcHeads;
+      const int nh = min(HR, a.group - w.hb * kTcHeads);
+      const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
+      const float* crow = p.cos_t + w.pos * p.table_stride;
+      const float* srow = p.sin_t + w.pos * p.table_stride;
+
+      // ---- the unit's rotated queries -> Q^T operand (K-major, 128-byte swizzle). Every QK
+      //      of the previous unit has completed: its last S^T was read below. ----
+      if (a.q_vec) {
+        // Full rotary, 16-byte rows: thread = (head, 8-dim chunk of the first half); one round
+        // of loads, both halves of the rotate_half pair from one thread.
+        const int hh = tid >> 3, c = tid & 7;
+        uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+        if (hh < nh) {
+          const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
+                            static_cast<int64_t>(h0 + hh) * p.q_hs;
+          const uint4 x1 = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+          const uint4 x2 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
+          const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
+          const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
+          const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          float f1[8], f2[8];
+          unpack16<E>(x1, f1);
+          unpack16<E>(x2, f2);
+          uint32_t wl[4], wh[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e0 = 2 * i, e1 = 2 * i + 1;
+            const raw a0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], true));
+            const raw a1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], true));
+            const raw b0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], false));
+            const raw b1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], false));
+            wl[i] = static_cast<uint32_t>(a0) | (static_cast<uint32_t>(a1) << 16);
+            wh[i] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
+          }
+          lo = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+          hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+          if (a.q_out != nullptr && w.chunk == 0) {
+            raw* qo = reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+            *reinterpret_cast<uint4*>(qo + 8 * c) = lo;
+            *reinterpret_cast<uint4*>(qo + 64 + 8 * c) = hi;
           }
         }
-        y0 = ys[0];
-        y1 = ys[1];
-        if (a.q_out != nullptr && w.chunk == 0) {
-          raw* qo = reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
-          qo[d] = y0;
-          qo[d + 1] = y1;
-        }
-      }
-      const int box = d >> 6, db = (d & 63) * 2;     // byte within the 128-byte row
-      uint8_t* dst = sh.q + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
-      const uint32_t packed = static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16);
-      *reinterpret_cast<uint32_t*>(dst) = packed;
-    }
-    // ---- the new token's K/V rows; head block 0 appends them to the cache ----
-    const bool holds_pos = w.pos < w.p1;
-    if (holds_pos) {
-      const raw* krow = reinterpret_cast<const raw*>(p.k) + w.t * p.k_ts + w.g * p.k_hs;
-      const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
-      raw* kn = reinterpret_cast<raw*>(sh.kn);
-      raw* vn = reinterpret_cast<raw*>(sh.vn);
-      const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
-      for (int d = tid; d < kTcDim; d += kTcThreads) {
-        raw kr = krow[d];
-        if (d < p.R) {
-          const int i = d < half_r ? d : d - half_r;
-          kr = E::from_f(rotate_one(E::to_f(krow[i]), E::to_f(krow[i + half_r]),
-                                    __ldg(crow + i), __ldg(srow + i), d < half_r));
-        }
-        const raw vr = vrow[d];
-        kn[d] = kr;
-        vn[d] = vr;
-        if (w.hb == 0) {
-          reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
-          reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
-        }
-      }
-    }
-    proxy_fence_shared();
-    __syncthreads();
-
-    float m_run[kTcHeads], lp[kTcHeads], acc[kTcHeads];
+        *reinterpret_cast<uint4*>(sh.q + sw128(hh, c)) = lo;
+        *reinterpret_cast<uint4*>(sh.q + kTcHeads * 128 + sw128(hh, c)) = hi;
+      } else {
+        for (int idx = tid; idx < kTcHeads * (kTcDim / 2); idx += kTcThreads) {
+          const int hh = idx / (kTcDim / 2);
+          const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
+          raw y0 = 0, y1 = 0;
+          if (hh < nh) {
+            const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
+                              static_cast<int64_t>(h0 + hh) * p.q_hs;
+            raw ys[2];
 #pragma unroll
-    for (int h = 0; h < kTcHeads; ++h) {
-      m_run[h] = -INFINITY;
-      lp[h] = 0.f;
-      acc[h] = 0.f;
-    }
-
-    for (int j = 0; j < w.ntiles; ++j) {
-      const int s = static_cast<int>(consumed % kTcStages);
-      const uint32_t par = static_cast<uint32_t>((consumed / kTcStages) & 1);
-      uint8_t* st = sh.stage[s];
-      const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
-      // Every wait ends in a CTA-wide vote, so a timeout leaves the loop in all threads.
-      if (__syncthreads_or(!mbar_wait(&sh.full[s], par))) {
-        timed_out = true;
-        break;
-      }
-      if (holds_pos && w.pos >= tp0 && w.pos < tp0 + kTcTile) {
-        // Patch the new token's row into the tile: 16 chunks of K, 16 of V.
-        if (tid < 32) {
-          const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
-          const int c = tid & 15;
-          const bool is_v = tid >= 16;
-          uint8_t* base = st + (is_v ? 2 : 0) * kTcBoxBytes + (c >> 3) * kTcBoxBytes;
-          *reinterpret_cast<uint4*>(base + sw128(r, c & 7)) = is_v ? sh.vn[c] : sh.kn[c];
+            for (int e = 0; e < 2; ++e) {
+              const int dd = d + e;
+              if (dd < p.R) {
+                const int i = dd < half_r ? dd : dd - half_r;
+                ys[e] = E::from_f(rotate_one(E::to_f(qrow[i]), E::to_f(qrow[i + half_r]),
+                                             __ldg(crow + i), __ldg(srow + i), dd < half_r));
+              } else {
+                ys[e] = qrow[dd];
+              }
+            }
+            y0 = ys[0];
+            y1 = ys[1];
+            if (a.q_out != nullptr && w.chunk == 0) {
+              raw* qo =
+                  reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+              qo[d] = y0;
+              qo[d + 1] = y1;
+            }
+          }
+          const int box = d >> 6, db = (d & 63) * 2;     // byte within the 128-byte row
+          uint8_t* dst = sh.q + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
+          *reinterpret_cast<uint32_t*>(dst) =
+              static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16);
         }
-        proxy_fence_shared();
-        __syncthreads();
       }
-      // S^T = K_tile . Q^T
-      if (tid == 0) {
+      // ---- the new token's K/V rows (patched into its tile by the MMA warp); head block 0
+      //      appends them to the cache ----
+      const bool holds_pos = w.pos < w.p1;
+      if (holds_pos) {
+        const raw* krow = reinterpret_cast<const raw*>(p.k) + w.t * p.k_ts + w.g * p.k_hs;
+        const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
+        raw* kn = reinterpret_cast<raw*>(sh.kn);
+        raw* vn = reinterpret_cast<raw*>(sh.vn);
+        const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
+        for (int d = tid; d < kTcDim; d += kTcThreads) {
+          raw kr = krow[d];
+          if (d < p.R) {
+            const int i = d < half_r ? d : d - half_r;
+            kr = E::from_f(rotate_one(E::to_f(krow[i]), E::to_f(krow[i + half_r]),
+                                      __ldg(crow + i), __ldg(srow + i), d < half_r));
+          }
+          const raw vr = vrow[d];
+          kn[d] = kr;
+          vn[d] = vr;
+          if (w.hb == 0) {
+            reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
+            reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
+          }
+        }
+      }
+      proxy_fence_shared();
+      mbar_arrive(&sh.q_bar);
+
+      float m_run[HR], lp[HR], acc[HR], corr_prev[HR];
+#pragma unroll
+      for (int h = 0; h < HR; ++h) {
+        m_run[h] = -INFINITY;
+        lp[h] = 0.f;
+        acc[h] = 0.f;
+        corr_prev[h] = 0.f;
+      }
+      bool ok = true;
+      for (int j = 0; j < w.ntiles; ++j) {
+        const int64_t c = cj + j;
+        const int b = static_cast<int>(c & 1);
+        ok = mbar_wait(&sh.s_bar[b], pair_parity(c)) && ok;
         tc_fence_after();
-        const uint32_t kb = smem_u32(st), qb = smem_u32(sh.q);
+        float sc[kTcHeads];
+        tc_ld16(tmem + tmem_lane + b * kTcHeads, sc);
+        const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
+        const bool live = tp0 + tid < w.p1;
+        float mx[HR];
 #pragma unroll
-        for (int ks = 0; ks < kTcDim / 16; ++ks) {
-          const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
-          const uint64_t ad = tc_sdesc(kb + (ks >> 2) * kTcBoxBytes + off, 16, 1024);
-          const uint64_t bd = tc_sdesc(qb + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
-          tc_mma(tmem, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+        for (int h = 0; h < HR; ++h) {
+          sc[h] = h < nh ? (live ? sc[h] * scale : -INFINITY) : 0.f;
+          mx[h] = sc[h];
         }
-        tc_commit(&sh.s_bar);
-      }
-      if (__syncthreads_or(!mbar_wait(&sh.s_bar, mma_phase))) {
-        timed_out = true;
-        break;
-      }
-      tc_fence_after();
-      float sc[kTcHeads];
-      tc_ld16(tmem + tmem_lane, sc);
-      const int64_t mypos = tp0 + tid;
-      const bool live = mypos < w.p1;
 #pragma unroll
-      for (int h = 0; h < kTcHeads; ++h)
-        sc[h] = h < nh ? (live ? sc[h] * scale : -INFINITY) : 0.f;
-      // Per-head maximum over the tile's 128 positions.
-      float mx[kTcHeads];
+        for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
-      for (int h = 0; h < kTcHeads; ++h) mx[h] = sc[h];
+          for (int h = 0; h < HR; ++h)
+            mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+        if (lane == 0)
+#pragma unroll
+          for (int h = 0; h < HR; ++h) sh.red[b][warp][h] = mx[h];
+        // One consumer barrier per tile, which also carries the timeout vote.
+        if (consumer_any(!ok)) {
+          timed_out = true;
+          break;
+        }
+        float corr_cur[HR];
+        {
+          const int half = tid >> 6, pc = tid & 63;
+          uint8_t* pb = sh.pm[b] + half * (kTcHeads * 128);
+#pragma unroll
+          for (int h = 0; h < HR; ++h) {
+            const float mt = fmaxf(fmaxf(sh.red[b][0][h], sh.red[b][1][h]),
+                                   fmaxf(sh.red[b][2][h], sh.red[b][3][h]));
+            const float m_new = fmaxf(m_run[h], mt);
+            corr_cur[h] = exp2f(m_run[h] - m_new);
+            const float e = exp2f(sc[h] - m_new);
+            lp[h] = fmaf(lp[h], corr_cur[h], e);
+            m_run[h] = m_new;
+            *reinterpret_cast<raw*>(pb + sw128(h, (pc * 2) >> 4) + ((pc * 2) & 15)) =
+                E::from_f(e);
+          }
+        }
+        // P(c) is ready, and this thread is done with S^T(c) and O^T(c - 2).
+        proxy_fence_shared();
+        tc_fence_before();
+        mbar_arrive(&sh.p_bar[b]);
+        if (j >= 1) {
+          // The previous tile's O^T: its PV ran while this tile's softmax did.
+          ok = mbar_wait(&sh.o_bar[b ^ 1], pair_parity(c - 1)) && ok;
+          tc_fence_after();
+          float o[kTcHeads];
+          tc_ld16(tmem + tmem_lane + 2 * kTcHeads + (b ^ 1) * kTcHeads, o);
+#pragma unroll
+          for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < HR; ++h) corr_prev[h] = corr_cur[h];
+      }
+      if (timed_out) break;
+      {
+        const int64_t c = cj + w.ntiles - 1;
+        ok = mbar_wait(&sh.o_bar[c & 1], pair_parity(c)) && ok;
+        tc_fence_after();
+        float o[kTcHeads];
+        tc_ld16(tmem + tmem_lane + 2 * kTcHeads + static_cast<int>(c & 1) * kTcHeads, o);
+#pragma unroll
+        for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
+        tc_fence_before();
+      }
+      cj += w.ntiles;
+
+      // ---- the unit's partial: l per head (sum over positions), then out or workspace ----
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
-        for (int h = 0; h < kTcHeads; ++h)
-          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+        for (int h = 0; h < HR; ++h) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
       if (lane == 0)
 #pragma unroll
-        for (int h = 0; h < kTcHeads; ++h) sh.red[warp][h] = mx[h];
-      __syncthreads();
-      float corr[kTcHeads];
-      raw pr[kTcHeads];
-#pragma unroll
-      for (int h = 0; h < kTcHeads; ++h) {
-        const float mt = fmaxf(fmaxf(sh.red[0][h], sh.red[1][h]),
-                               fmaxf(sh.red[2][h], sh.red[3][h]));
-        const float m_new = fmaxf(m_run[h], mt);
-        corr[h] = exp2f(m_run[h] - m_new);
-        const float e = exp2f(sc[h] - m_new);
-        lp[h] = fmaf(lp[h], corr[h], e);
-        pr[h] = E::from_f(e);
-        m_run[h] = m_new;
-      }
-      // P (B operand, K-major: rows = heads, 64 positions per 128-byte row, two halves).
-      {
-        const int half = tid >> 6, pc = tid & 63;
-        uint8_t* pb = sh.pm + half * (kTcHeads * 128);
-#pragma unroll
-        for (int h = 0; h < kTcHeads; ++h)
-          *reinterpret_cast<raw*>(pb + sw128(h, (pc * 2) >> 4) + ((pc * 2) & 15)) = pr[h];
-      }
-      proxy_fence_shared();
-      tc_fence_before();
-      __syncthreads();
-      // O^T = V^T . P^T
-      if (tid == 0) {
-        tc_fence_after();
-        const uint32_t vb = smem_u32(st + 2 * kTcBoxBytes), pb = smem_u32(sh.pm);
-#pragma unroll
-        for (int ks = 0; ks < kTcTile / 16; ++ks) {
-          const uint64_t ad = tc_sdesc(vb + ks * 2048, kTcBoxBytes, 1024);
-          const uint64_t bd = tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
-          tc_mma(tmem + kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
-        }
-        tc_commit(&sh.o_bar);
-      }
-      if (__syncthreads_or(!mbar_wait(&sh.o_bar, mma_phase))) {
+        for (int h = 0; h < HR; ++h) sh.lsum[warp][h] = lp[h];
+      if (consumer_any(!ok)) {
         timed_out = true;
         break;
       }
-      mma_phase ^= 1u;
-      tc_fence_after();
-      float o[kTcHeads];
-      tc_ld16(tmem + tmem_lane + kTcHeads, o);
+      float L[HR];
 #pragma unroll
-      for (int h = 0; h < kTcHeads; ++h) acc[h] = fmaf(acc[h], corr[h], o[h]);
-      tc_fence_before();
-      __syncthreads();
-      ++consumed;
-      if (tid == 0) issue_next();
-    }
-    if (timed_out) break;
-
-    // ---- the unit's partial: l per head (sum over positions), then out or workspace ----
+      for (int h = 0; h < HR; ++h)
+        L[h] = (sh.lsum[0][h] + sh.lsum[1][h]) + (sh.lsum[2][h] + sh.lsum[3][h]);
+      raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+      float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
+      const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
+      const int d = tid;   // this thread's dim of O^T
+      if (nchunks == 1) {
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-      for (int h = 0; h < kTcHeads; ++h) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
-    if (lane == 0)
-#pragma unroll
-      for (int h = 0; h < kTcHeads; ++h) sh.red[warp][h] = lp[h];
-    __syncthreads();
-    float L[kTcHeads];
-#pragma unroll
-    for (int h = 0; h < kTcHeads; ++h)
-      L[h] = (sh.red[0][h] + sh.red[1][h]) + (sh.red[2][h] + sh.red[3][h]);
-    __syncthreads();   // sh.red is reused by the next unit
-    raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
-    float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
-    const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
-    const int d = tid;   // this thread's dim of O^T
-    if (nchunks == 1) {
-#pragma unroll
-      for (int h = 0; h < kTcHeads; ++h)
-        if (h < nh) out[h * int64_t{kTcDim} + d] = E::from_f(acc[h] / L[h]);
-      continue;
-    }
-#pragma unroll
-    for (int h = 0; h < kTcHeads; ++h) {
-      if (h >= nh) continue;
-      float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
-      dst[d] = acc[h];
-      if (d == 0) {
-        dst[kTcDim] = m_run[h];
-        dst[kTcDim + 1] = L[h];
+        for (int h = 0; h < HR; ++h)
+          if (h < nh) out[h * int64_t{kTcDim} + d] = E::from_f(acc[h] / L[h]);
+        continue;
       }
-    }
-    __threadfence();
-    __syncthreads();
-    int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
-    if (tid == 0) sh.last = atomicAdd(counter, 1) == nchunks - 1;
-    __syncthreads();
-    if (sh.last) {
-      __threadfence();
-      for (int h = 0; h < nh; ++h) {
-        const float* hw = ws + h * ws_head;
-        float M = -INFINITY;
-        for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(hw + c * row + kTcDim));
-        float Ls = 0.f, O = 0.f;
-        for (int c = 0; c < nchunks; ++c) {
-          const float wgt = exp2f(__ldcg(hw + c * row + kTcDim) - M);
-          Ls = fmaf(__ldcg(hw + c * row + kTcDim + 1), wgt, Ls);
-          O = fmaf(__ldcg(hw + c * row + d), wgt, O);
+#pragma unroll
+      for (int h = 0; h < HR; ++h) {
+        if (h >= nh) continue;
+        float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
+        dst[d] = acc[h];
+        if (d == 0) {
+          dst[kTcDim] = m_run[h];
+          dst[kTcDim + 1] = L[h];
         }
-        out[h * int64_t{kTcDim} + d] = E::from_f(O / Ls);
       }
-      if (tid == 0) *counter = 0;
+      // The barrier orders every consumer's partial before thread 0's fence and arrival.
+      consumer_sync();
+      int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
+      if (tid == 0) {
+        __threadfence();
+        sh.last = atomicAdd(counter, 1) == nchunks - 1;
+      }
+      consumer_sync();
+      if (sh.last) {
+        __threadfence();
+        // Merge every chunk, 32 at a time: (m, l) of the group to shared memory, then each
+        // thread folds its dim of every head with the loads of a group in flight together.
+        float M[HR], Ls[HR], O[HR];
+#pragma unroll
+        for (int h = 0; h < HR; ++h) {
+          M[h] = -INFINITY;
+          Ls[h] = 0.f;
+          O[h] = 0.f;
+        }
+        for (int cb = 0; cb < nchunks; cb += 32) {
+          const int nc = min(32, nchunks - cb);
+          for (int i = tid; i < HR * 32; i += kTcThreads) {
+            const int h = i >> 5, c = i & 31;
+            float mv = -INFINITY, lv = 0.f;
+            if (h < nh && c < nc) {
+              const float* src = ws + h * ws_head + static_cast<int64_t>(cb + c) * row + kTcDim;
+              mv = __ldcg(src);
+              lv = __ldcg(src + 1);
+            }
+            sh.mrg[0][h][c] = mv;
+            sh.mrg[1][h][c] = lv;
+          }
+          consumer_sync();
+#pragma unroll
+          for (int h = 0; h < HR; ++h) {
+            if (h >= nh) continue;
+            float mg = M[h];
+            for (int c = 0; c < nc; ++c) mg = fmaxf(mg, sh.mrg[0][h][c]);
+            const float rescale = exp2f(M[h] - mg);
+            float l_acc = Ls[h] * rescale, o_acc = O[h] * rescale;
+            const float* hw = ws + h * ws_head + static_cast<int64_t>(cb) * row + d;
+#pragma unroll 8
+            for (int c = 0; c < nc; ++c) {
+              const float wgt = exp2f(sh.mrg[0][h][c] - mg);
+              l_acc = fmaf(sh.mrg[1][h][c], wgt, l_acc);
+              o_acc = fmaf(__ldcg(hw + static_cast<int64_t>(c) * row), wgt, o_acc);
+            }
+            M[h] = mg;
+            Ls[h] = l_acc;
+            O[h] = o_acc;
+          }
+          consumer_sync();
+        }
+#pragma unroll
+        for (int h = 0; h < HR; ++h)
+          if (h < nh) out[h * int64_t{kTcDim} + d] = E::from_f(O[h] / Ls[h]);
+        if (tid == 0) *counter = 0;
+      }
+      consumer_sync();   // sh.last is reused by the next unit
     }
-    __syncthreads();   // sh.last is reused by the next unit
+    if (timed_out && tid == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
   }
 
-  if (timed_out) {
-    if (tid == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
-    // Let the copies this CTA issued land before its shared memory goes away.
-    if (tid == 0)
-      for (int64_t i = consumed; i < issued; ++i)
-        (void)mbar_wait(&sh.full[i % kTcStages], static_cast<uint32_t>((i / kTcStages) & 1));
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

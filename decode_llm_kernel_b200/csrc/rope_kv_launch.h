@@ -91,6 +91,7 @@ struct AttentionParams {
   int32_t max_chunks;    // ceil(S / chunk)
   int32_t group;         // Hq / Hkv
   int32_t nhb;           // head blocks per KV head
+  int32_t q_vec;         // tensor-core kernel: full rotary with 16-byte q rows and table rows
 };
 
 struct AttentionShape {

@@ -250,3 +250,21 @@ def test_default_scale_is_inverse_sqrt_head_dim():
     case = make_case(21, 4, 8, 8, 64, 128, torch.float32)
     got = run_gpu(case)
     check(case, got, scale=1.0 / math.sqrt(64))
+
+
+def test_tensor_core_out_of_range_position_sets_status_and_writes_nothing():
+    from decode_llm_kernel_b200 import cuda
+    o = ops()
+    cuda.read_status()
+    case = make_case(34, 3, 32, 8, 128, 300, torch.bfloat16, positions=[5, 300, 299])
+    q, k, v, p, cos, sin, kc, vc, ri = [t.cuda() for t in case]
+    kc0 = kc.clone()
+    attn = torch.full_like(q, 7.0)
+    o.fused_rope_kv_append_attention(q, k, v, p, cos, sin, kc, vc, ri, attn_out=attn,
+                                     path="tensor_cores")
+    status = cuda.read_status()
+    assert status & 1, cuda.require().status_string(status)
+    bad_row = int(case[8][1])
+    assert torch.equal(kc[bad_row].cpu(), kc0[bad_row].cpu())
+    assert torch.all(attn[1] == 7.0)
+    assert not torch.any(attn[0] == 7.0) and not torch.any(attn[2] == 7.0)
