@@ -616,7 +616,8 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
     }
     pl.chunk = (chunk + 127) / 128 * 128;
     pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);
-    pl.counter_bytes = (T * Hkv * pl.nhb * 4 + 255) / 256 * 256;
+    // Arrival counters of the units, then the persistent grid's unit counter.
+    pl.counter_bytes = ((T * Hkv * pl.nhb + 1) * 4 + 255) / 256 * 256;
     pl.partial_bytes = T * Hq * pl.max_chunks * (D + 2) * 4;
     return pl;
   }
@@ -757,6 +758,7 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
   const int index_bits_tc = positions->dtype == DRK_I32 ? 32 : 64;
   if (pl.tc) {
     const int64_t units = T * Hkv * pl.nhb * pl.max_chunks;
+    if (units > 0x7fffffffLL) throw Unsupported("fused attention: more than 2^31 work units");
     // One round of 16-byte loads for the query rotation: full rotary, aligned q rows, q_out and
     // table rows.
     const uintptr_t qa = reinterpret_cast<uintptr_t>(q->data) |

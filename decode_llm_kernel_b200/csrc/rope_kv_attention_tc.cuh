@@ -2,11 +2,15 @@
 // 16-bit caches with head_dim 128: the bandwidth form of rope_kv_attention.cuh.
 //
 // Work unit: (token t, KV head g, head block hb of up to 16 query heads, chunk of positions).
-// A persistent grid (one CTA per SM) walks units u = blockIdx.x, +gridDim.x, ... and streams
-// each unit's positions in tiles of 128 through a kTcStages-deep ring of shared-memory stages.
+// A persistent grid (one CTA per SM) takes units from a global atomic counter in the order they
+// are numbered (so the chunks and head blocks of one KV head run at about the same time) and
+// streams each unit's positions in tiles of 128 through a kTcStages-deep ring of shared-memory
+// stages. Taking units dynamically keeps the CTAs level even though the unit that holds the new
+// token, and whichever chunk arrives last and merges, do more work than the others.
 // Three roles, synchronised by mbarriers only:
-//   - warp 4, the producer, walks the CTA's sequence of tiles and refills a stage as soon as the
-//     tensor core has finished reading it (an "empty" mbarrier that tcgen05.commit arrives on
+//   - warp 4, the producer, takes the units, passes their indices to the other warps through a
+//     small queue in shared memory, and refills a stage as soon as the tensor core has finished
+//     reading it (an "empty" mbarrier that tcgen05.commit arrives on
 //     after the tile's last MMA), so the ring stays full;
 //   - warp 5 issues the MMAs (one lane) and patches the new token's row into the tile holding
 //     it, so no softmax thread ever waits on an MMA issue;
@@ -65,6 +69,9 @@ constexpr uint32_t kTcBoxBytes = kTcTile * 128;    // [128 rows][64 dims] of 2 b
 constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
 constexpr uint32_t kTcQBytes = 2 * kTcHeads * 128; // [2 dim halves][16 heads][128 B]
 constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 heads][128 B]
+// Unit queue slots. The producer is at most kTcStages tiles ahead of the MMA warp and the
+// consumers at most two tiles behind it, so at most kTcStages + 3 queued units are unread.
+constexpr int kTcQueue = 8;
 constexpr uint32_t kTcTmemCols = 64;               // S^T buffers at 0, 16; O^T at 32, 48
 
 struct TcShared {
@@ -82,6 +89,8 @@ struct TcShared {
   uint64_t o_bar[2];                               // PV done (tcgen05.commit)
   uint64_t p_bar[2];                               // P written (128 consumer arrivals)
   uint64_t q_bar;                                  // unit's Q and new K/V rows written (128)
+  int64_t uq[kTcQueue];                            // unit indices taken by the producer; -1 ends
+  uint64_t uq_bar[kTcQueue];                       // a queue slot was written (producer)
   uint32_t tmem_base;
   int last;
 };
@@ -209,25 +218,6 @@ __device__ __forceinline__ TcUnit tc_unit(const KernelParams& p, const Attention
   return w;
 }
 
-// The producer's cursor over the CTA's flat sequence of (unit, tile).
-struct TcCursor {
-  int64_t u;
-  int tile;
-  TcUnit w;
-};
-
-template <typename Idx>
-__device__ __forceinline__ bool tc_cursor_valid(const KernelParams& p, const AttentionParams& a,
-                                                int64_t units, TcCursor& c) {
-  while (c.u < units) {
-    if (c.tile < c.w.ntiles) return true;
-    c.u += gridDim.x;
-    c.tile = 0;
-    if (c.u < units) c.w = tc_unit<Idx>(p, a, c.u);
-  }
-  return false;
-}
-
 template <typename E, typename Idx, int HR>
 __global__ void __launch_bounds__(kTcBlock, 1)
 rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
@@ -259,6 +249,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       mbar_init(&sh.p_bar[b], kTcThreads);
     }
     mbar_init(&sh.q_bar, kTcThreads);
+    for (int i = 0; i < kTcQueue; ++i) mbar_init(&sh.uq_bar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // P rows of heads past HR are never written per tile: zero both buffers once.
@@ -281,28 +272,51 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   auto pair_parity = [&](int64_t c) { return static_cast<uint32_t>((c >> 1) & 1); };
 
   if (warp == kTcProducerWarp) {
-    // ---- producer (one lane): refill each stage once its last MMA has read it ----
+    // ---- producer (one lane): take units, queue them, refill each stage once its last MMA
+    //      has read it ----
     if (lane == 0) {
-      TcCursor prod{static_cast<int64_t>(blockIdx.x), 0, {}};
-      if (prod.u < units) prod.w = tc_unit<Idx>(p, a, prod.u);
-      int64_t issued = 0;
+      int* next_unit = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
+      int64_t issued = 0, queued = 0;
       bool ok = true;
-      while (tc_cursor_valid<Idx>(p, a, units, prod)) {
-        const int s = static_cast<int>(issued % kTcStages);
-        if (issued >= kTcStages)
-          ok = mbar_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
-        if (!ok) break;
-        uint8_t* st = sh.stage[s];
-        const int z = static_cast<int>(prod.w.p0 + static_cast<int64_t>(prod.tile) * kTcTile);
-        const int ri = static_cast<int>(prod.w.ri);
-        mbar_expect_tx(&sh.full[s], kTcStageBytes);
-        tma_load_4d(st, &kmap, 0, prod.w.g, z, ri, &sh.full[s]);
-        tma_load_4d(st + kTcBoxBytes, &kmap, 64, prod.w.g, z, ri, &sh.full[s]);
-        tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, prod.w.g, z, ri, &sh.full[s]);
-        tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, prod.w.g, z, ri, &sh.full[s]);
-        ++issued;
-        ++prod.tile;
+      auto enqueue = [&](int64_t u) {
+        const int slot = static_cast<int>(queued % kTcQueue);
+        sh.uq[slot] = u;
+        mbar_arrive(&sh.uq_bar[slot]);
+        ++queued;
+      };
+      while (ok) {
+        const int64_t u = atomicAdd(next_unit, 1);
+        if (u >= units) break;
+        const TcUnit w = tc_unit<Idx>(p, a, u);
+        if (w.bad) {
+          if (w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
+            uint32_t bad = 0;
+            if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
+            if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
+            if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
+            atomicOr(p.status, bad);
+          }
+          continue;
+        }
+        if (w.ntiles == 0) continue;
+        enqueue(u);
+        for (int tile = 0; tile < w.ntiles; ++tile) {
+          const int s = static_cast<int>(issued % kTcStages);
+          if (issued >= kTcStages)
+            ok = mbar_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
+          if (!ok) break;
+          uint8_t* st = sh.stage[s];
+          const int z = static_cast<int>(w.p0 + static_cast<int64_t>(tile) * kTcTile);
+          const int ri = static_cast<int>(w.ri);
+          mbar_expect_tx(&sh.full[s], kTcStageBytes);
+          tma_load_4d(st, &kmap, 0, w.g, z, ri, &sh.full[s]);
+          tma_load_4d(st + kTcBoxBytes, &kmap, 64, w.g, z, ri, &sh.full[s]);
+          tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, w.g, z, ri, &sh.full[s]);
+          tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, w.g, z, ri, &sh.full[s]);
+          ++issued;
+        }
       }
+      enqueue(-1);
       if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
       // Every copy this CTA issued lands before its shared memory goes away.
       for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i)
@@ -338,10 +352,15 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     };
     int64_t cj = 0, nunits = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const TcUnit w = tc_unit<Idx>(p, a, u);
-      if (w.bad || w.ntiles == 0) continue;
+    while (ok) {
       // Wait results are made warp-uniform so the warp never splits at a __syncwarp.
+      const int slot = static_cast<int>(nunits % kTcQueue);
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.uq_bar[slot],
+                                             static_cast<uint32_t>((nunits / kTcQueue) & 1)));
+      if (!ok) break;
+      const int64_t u = sh.uq[slot];
+      if (u < 0) break;
+      const TcUnit w = tc_unit<Idx>(p, a, u);
       ok = __all_sync(0xffffffffu, mbar_wait(&sh.q_bar, static_cast<uint32_t>(nunits & 1)));
       ++nunits;
       const bool holds_pos = w.pos < w.p1;
@@ -389,19 +408,15 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     const int half_r = p.R >> 1;
     const int row = p.D + 2;
 
-    for (int64_t u = blockIdx.x; u < units && !timed_out; u += gridDim.x) {
-      const TcUnit w = tc_unit<Idx>(p, a, u);
-      if (w.bad) {
-        if (tid == 0 && w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
-          uint32_t bad = 0;
-          if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
-          if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
-          if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
-          atomicOr(p.status, bad);
-        }
-        continue;
+    for (int64_t k = 0; !timed_out; ++k) {
+      const int slot = static_cast<int>(k % kTcQueue);
+      if (consumer_any(!mbar_wait(&sh.uq_bar[slot], static_cast<uint32_t>((k / kTcQueue) & 1)))) {
+        timed_out = true;
+        break;
       }
-      if (w.ntiles == 0) continue;
+      const int64_t u = sh.uq[slot];
+      if (u < 0) break;
+      const TcUnit w = tc_unit<Idx>(p, a, u);
       const int h0 = w.g * a.group + w.hb * kTcHeads;
       const int nh = min(HR, a.group - w.hb * kTcHeads);
       const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);

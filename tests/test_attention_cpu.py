@@ -37,25 +37,27 @@ def ws_bytes(lib, T, Hq, Hkv, D, S, dtype=torch.bfloat16, chunk=0, hpb=0, path=A
     return lib.drk_attention_workspace_bytes(T, Hq, Hkv, D, S, CODES[dtype], ctypes.byref(o), 0)
 
 
-def expected(T, Hq, Hkv, D, S, chunk, nhb):
+def expected(T, Hq, Hkv, D, S, chunk, nhb, tensor_cores=False):
+    """Arrival counters (plus the tensor-core grid's unit counter), then fp32 partials."""
     max_chunks = -(-S // chunk)
-    counters = -(-(T * Hkv * nhb * 4) // 256) * 256
+    counters = -(-((T * Hkv * nhb + (1 if tensor_cores else 0)) * 4) // 256) * 256
     return counters + T * Hq * max_chunks * (D + 2) * 4
 
 
 def test_tensor_core_workspace_rounds_chunk_to_tiles(lib):
     assert ws_bytes(lib, 4, 32, 8, 128, 1000, chunk=256, path=TENSOR_CORES) == \
-        expected(4, 32, 8, 128, 1000, 256, 1)
+        expected(4, 32, 8, 128, 1000, 256, 1, True)
     # a chunk that is not a multiple of the 128-position tile is rounded up
     assert ws_bytes(lib, 4, 32, 8, 128, 1000, chunk=200, path=TENSOR_CORES) == \
-        expected(4, 32, 8, 128, 1000, 256, 1)
+        expected(4, 32, 8, 128, 1000, 256, 1, True)
     # auto takes the tensor-core kernel for bf16 / head_dim 128
-    assert ws_bytes(lib, 4, 32, 8, 128, 1000, chunk=256) == expected(4, 32, 8, 128, 1000, 256, 1)
+    assert ws_bytes(lib, 4, 32, 8, 128, 1000, chunk=256) == \
+        expected(4, 32, 8, 128, 1000, 256, 1, True)
 
 
 def test_tensor_core_splits_large_groups_into_blocks_of_16(lib):
     assert ws_bytes(lib, 3, 71, 1, 128, 512, chunk=128, path=TENSOR_CORES) == \
-        expected(3, 71, 1, 128, 512, 128, 5)
+        expected(3, 71, 1, 128, 512, 128, 5, True)
 
 
 def test_cuda_core_workspace(lib):
