@@ -608,11 +608,12 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
     int64_t chunk = ao.chunk;
     if (chunk < 0) invalid("chunk must be >= 0, got ", chunk);
     if (chunk == 0) {
-      // Enough units for about four per SM, so the static walk balances; at most 4096.
+      // The grid takes units dynamically, so about two units per SM keep it busy; longer
+      // chunks mean fewer cross-chunk merges. At least 512 positions (four tiles) per unit.
       const int64_t heads = std::max<int64_t>(1, T * Hkv * pl.nhb);
-      const int64_t target = 4LL * drk::device_sm_count(device);
-      chunk = 128;
-      while (chunk < 4096 && heads * ((S + 2 * chunk - 1) / (2 * chunk)) >= target) chunk <<= 1;
+      const int64_t target = 2LL * drk::device_sm_count(device);
+      chunk = 512;
+      while (chunk < S && heads * ((S + 2 * chunk - 1) / (2 * chunk)) >= target) chunk <<= 1;
     }
     pl.chunk = (chunk + 127) / 128 * 128;
     pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);

@@ -7,22 +7,29 @@
 // streams each unit's positions in tiles of 128 through a kTcStages-deep ring of shared-memory
 // stages. Taking units dynamically keeps the CTAs level even though the unit that holds the new
 // token, and whichever chunk arrives last and merges, do more work than the others.
-// Three roles, synchronised by mbarriers only:
+// Six roles, synchronised by mbarriers only:
 //   - warp 4, the producer, takes the units, passes their indices to the other warps through a
 //     small queue in shared memory, and refills a stage as soon as the tensor core has finished
-//     reading it (an "empty" mbarrier that tcgen05.commit arrives on
-//     after the tile's last MMA), so the ring stays full;
-//   - warp 5 issues the MMAs (one lane) and patches the new token's row into the tile holding
-//     it, so no softmax thread ever waits on an MMA issue;
-//   - warps 0-3 (the 128 TMEM lanes) run the softmax, the output correction and the chunk
-//     merge, synchronising among themselves with a named barrier.
+//     reading it (an "empty" mbarrier that tcgen05.commit arrives on after the tile's last MMA),
+//     so the ring stays full;
+//   - warp 6 prepares each unit ahead of the tensor core: the rotated queries (into one of two
+//     Q buffers), the new token's rotated K and raw V row, the cache-slot append and q_out;
+//   - warp 5 issues the QK products (one lane) and patches the new token's row into the tile
+//     holding it; warp 8 issues the PV products. Each tcgen05.mma blocks its issuing thread for
+//     about as long as the tensor pipe takes to run it, so two issuers keep the pipe fed while
+//     the other waits on a barrier;
+//   - warps 0-3 (the 128 TMEM lanes) run the softmax and the output correction, and hand each
+//     unit's accumulators to warp 7 through shared memory;
+//   - warp 7 writes the unit's output, or its partial, and merges a split KV head's chunks when
+//     it sees the last of them arrive.
+// So the softmax warps never wait on an MMA issue, a query rotation or a merge.
 // Per tile:
 //   1. TMA (cp.async.bulk.tensor, 128-byte swizzle) brings K[128 positions][128 dims] and V of
 //      the same rows, as two 64-dim boxes each (64 KB), completing on the stage's mbarrier;
 //   2. one thread issues S^T = K_tile . Q^T on the tensor cores (M = 128 positions, N = 16
 //      heads, K = 128 dims: 8 tcgen05.mma of K = 16; A = K tile, K-major; B = the unit's
 //      rotated queries, K-major) into a TMEM accumulator;
-//   3. each thread reads its position's scores from TMEM (thread = TMEM lane = position),
+//   3. each softmax thread reads its position's scores from TMEM (thread = TMEM lane = position),
 //      scales them, masks positions past the unit's end, takes the per-head tile maximum across
 //      the consumers, and writes p = 2^(s - m) to shared memory in the storage type (the B
 //      operand of the next product, K-major); per-thread partial row sums stay in registers;
@@ -30,8 +37,10 @@
 //      V tile read MN-major, B = P) into a second TMEM accumulator;
 //   5. each thread (= one dim) reads its head values and folds them into its fp32 accumulator
 //      with the online-softmax correction.
-// S^T, O^T and P are double-buffered: the next tile's QK is issued with this tile's PV, and this
-// tile's O^T is read after the next tile's softmax. Only the HR real heads of a unit (the group
+// S^T is triple-buffered and O^T and P double-buffered: QKs run up to two tiles ahead of the
+// softmax, and a tile's O^T is read after the next tile's softmax. Each tcgen05.mma of these shapes occupies
+// the tensor pipe for a fixed ~85 cycles whatever N is, so the pipe, not the math, sets the
+// floor of ~16 x 85 cycles per 128-position tile. Only the HR real heads of a unit (the group
 // size rounded up to a power of two, at most 16) go through the softmax; the MMA always runs
 // N = 16 with zero query rows.
 // At a unit's end the partial (acc, m, l) per head goes to the workspace; the last chunk of a
@@ -60,7 +69,10 @@ namespace drk {
 constexpr int kTcThreads = 128;                    // consumers: warps 0-3
 constexpr int kTcProducerWarp = 4;
 constexpr int kTcMmaWarp = 5;
-constexpr int kTcBlock = kTcThreads + 64;          // + the producer and MMA warps
+constexpr int kTcPrepWarp = 6;
+constexpr int kTcEpilogueWarp = 7;
+constexpr int kTcPvWarp = 8;
+constexpr int kTcBlock = kTcThreads + 160;         // + producer, QK, prep, epilogue, PV warps
 constexpr int kTcTile = 128;                       // positions per tile (MMA M of S^T)
 constexpr int kTcHeads = 16;                       // query heads per unit (MMA N)
 constexpr int kTcDim = 128;                        // head_dim
@@ -69,30 +81,40 @@ constexpr uint32_t kTcBoxBytes = kTcTile * 128;    // [128 rows][64 dims] of 2 b
 constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
 constexpr uint32_t kTcQBytes = 2 * kTcHeads * 128; // [2 dim halves][16 heads][128 B]
 constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 heads][128 B]
-// Unit queue slots. The producer is at most kTcStages tiles ahead of the MMA warp and the
-// consumers at most two tiles behind it, so at most kTcStages + 3 queued units are unread.
-constexpr int kTcQueue = 8;
-constexpr uint32_t kTcTmemCols = 64;               // S^T buffers at 0, 16; O^T at 32, 48
+// Unit queue slots. The producer is at most kTcStages tiles ahead of the MMA warp, the prep
+// warp at most two units ahead of it (two Q buffers), the consumers at most two tiles behind it
+// and the epilogue warp at most one unit behind the consumers, so fewer than 8 queued units are
+// ever unread.
+constexpr int kTcQueue = 16;
+constexpr int kTcSBufs = 3;                        // S^T accumulators in flight
+constexpr uint32_t kTcOCol = kTcSBufs * 16;        // first O^T column
+constexpr uint32_t kTcTmemCols = 128;              // S^T at 0, 16, 32; O^T at 48, 64
 
 struct TcShared {
   uint8_t stage[kTcStages][kTcStageBytes];         // K lo, K hi, V lo, V hi boxes
-  uint8_t q[kTcQBytes];
+  uint8_t q[2][kTcQBytes];                         // Q^T operand, double-buffered across units
   uint8_t pm[2][kTcPBytes];                        // P, double-buffered across tiles
+  float ep_acc[kTcHeads][kTcDim];                  // a unit's O accumulators for the epilogue
+  float ep_m[kTcHeads];
+  float ep_l[kTcHeads];
   float red[2][kTcThreads / 32][kTcHeads];         // per-warp tile maxima, double-buffered
   float lsum[kTcThreads / 32][kTcHeads];           // per-warp row sums at a unit's end
-  float mrg[2][kTcHeads][32];                      // merge: (m, l) of up to 32 chunks per head
-  uint4 kn[16];                                    // the new token's K row (storage type)
-  uint4 vn[16];
+  uint4 kn[2][16];                                 // the new token's K row (storage type)
+  uint4 vn[2][16];
   uint64_t full[kTcStages];
   uint64_t empty[kTcStages];
-  uint64_t s_bar[2];                               // QK done (tcgen05.commit)
+  uint64_t s_bar[kTcSBufs];                        // QK done (tcgen05.commit)
+  uint64_t s_free[kTcSBufs];                       // S^T read by the softmax (128 arrivals)
   uint64_t o_bar[2];                               // PV done (tcgen05.commit)
   uint64_t p_bar[2];                               // P written (128 consumer arrivals)
-  uint64_t q_bar;                                  // unit's Q and new K/V rows written (128)
-  int64_t uq[kTcQueue];                            // unit indices taken by the producer; -1 ends
+  uint64_t q_full[2];                              // a unit's Q and new K/V row are ready (prep)
+  uint64_t q_free[2];                              // its last QK has completed (tcgen05.commit)
+  uint64_t ep_full;                                // accumulators handed over (128 arrivals)
+  uint64_t ep_empty;                               // the epilogue has read them
+  int64_t uq[kTcQueue][3];                         // (unit, position, request) taken by the
+                                                   // producer; unit -1 ends the walk
   uint64_t uq_bar[kTcQueue];                       // a queue slot was written (producer)
   uint32_t tmem_base;
-  int last;
 };
 constexpr size_t kTcSmemBytes = sizeof(TcShared) + 1024;   // + alignment slack
 
@@ -135,6 +157,20 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 __device__ __forceinline__ void proxy_fence_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// mbar_wait with a non-blocking first look: a phase that has already completed costs one
+// test_wait instead of a try_wait round. Bounded like mbar_wait.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0 || mbar_wait(bar, parity);
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -198,9 +234,9 @@ struct TcUnit {
   bool bad;            // invalid position or request index
 };
 
-template <typename Idx>
-__device__ __forceinline__ TcUnit tc_unit(const KernelParams& p, const AttentionParams& a,
-                                          int64_t u) {
+// A unit from its index and its token's position and request index.
+__device__ __forceinline__ TcUnit tc_unit_at(const KernelParams& p, const AttentionParams& a,
+                                             int64_t u, int64_t pos, int64_t ri) {
   TcUnit w;
   const int64_t per_token_head = static_cast<int64_t>(a.max_chunks) * a.nhb;
   const int64_t tg = u / per_token_head;
@@ -209,13 +245,21 @@ __device__ __forceinline__ TcUnit tc_unit(const KernelParams& p, const Attention
   w.hb = static_cast<int>(rest - static_cast<int64_t>(w.chunk) * a.nhb);
   w.t = tg / p.Hkv;
   w.g = static_cast<int>(tg - w.t * p.Hkv);
-  w.pos = load_index<Idx>(p.positions, w.t);
-  w.ri = load_index<Idx>(p.request_indices, w.t);
+  w.pos = pos;
+  w.ri = ri;
   w.bad = w.pos < 0 || w.pos >= p.S || w.pos >= p.table_rows || w.ri < 0 || w.ri >= p.B;
   w.p0 = static_cast<int64_t>(w.chunk) * a.chunk;
   w.p1 = w.bad ? w.p0 : min(w.pos + 1, w.p0 + a.chunk);
   w.ntiles = w.p1 > w.p0 ? static_cast<int>((w.p1 - w.p0 + kTcTile - 1) / kTcTile) : 0;
   return w;
+}
+
+template <typename Idx>
+__device__ __forceinline__ TcUnit tc_unit(const KernelParams& p, const AttentionParams& a,
+                                          int64_t u) {
+  const int64_t t = u / (static_cast<int64_t>(a.max_chunks) * a.nhb * p.Hkv);
+  return tc_unit_at(p, a, u, load_index<Idx>(p.positions, t),
+                    load_index<Idx>(p.request_indices, t));
 }
 
 template <typename E, typename Idx, int HR>
@@ -243,12 +287,18 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTcSBufs; ++b) {
       mbar_init(&sh.s_bar[b], 1);
+      mbar_init(&sh.s_free[b], kTcThreads);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&sh.o_bar[b], 1);
       mbar_init(&sh.p_bar[b], kTcThreads);
+      mbar_init(&sh.q_full[b], 1);
+      mbar_init(&sh.q_free[b], 1);
     }
-    mbar_init(&sh.q_bar, kTcThreads);
+    mbar_init(&sh.ep_full, kTcThreads);
+    mbar_init(&sh.ep_empty, 1);
     for (int i = 0; i < kTcQueue; ++i) mbar_init(&sh.uq_bar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -270,6 +320,14 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   auto stage_of = [&](int64_t c) { return sh.stage[static_cast<int>(c % kTcStages)]; };
   auto full_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kTcStages) & 1); };
   auto pair_parity = [&](int64_t c) { return static_cast<uint32_t>((c >> 1) & 1); };
+  auto sbuf = [&](int64_t c) { return static_cast<int>(c % kTcSBufs); };
+  auto s_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kTcSBufs) & 1); };
+  // The k-th queued unit index (all lanes of the calling warp poll; -1 ends the walk).
+  auto queue_wait = [&](int64_t k) {
+    return tc_wait(&sh.uq_bar[k % kTcQueue], static_cast<uint32_t>((k / kTcQueue) & 1));
+  };
+  const int half_r = p.R >> 1;
+  const int row = p.D + 2;
 
   if (warp == kTcProducerWarp) {
     // ---- producer (one lane): take units, queue them, refill each stage once its last MMA
@@ -278,9 +336,11 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       int* next_unit = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
       int64_t issued = 0, queued = 0;
       bool ok = true;
-      auto enqueue = [&](int64_t u) {
+      auto enqueue = [&](int64_t u, int64_t pos, int64_t ri) {
         const int slot = static_cast<int>(queued % kTcQueue);
-        sh.uq[slot] = u;
+        sh.uq[slot][0] = u;
+        sh.uq[slot][1] = pos;
+        sh.uq[slot][2] = ri;
         mbar_arrive(&sh.uq_bar[slot]);
         ++queued;
       };
@@ -299,11 +359,11 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           continue;
         }
         if (w.ntiles == 0) continue;
-        enqueue(u);
+        enqueue(u, w.pos, w.ri);
         for (int tile = 0; tile < w.ntiles; ++tile) {
           const int s = static_cast<int>(issued % kTcStages);
           if (issued >= kTcStages)
-            ok = mbar_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
+            ok = tc_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
           if (!ok) break;
           uint8_t* st = sh.stage[s];
           const int z = static_cast<int>(w.p0 + static_cast<int64_t>(tile) * kTcTile);
@@ -316,157 +376,79 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           ++issued;
         }
       }
-      enqueue(-1);
+      enqueue(-1, 0, 0);
       if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
       // Every copy this CTA issued lands before its shared memory goes away.
       for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i)
         (void)mbar_wait(&sh.full[i % kTcStages], static_cast<uint32_t>((i / kTcStages) & 1));
     }
-  } else if (warp == kTcMmaWarp) {
-    // ---- MMA issuer: per tile c, S^T(c) = K . Q^T once its data has landed, then
-    //      O^T(c - 1) = V^T . P^T(c - 1) once the consumers have written P(c - 1) ----
-    auto issue_qk = [&](const uint8_t* st, int b) {
-      const uint32_t kb = smem_u32(st), qb = smem_u32(sh.q);
-#pragma unroll
-      for (int ks = 0; ks < kTcDim / 16; ++ks) {
-        const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
-        const uint64_t ad = tc_sdesc(kb + (ks >> 2) * kTcBoxBytes + off, 16, 1024);
-        const uint64_t bd = tc_sdesc(qb + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
-        tc_mma(tmem + b * kTcHeads, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
-      }
-      tc_commit(&sh.s_bar[b]);
-    };
-    auto issue_pv = [&](int64_t c) {
-      const int b = static_cast<int>(c & 1);
-      const uint8_t* st = stage_of(c);
-      const uint32_t vb = smem_u32(st + 2 * kTcBoxBytes), pb = smem_u32(sh.pm[b]);
-#pragma unroll
-      for (int ks = 0; ks < kTcTile / 16; ++ks) {
-        const uint64_t ad = tc_sdesc(vb + ks * 2048, kTcBoxBytes, 1024);
-        const uint64_t bd =
-            tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
-        tc_mma(tmem + 2 * kTcHeads + b * kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
-      }
-      tc_commit(&sh.o_bar[b]);
-      tc_commit(&sh.empty[static_cast<int>(c % kTcStages)]);
-    };
-    int64_t cj = 0, nunits = 0;
+  } else if (warp == kTcPrepWarp) {
+    // ---- prep: the unit's rotated queries (Q^T operand, K-major, 128-byte swizzle) and the
+    //      new token's K/V row, into buffer k % 2 once the QKs of unit k - 2 have completed;
+    //      the cache-slot append (head block 0) and q_out (chunk 0) ----
     bool ok = true;
-    while (ok) {
-      // Wait results are made warp-uniform so the warp never splits at a __syncwarp.
-      const int slot = static_cast<int>(nunits % kTcQueue);
-      ok = __all_sync(0xffffffffu, mbar_wait(&sh.uq_bar[slot],
-                                             static_cast<uint32_t>((nunits / kTcQueue) & 1)));
+    for (int64_t k = 0; ok; ++k) {
+      ok = __all_sync(0xffffffffu, queue_wait(k));
       if (!ok) break;
-      const int64_t u = sh.uq[slot];
-      if (u < 0) break;
-      const TcUnit w = tc_unit<Idx>(p, a, u);
-      ok = __all_sync(0xffffffffu, mbar_wait(&sh.q_bar, static_cast<uint32_t>(nunits & 1)));
-      ++nunits;
-      const bool holds_pos = w.pos < w.p1;
-      for (int j = 0; j <= w.ntiles && ok; ++j) {
-        const int64_t c = cj + j;
-        if (j < w.ntiles) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&sh.full[c % kTcStages], full_parity(c)));
-          if (!ok) break;
-          const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
-          if (holds_pos && w.pos >= tp0 && w.pos < tp0 + kTcTile) {
-            // The new token's K and V row, 16 chunks each, into the staged tile.
-            const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
-            const int ch = lane & 15;
-            const bool is_v = lane >= 16;
-            uint8_t* base = stage_of(c) + (is_v ? 2 : 0) * kTcBoxBytes + (ch >> 3) * kTcBoxBytes;
-            *reinterpret_cast<uint4*>(base + sw128(r, ch & 7)) = is_v ? sh.vn[ch] : sh.kn[ch];
-            proxy_fence_shared();
-          }
-          __syncwarp();
-          if (lane == 0) {
-            tc_fence_after();
-            issue_qk(stage_of(c), static_cast<int>(c & 1));
-          }
-          __syncwarp();
-        }
-        if (j >= 1) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&sh.p_bar[(c - 1) & 1], pair_parity(c - 1)));
-          if (!ok) break;
-          if (lane == 0) {
-            tc_fence_after();
-            issue_pv(c - 1);
-          }
-          __syncwarp();
-        }
+      const int64_t* msg = sh.uq[k % kTcQueue];
+      if (msg[0] < 0) break;
+      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+      const int qb = static_cast<int>(k & 1);
+      if (k >= 2) {
+        ok = __all_sync(0xffffffffu, tc_wait(&sh.q_free[qb],
+                                             static_cast<uint32_t>(((k >> 1) - 1) & 1)));
+        if (!ok) break;
       }
-      cj += w.ntiles;
-    }
-    if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
-  } else {
-    // ---- consumers (warps 0-3): softmax, output correction, chunk merge ----
-    const uint32_t tmem_lane = static_cast<uint32_t>(warp * 32) << 16;
-    int64_t cj = 0;                // tiles of the walk consumed so far
-    bool timed_out = false;
-    const float scale = a.scale_log2;
-    const int half_r = p.R >> 1;
-    const int row = p.D + 2;
-
-    for (int64_t k = 0; !timed_out; ++k) {
-      const int slot = static_cast<int>(k % kTcQueue);
-      if (consumer_any(!mbar_wait(&sh.uq_bar[slot], static_cast<uint32_t>((k / kTcQueue) & 1)))) {
-        timed_out = true;
-        break;
-      }
-      const int64_t u = sh.uq[slot];
-      if (u < 0) break;
-      const TcUnit w = tc_unit<Idx>(p, a, u);
       const int h0 = w.g * a.group + w.hb * kTcHeads;
       const int nh = min(HR, a.group - w.hb * kTcHeads);
-      const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
       const float* crow = p.cos_t + w.pos * p.table_stride;
       const float* srow = p.sin_t + w.pos * p.table_stride;
-
-      // ---- the unit's rotated queries -> Q^T operand (K-major, 128-byte swizzle). Every QK
-      //      of the previous unit has completed: its last S^T was read below. ----
+      uint8_t* qs = sh.q[qb];
       if (a.q_vec) {
-        // Full rotary, 16-byte rows: thread = (head, 8-dim chunk of the first half); one round
-        // of loads, both halves of the rotate_half pair from one thread.
-        const int hh = tid >> 3, c = tid & 7;
-        uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-        if (hh < nh) {
-          const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
-                            static_cast<int64_t>(h0 + hh) * p.q_hs;
-          const uint4 x1 = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-          const uint4 x2 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
-          const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
-          const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
-          const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
-          const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
-          const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-          float f1[8], f2[8];
-          unpack16<E>(x1, f1);
-          unpack16<E>(x2, f2);
-          uint32_t wl[4], wh[4];
+        // Full rotary, 16-byte rows: item = (head, 8-dim chunk of the first half); both halves
+        // of the rotate_half pair from one lane.
+        for (int item = lane; item < kTcHeads * 8; item += 32) {
+          const int hh = item >> 3, c = item & 7;
+          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+          if (hh < nh) {
+            const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
+                              static_cast<int64_t>(h0 + hh) * p.q_hs;
+            const uint4 x1 = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+            const uint4 x2 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
+            const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
+            const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
+            const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            float f1[8], f2[8];
+            unpack16<E>(x1, f1);
+            unpack16<E>(x2, f2);
+            uint32_t wl[4], wh[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int e0 = 2 * i, e1 = 2 * i + 1;
-            const raw a0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], true));
-            const raw a1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], true));
-            const raw b0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], false));
-            const raw b1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], false));
-            wl[i] = static_cast<uint32_t>(a0) | (static_cast<uint32_t>(a1) << 16);
-            wh[i] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
+            for (int i = 0; i < 4; ++i) {
+              const int e0 = 2 * i, e1 = 2 * i + 1;
+              const raw a0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], true));
+              const raw a1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], true));
+              const raw b0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], false));
+              const raw b1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], false));
+              wl[i] = static_cast<uint32_t>(a0) | (static_cast<uint32_t>(a1) << 16);
+              wh[i] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
+            }
+            lo = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+            hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+            if (a.q_out != nullptr && w.chunk == 0) {
+              raw* qo =
+                  reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+              *reinterpret_cast<uint4*>(qo + 8 * c) = lo;
+              *reinterpret_cast<uint4*>(qo + 64 + 8 * c) = hi;
+            }
           }
-          lo = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-          hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-          if (a.q_out != nullptr && w.chunk == 0) {
-            raw* qo = reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
-            *reinterpret_cast<uint4*>(qo + 8 * c) = lo;
-            *reinterpret_cast<uint4*>(qo + 64 + 8 * c) = hi;
-          }
+          *reinterpret_cast<uint4*>(qs + sw128(hh, c)) = lo;
+          *reinterpret_cast<uint4*>(qs + kTcHeads * 128 + sw128(hh, c)) = hi;
         }
-        *reinterpret_cast<uint4*>(sh.q + sw128(hh, c)) = lo;
-        *reinterpret_cast<uint4*>(sh.q + kTcHeads * 128 + sw128(hh, c)) = hi;
       } else {
-        for (int idx = tid; idx < kTcHeads * (kTcDim / 2); idx += kTcThreads) {
+        for (int idx = lane; idx < kTcHeads * (kTcDim / 2); idx += 32) {
           const int hh = idx / (kTcDim / 2);
           const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
           raw y0 = 0, y1 = 0;
@@ -495,21 +477,18 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             }
           }
           const int box = d >> 6, db = (d & 63) * 2;     // byte within the 128-byte row
-          uint8_t* dst = sh.q + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
+          uint8_t* dst = qs + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
           *reinterpret_cast<uint32_t*>(dst) =
               static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16);
         }
       }
-      // ---- the new token's K/V rows (patched into its tile by the MMA warp); head block 0
-      //      appends them to the cache ----
-      const bool holds_pos = w.pos < w.p1;
-      if (holds_pos) {
+      if (w.pos < w.p1) {
         const raw* krow = reinterpret_cast<const raw*>(p.k) + w.t * p.k_ts + w.g * p.k_hs;
         const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
-        raw* kn = reinterpret_cast<raw*>(sh.kn);
-        raw* vn = reinterpret_cast<raw*>(sh.vn);
+        raw* kn = reinterpret_cast<raw*>(sh.kn[qb]);
+        raw* vn = reinterpret_cast<raw*>(sh.vn[qb]);
         const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
-        for (int d = tid; d < kTcDim; d += kTcThreads) {
+        for (int d = lane; d < kTcDim; d += 32) {
           raw kr = krow[d];
           if (d < p.R) {
             const int i = d < half_r ? d : d - half_r;
@@ -526,7 +505,201 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         }
       }
       proxy_fence_shared();
-      mbar_arrive(&sh.q_bar);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.q_full[qb]);
+    }
+    if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+  } else if (warp == kTcMmaWarp) {
+    // ---- QK issuer: S^T(c) = K . Q^T once tile c has landed and the softmax has read the
+    //      S^T buffer's previous tile (c - 3); the tile is patched first if it holds pos ----
+    int64_t cj = 0;
+    bool ok = true;
+    for (int64_t k = 0; ok; ++k) {
+      // Wait results are made warp-uniform so the warp never splits at a __syncwarp.
+      ok = __all_sync(0xffffffffu, queue_wait(k));
+      if (!ok) break;
+      const int64_t* msg = sh.uq[k % kTcQueue];
+      if (msg[0] < 0) break;
+      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+      const int qb = static_cast<int>(k & 1);
+      ok = __all_sync(0xffffffffu, tc_wait(&sh.q_full[qb], static_cast<uint32_t>((k >> 1) & 1)));
+      if (!ok) break;
+      const bool holds_pos = w.pos < w.p1;
+      const uint32_t qaddr = smem_u32(sh.q[qb]);
+      for (int j = 0; j < w.ntiles; ++j) {
+        const int64_t c = cj + j;
+        const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
+        const bool patch_tile = holds_pos && w.pos >= tp0 && w.pos < tp0 + kTcTile;
+        // Lane 0 alone polls unless every lane is about to write into the tile.
+        bool mine = true;
+        if (lane == 0 && c >= kTcSBufs)
+          mine = tc_wait(&sh.s_free[sbuf(c)], static_cast<uint32_t>(((c / kTcSBufs) - 1) & 1));
+        if (mine && (patch_tile || lane == 0))
+          mine = tc_wait(&sh.full[c % kTcStages], full_parity(c));
+        ok = __all_sync(0xffffffffu, mine);
+        if (!ok) break;
+        if (patch_tile) {
+          // The new token's K and V row, 16 chunks each, into the staged tile.
+          const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
+          const int ch = lane & 15;
+          const bool is_v = lane >= 16;
+          uint8_t* base = stage_of(c) + (is_v ? 2 : 0) * kTcBoxBytes + (ch >> 3) * kTcBoxBytes;
+          *reinterpret_cast<uint4*>(base + sw128(r, ch & 7)) =
+              is_v ? sh.vn[qb][ch] : sh.kn[qb][ch];
+          proxy_fence_shared();
+          __syncwarp();
+        }
+        if (lane == 0) {
+          tc_fence_after();
+          const int b = sbuf(c);
+          const uint32_t kb = smem_u32(stage_of(c));
+#pragma unroll
+          for (int ks = 0; ks < kTcDim / 16; ++ks) {
+            const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
+            const uint64_t ad = tc_sdesc(kb + (ks >> 2) * kTcBoxBytes + off, 16, 1024);
+            const uint64_t bd = tc_sdesc(qaddr + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
+            tc_mma(tmem + b * kTcHeads, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(&sh.s_bar[b]);
+          // After the unit's last QK, the prep warp may refill this Q buffer.
+          if (j + 1 == w.ntiles) tc_commit(&sh.q_free[qb]);
+        }
+        __syncwarp();
+      }
+      cj += w.ntiles;
+    }
+    if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+  } else if (warp == kTcPvWarp) {
+    // ---- PV issuer: O^T(c) = V^T . P^T(c) once the softmax has written P(c); its completion
+    //      frees tile c's stage (QK(c) completed before the softmax could write P(c)) ----
+    if (lane == 0) {
+      int64_t c = 0;
+      bool ok = true;
+      for (int64_t k = 0; ok; ++k) {
+        ok = queue_wait(k);
+        if (!ok) break;
+        const int64_t* msg = sh.uq[k % kTcQueue];
+        if (msg[0] < 0) break;
+        const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+        for (int j = 0; j < w.ntiles; ++j, ++c) {
+          ok = tc_wait(&sh.p_bar[c & 1], pair_parity(c));
+          if (!ok) break;
+          tc_fence_after();
+          const int b = static_cast<int>(c & 1);
+          const uint32_t vb = smem_u32(stage_of(c) + 2 * kTcBoxBytes), pb = smem_u32(sh.pm[b]);
+#pragma unroll
+          for (int ks = 0; ks < kTcTile / 16; ++ks) {
+            const uint64_t ad = tc_sdesc(vb + ks * 2048, kTcBoxBytes, 1024);
+            const uint64_t bd =
+                tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
+            tc_mma(tmem + kTcOCol + b * kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(&sh.o_bar[b]);
+          tc_commit(&sh.empty[static_cast<int>(c % kTcStages)]);
+        }
+      }
+      if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+    }
+  } else if (warp == kTcEpilogueWarp) {
+    // ---- epilogue: a unit's output, or its partial and the cross-chunk merge ----
+    bool ok = true;
+    for (int64_t k = 0; ok; ++k) {
+      ok = __all_sync(0xffffffffu, queue_wait(k));
+      if (!ok) break;
+      const int64_t* msg = sh.uq[k % kTcQueue];
+      if (msg[0] < 0) break;
+      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+      ok = __all_sync(0xffffffffu, tc_wait(&sh.ep_full, static_cast<uint32_t>(k & 1)));
+      if (!ok) break;
+      const int h0 = w.g * a.group + w.hb * kTcHeads;
+      const int nh = min(HR, a.group - w.hb * kTcHeads);
+      const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
+      float acc[HR][4], mh[HR], lh[HR];
+#pragma unroll
+      for (int h = 0; h < HR; ++h) {
+        mh[h] = sh.ep_m[h];
+        lh[h] = sh.ep_l[h];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[h][i] = sh.ep_acc[h][lane + 32 * i];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.ep_empty);   // the softmax warps may refill the buffer
+      raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+      if (nchunks == 1) {
+#pragma unroll
+        for (int h = 0; h < HR; ++h)
+          if (h < nh)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(acc[h][i] / lh[h]);
+        continue;
+      }
+      float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
+      const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
+#pragma unroll
+      for (int h = 0; h < HR; ++h) {
+        if (h >= nh) continue;
+        float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = acc[h][i];
+        if (lane == 0) {
+          dst[kTcDim] = mh[h];
+          dst[kTcDim + 1] = lh[h];
+        }
+      }
+      __syncwarp();
+      int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(counter, 1) == nchunks - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      for (int h = 0; h < nh; ++h) {
+        const float* hw = ws + h * ws_head;
+        float M = -INFINITY;
+        for (int c = lane; c < nchunks; c += 32) M = fmaxf(M, __ldcg(hw + c * row + kTcDim));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+          M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int c = lane; c < nchunks; c += 32)
+          L = fmaf(__ldcg(hw + c * row + kTcDim + 1), exp2f(__ldcg(hw + c * row + kTcDim) - M), L);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        float O[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int c = 0; c < nchunks; ++c) {
+          const float* cb = hw + static_cast<int64_t>(c) * row;
+          const float wgt = exp2f(__ldcg(cb + kTcDim) - M);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cb + lane + 32 * i), wgt, O[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / L);
+      }
+      if (lane == 0) *counter = 0;
+    }
+    if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
+  } else {
+    // ---- softmax warps (0-3): scores, P, output correction; hand the unit to the epilogue ----
+    const uint32_t tmem_lane = static_cast<uint32_t>(warp * 32) << 16;
+    int64_t cj = 0;                // tiles of the walk consumed so far
+    bool timed_out = false;
+    const float scale = a.scale_log2;
+
+    for (int64_t k = 0; !timed_out; ++k) {
+      if (consumer_any(!queue_wait(k))) {
+        timed_out = true;
+        break;
+      }
+      const int64_t* msg = sh.uq[k % kTcQueue];
+      if (msg[0] < 0) break;
+      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+      const int nh = min(HR, a.group - w.hb * kTcHeads);
 
       float m_run[HR], lp[HR], acc[HR], corr_prev[HR];
 #pragma unroll
@@ -540,10 +713,12 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       for (int j = 0; j < w.ntiles; ++j) {
         const int64_t c = cj + j;
         const int b = static_cast<int>(c & 1);
-        ok = mbar_wait(&sh.s_bar[b], pair_parity(c)) && ok;
+        ok = tc_wait(&sh.s_bar[sbuf(c)], s_parity(c)) && ok;
         tc_fence_after();
         float sc[kTcHeads];
-        tc_ld16(tmem + tmem_lane + b * kTcHeads, sc);
+        tc_ld16(tmem + tmem_lane + sbuf(c) * kTcHeads, sc);
+        tc_fence_before();
+        mbar_arrive(&sh.s_free[sbuf(c)]);   // the QK issuer may reuse this S^T buffer
         const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
         const bool live = tp0 + tid < w.p1;
         float mx[HR];
@@ -582,16 +757,16 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
                 E::from_f(e);
           }
         }
-        // P(c) is ready, and this thread is done with S^T(c) and O^T(c - 2).
+        // P(c) is ready, and this thread is done with O^T(c - 2).
         proxy_fence_shared();
         tc_fence_before();
         mbar_arrive(&sh.p_bar[b]);
         if (j >= 1) {
           // The previous tile's O^T: its PV ran while this tile's softmax did.
-          ok = mbar_wait(&sh.o_bar[b ^ 1], pair_parity(c - 1)) && ok;
+          ok = tc_wait(&sh.o_bar[b ^ 1], pair_parity(c - 1)) && ok;
           tc_fence_after();
           float o[kTcHeads];
-          tc_ld16(tmem + tmem_lane + 2 * kTcHeads + (b ^ 1) * kTcHeads, o);
+          tc_ld16(tmem + tmem_lane + kTcOCol + (b ^ 1) * kTcHeads, o);
 #pragma unroll
           for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
         }
@@ -601,17 +776,17 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       if (timed_out) break;
       {
         const int64_t c = cj + w.ntiles - 1;
-        ok = mbar_wait(&sh.o_bar[c & 1], pair_parity(c)) && ok;
+        ok = tc_wait(&sh.o_bar[c & 1], pair_parity(c)) && ok;
         tc_fence_after();
         float o[kTcHeads];
-        tc_ld16(tmem + tmem_lane + 2 * kTcHeads + static_cast<int>(c & 1) * kTcHeads, o);
+        tc_ld16(tmem + tmem_lane + kTcOCol + static_cast<int>(c & 1) * kTcHeads, o);
 #pragma unroll
         for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
         tc_fence_before();
       }
       cj += w.ntiles;
 
-      // ---- the unit's partial: l per head (sum over positions), then out or workspace ----
+      // ---- row sums per head, then the hand-over to the epilogue warp ----
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
@@ -619,93 +794,20 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       if (lane == 0)
 #pragma unroll
         for (int h = 0; h < HR; ++h) sh.lsum[warp][h] = lp[h];
+      if (k >= 1) ok = tc_wait(&sh.ep_empty, static_cast<uint32_t>((k - 1) & 1)) && ok;
       if (consumer_any(!ok)) {
         timed_out = true;
         break;
       }
-      float L[HR];
-#pragma unroll
-      for (int h = 0; h < HR; ++h)
-        L[h] = (sh.lsum[0][h] + sh.lsum[1][h]) + (sh.lsum[2][h] + sh.lsum[3][h]);
-      raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
-      float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
-      const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
-      const int d = tid;   // this thread's dim of O^T
-      if (nchunks == 1) {
-#pragma unroll
-        for (int h = 0; h < HR; ++h)
-          if (h < nh) out[h * int64_t{kTcDim} + d] = E::from_f(acc[h] / L[h]);
-        continue;
-      }
 #pragma unroll
       for (int h = 0; h < HR; ++h) {
-        if (h >= nh) continue;
-        float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
-        dst[d] = acc[h];
-        if (d == 0) {
-          dst[kTcDim] = m_run[h];
-          dst[kTcDim + 1] = L[h];
+        sh.ep_acc[h][tid] = acc[h];
+        if (tid == 0) {
+          sh.ep_m[h] = m_run[h];
+          sh.ep_l[h] = (sh.lsum[0][h] + sh.lsum[1][h]) + (sh.lsum[2][h] + sh.lsum[3][h]);
         }
       }
-      // The barrier orders every consumer's partial before thread 0's fence and arrival.
-      consumer_sync();
-      int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
-      if (tid == 0) {
-        __threadfence();
-        sh.last = atomicAdd(counter, 1) == nchunks - 1;
-      }
-      consumer_sync();
-      if (sh.last) {
-        __threadfence();
-        // Merge every chunk, 32 at a time: (m, l) of the group to shared memory, then each
-        // thread folds its dim of every head with the loads of a group in flight together.
-        float M[HR], Ls[HR], O[HR];
-#pragma unroll
-        for (int h = 0; h < HR; ++h) {
-          M[h] = -INFINITY;
-          Ls[h] = 0.f;
-          O[h] = 0.f;
-        }
-        for (int cb = 0; cb < nchunks; cb += 32) {
-          const int nc = min(32, nchunks - cb);
-          for (int i = tid; i < HR * 32; i += kTcThreads) {
-            const int h = i >> 5, c = i & 31;
-            float mv = -INFINITY, lv = 0.f;
-            if (h < nh && c < nc) {
-              const float* src = ws + h * ws_head + static_cast<int64_t>(cb + c) * row + kTcDim;
-              mv = __ldcg(src);
-              lv = __ldcg(src + 1);
-            }
-            sh.mrg[0][h][c] = mv;
-            sh.mrg[1][h][c] = lv;
-          }
-          consumer_sync();
-#pragma unroll
-          for (int h = 0; h < HR; ++h) {
-            if (h >= nh) continue;
-            float mg = M[h];
-            for (int c = 0; c < nc; ++c) mg = fmaxf(mg, sh.mrg[0][h][c]);
-            const float rescale = exp2f(M[h] - mg);
-            float l_acc = Ls[h] * rescale, o_acc = O[h] * rescale;
-            const float* hw = ws + h * ws_head + static_cast<int64_t>(cb) * row + d;
-#pragma unroll 8
-            for (int c = 0; c < nc; ++c) {
-              const float wgt = exp2f(sh.mrg[0][h][c] - mg);
-              l_acc = fmaf(sh.mrg[1][h][c], wgt, l_acc);
-              o_acc = fmaf(__ldcg(hw + static_cast<int64_t>(c) * row), wgt, o_acc);
-            }
-            M[h] = mg;
-            Ls[h] = l_acc;
-            O[h] = o_acc;
-          }
-          consumer_sync();
-        }
-#pragma unroll
-        for (int h = 0; h < HR; ++h)
-          if (h < nh) out[h * int64_t{kTcDim} + d] = E::from_f(O[h] / Ls[h]);
-        if (tid == 0) *counter = 0;
-      }
-      consumer_sync();   // sh.last is reused by the next unit
+      mbar_arrive(&sh.ep_full);
     }
     if (timed_out && tid == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
   }
