@@ -7,21 +7,22 @@
 // streams each unit's positions in tiles of 128 through a kTcStages-deep ring of shared-memory
 // stages. Taking units dynamically keeps the CTAs level even though the unit that holds the new
 // token, and whichever chunk arrives last and merges, do more work than the others.
-// Six roles, synchronised by mbarriers only:
+// Five roles, synchronised by mbarriers only:
 //   - warp 4, the producer, takes the units, passes their indices to the other warps through a
 //     small queue in shared memory, and refills a stage as soon as the tensor core has finished
 //     reading it (an "empty" mbarrier that tcgen05.commit arrives on after the tile's last MMA),
 //     so the ring stays full;
-//   - warp 6 prepares each unit ahead of the tensor core: the rotated queries (into one of two
-//     Q buffers), the new token's rotated K and raw V row, the cache-slot append and q_out;
+//   - warp 6, the aux warp, prepares each unit ahead of the tensor core (the rotated queries
+//     into one of two Q buffers, the new token's rotated K and raw V row, the cache-slot append
+//     and q_out) and finishes the unit before it (below);
 //   - warp 5 issues the QK products (one lane) and patches the new token's row into the tile
-//     holding it; warp 8 issues the PV products. Each tcgen05.mma blocks its issuing thread for
+//     holding it; warp 7 issues the PV products. Each tcgen05.mma blocks its issuing thread for
 //     about as long as the tensor pipe takes to run it, so two issuers keep the pipe fed while
 //     the other waits on a barrier;
 //   - warps 0-3 (the 128 TMEM lanes) run the softmax and the output correction, and hand each
-//     unit's accumulators to warp 7 through shared memory;
-//   - warp 7 writes the unit's output, or its partial, and merges a split KV head's chunks when
-//     it sees the last of them arrive.
+//     unit's accumulators to the aux warp through shared memory, which writes the unit's
+//     output, or its partial, and merges a split KV head's chunks when it sees the last of
+//     them arrive.
 // So the softmax warps never wait on an MMA issue, a query rotation or a merge.
 // Per tile:
 //   1. TMA (cp.async.bulk.tensor, 128-byte swizzle) brings K[128 positions][128 dims] and V of
@@ -69,10 +70,11 @@ namespace drk {
 constexpr int kTcThreads = 128;                    // consumers: warps 0-3
 constexpr int kTcProducerWarp = 4;
 constexpr int kTcMmaWarp = 5;
-constexpr int kTcPrepWarp = 6;
-constexpr int kTcEpilogueWarp = 7;
-constexpr int kTcPvWarp = 8;
-constexpr int kTcBlock = kTcThreads + 160;         // + producer, QK, prep, epilogue, PV warps
+constexpr int kTcAuxWarp = 6;
+constexpr int kTcPvWarp = 7;
+// Eight warps: each sub-partition's register file (16K) then holds two warps, so a thread may
+// use up to 255 registers.
+constexpr int kTcBlock = kTcThreads + 128;         // + producer, QK, aux and PV warps
 constexpr int kTcTile = 128;                       // positions per tile (MMA M of S^T)
 constexpr int kTcHeads = 16;                       // query heads per unit (MMA N)
 constexpr int kTcDim = 128;                        // head_dim
@@ -98,7 +100,8 @@ struct TcShared {
   float ep_m[kTcHeads];
   float ep_l[kTcHeads];
   float red[2][kTcThreads / 32][kTcHeads];         // per-warp tile maxima, double-buffered
-  float lsum[kTcThreads / 32][kTcHeads];           // per-warp row sums at a unit's end
+  float lsum[2][kTcThreads / 32][kTcHeads];        // per-warp row sums at a unit's end
+  float pend_m[2][kTcHeads];                       // that unit's running maxima
   uint4 kn[2][16];                                 // the new token's K row (storage type)
   uint4 vn[2][16];
   uint64_t full[kTcStages];
@@ -344,22 +347,39 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         mbar_arrive(&sh.uq_bar[slot]);
         ++queued;
       };
-      while (ok) {
-        const int64_t u = atomicAdd(next_unit, 1);
-        if (u >= units) break;
-        const TcUnit w = tc_unit<Idx>(p, a, u);
-        if (w.bad) {
-          if (w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
-            uint32_t bad = 0;
-            if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
-            if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
-            if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
-            atomicOr(p.status, bad);
+      int64_t unit_index = -1;   // index of the unit take() last returned
+      // The next unit with work, reporting bad indices on the way; t = -1 when none is left.
+      auto take = [&]() {
+        while (true) {
+          const int64_t u = atomicAdd(next_unit, 1);
+          if (u >= units) return TcUnit{-1, 0, 0, 0, 0, 0, 0, 0, 0, false};
+          const TcUnit w = tc_unit<Idx>(p, a, u);
+          if (w.bad) {
+            if (w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
+              uint32_t bad = 0;
+              if (w.pos < 0 || w.pos >= p.S) bad |= kStatusPosCache;
+              if (w.ri < 0 || w.ri >= p.B) bad |= kStatusRequest;
+              if (w.pos < 0 || w.pos >= p.table_rows) bad |= kStatusPosTable;
+              atomicOr(p.status, bad);
+            }
+            continue;
           }
-          continue;
+          if (w.ntiles > 0) {
+            unit_index = u;
+            return w;
+          }
         }
-        if (w.ntiles == 0) continue;
-        enqueue(u, w.pos, w.ri);
+      };
+      // Units are queued one ahead of the one being streamed, so the prep warp has a whole
+      // unit's time to rotate the next unit's queries.
+      TcUnit next = take();
+      int64_t next_index = unit_index;
+      if (next.t >= 0) enqueue(next_index, next.pos, next.ri);
+      while (ok && next.t >= 0) {
+        const TcUnit w = next;
+        next = take();
+        next_index = unit_index;
+        if (next.t >= 0) enqueue(next_index, next.pos, next.ri);
         for (int tile = 0; tile < w.ntiles; ++tile) {
           const int s = static_cast<int>(issued % kTcStages);
           if (issued >= kTcStages)
@@ -382,131 +402,222 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i)
         (void)mbar_wait(&sh.full[i % kTcStages], static_cast<uint32_t>((i / kTcStages) & 1));
     }
-  } else if (warp == kTcPrepWarp) {
-    // ---- prep: the unit's rotated queries (Q^T operand, K-major, 128-byte swizzle) and the
-    //      new token's K/V row, into buffer k % 2 once the QKs of unit k - 2 have completed;
-    //      the cache-slot append (head block 0) and q_out (chunk 0) ----
+  } else if (warp == kTcAuxWarp) {
+    // ---- aux warp, per queued unit k: prepare unit k, then finish unit k - 1 ----
+    // Prep: the unit's rotated queries (Q^T operand, K-major, 128-byte swizzle) and the new
+    // token's K/V row into buffer k % 2 once the QKs of unit k - 2 have completed; the
+    // cache-slot append (head block 0) and q_out (chunk 0).
+    auto prep_unit = [&](int64_t k, const TcUnit& w) {
+      const int qb = static_cast<int>(k & 1);
+      if (k >= 2 && !__all_sync(0xffffffffu, tc_wait(&sh.q_free[qb],
+                                                      static_cast<uint32_t>(((k >> 1) - 1) & 1))))
+        return false;
+        const int h0 = w.g * a.group + w.hb * kTcHeads;
+        const int nh = min(HR, a.group - w.hb * kTcHeads);
+        const float* crow = p.cos_t + w.pos * p.table_stride;
+        const float* srow = p.sin_t + w.pos * p.table_stride;
+        uint8_t* qs = sh.q[qb];
+        if (a.q_vec) {
+          // Full rotary, 16-byte rows: item = (head, 8-dim chunk of the first half); both halves
+          // of the rotate_half pair from one lane.
+          for (int item = lane; item < kTcHeads * 8; item += 32) {
+            const int hh = item >> 3, c = item & 7;
+            uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+            if (hh < nh) {
+              const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
+                                static_cast<int64_t>(h0 + hh) * p.q_hs;
+              const uint4 x1 = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+              const uint4 x2 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
+              const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
+              const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
+              const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
+              const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
+              const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+              const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+              float f1[8], f2[8];
+              unpack16<E>(x1, f1);
+              unpack16<E>(x2, f2);
+              uint32_t wl[4], wh[4];
+  #pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e0 = 2 * i, e1 = 2 * i + 1;
+                const raw a0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], true));
+                const raw a1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], true));
+                const raw b0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], false));
+                const raw b1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], false));
+                wl[i] = static_cast<uint32_t>(a0) | (static_cast<uint32_t>(a1) << 16);
+                wh[i] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
+              }
+              lo = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+              hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+              if (a.q_out != nullptr && w.chunk == 0) {
+                raw* qo =
+                    reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+                *reinterpret_cast<uint4*>(qo + 8 * c) = lo;
+                *reinterpret_cast<uint4*>(qo + 64 + 8 * c) = hi;
+              }
+            }
+            *reinterpret_cast<uint4*>(qs + sw128(hh, c)) = lo;
+            *reinterpret_cast<uint4*>(qs + kTcHeads * 128 + sw128(hh, c)) = hi;
+          }
+        } else {
+          for (int idx = lane; idx < kTcHeads * (kTcDim / 2); idx += 32) {
+            const int hh = idx / (kTcDim / 2);
+            const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
+            raw y0 = 0, y1 = 0;
+            if (hh < nh) {
+              const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
+                                static_cast<int64_t>(h0 + hh) * p.q_hs;
+              raw ys[2];
+  #pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int dd = d + e;
+                if (dd < p.R) {
+                  const int i = dd < half_r ? dd : dd - half_r;
+                  ys[e] = E::from_f(rotate_one(E::to_f(qrow[i]), E::to_f(qrow[i + half_r]),
+                                               __ldg(crow + i), __ldg(srow + i), dd < half_r));
+                } else {
+                  ys[e] = qrow[dd];
+                }
+              }
+              y0 = ys[0];
+              y1 = ys[1];
+              if (a.q_out != nullptr && w.chunk == 0) {
+                raw* qo =
+                    reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+                qo[d] = y0;
+                qo[d + 1] = y1;
+              }
+            }
+            const int box = d >> 6, db = (d & 63) * 2;     // byte within the 128-byte row
+            uint8_t* dst = qs + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
+            *reinterpret_cast<uint32_t*>(dst) =
+                static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16);
+          }
+        }
+        if (w.pos < w.p1) {
+          const raw* krow = reinterpret_cast<const raw*>(p.k) + w.t * p.k_ts + w.g * p.k_hs;
+          const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
+          raw* kn = reinterpret_cast<raw*>(sh.kn[qb]);
+          raw* vn = reinterpret_cast<raw*>(sh.vn[qb]);
+          const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
+          for (int d = lane; d < kTcDim; d += 32) {
+            raw kr = krow[d];
+            if (d < p.R) {
+              const int i = d < half_r ? d : d - half_r;
+              kr = E::from_f(rotate_one(E::to_f(krow[i]), E::to_f(krow[i + half_r]),
+                                        __ldg(crow + i), __ldg(srow + i), d < half_r));
+            }
+            const raw vr = vrow[d];
+            kn[d] = kr;
+            vn[d] = vr;
+            if (w.hb == 0) {
+              reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
+              reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
+            }
+          }
+        }
+        proxy_fence_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.q_full[qb]);
+      return true;
+    };
+    // Epilogue: the unit's output, or its partial and the cross-chunk merge.
+    auto epilogue_unit = [&](int64_t k, const TcUnit& w) {
+      if (!__all_sync(0xffffffffu, tc_wait(&sh.ep_full, static_cast<uint32_t>(k & 1))))
+        return false;
+        const int h0 = w.g * a.group + w.hb * kTcHeads;
+        const int nh = min(HR, a.group - w.hb * kTcHeads);
+        const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
+        float acc[HR][4], mh[HR], lh[HR];
+  #pragma unroll
+        for (int h = 0; h < HR; ++h) {
+          mh[h] = sh.ep_m[h];
+          lh[h] = sh.ep_l[h];
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) acc[h][i] = sh.ep_acc[h][lane + 32 * i];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.ep_empty);   // the softmax warps may refill the buffer
+        raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+        if (nchunks == 1) {
+  #pragma unroll
+          for (int h = 0; h < HR; ++h)
+            if (h < nh)
+  #pragma unroll
+              for (int i = 0; i < 4; ++i)
+                out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(acc[h][i] / lh[h]);
+          return true;
+        }
+        float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
+        const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
+  #pragma unroll
+        for (int h = 0; h < HR; ++h) {
+          if (h >= nh) continue;
+          float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = acc[h][i];
+          if (lane == 0) {
+            dst[kTcDim] = mh[h];
+            dst[kTcDim + 1] = lh[h];
+          }
+        }
+        __syncwarp();
+        int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
+        int last = 0;
+        if (lane == 0) {
+          __threadfence();
+          last = atomicAdd(counter, 1) == nchunks - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return true;
+        __threadfence();
+        for (int h = 0; h < nh; ++h) {
+          const float* hw = ws + h * ws_head;
+          float M = -INFINITY;
+          for (int c = lane; c < nchunks; c += 32) M = fmaxf(M, __ldcg(hw + c * row + kTcDim));
+  #pragma unroll
+          for (int off = 16; off >= 1; off >>= 1)
+            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+          float L = 0.f;
+          for (int c = lane; c < nchunks; c += 32)
+            L = fmaf(__ldcg(hw + c * row + kTcDim + 1), exp2f(__ldcg(hw + c * row + kTcDim) - M), L);
+  #pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+          float O[4] = {0.f, 0.f, 0.f, 0.f};
+  #pragma unroll 4
+          for (int c = 0; c < nchunks; ++c) {
+            const float* cb = hw + static_cast<int64_t>(c) * row;
+            const float wgt = exp2f(__ldcg(cb + kTcDim) - M);
+  #pragma unroll
+            for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cb + lane + 32 * i), wgt, O[i]);
+          }
+  #pragma unroll
+          for (int i = 0; i < 4; ++i)
+            out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / L);
+        }
+        if (lane == 0) *counter = 0;
+      return true;
+    };
     bool ok = true;
+    TcUnit prev{};
     for (int64_t k = 0; ok; ++k) {
       ok = __all_sync(0xffffffffu, queue_wait(k));
       if (!ok) break;
       const int64_t* msg = sh.uq[k % kTcQueue];
-      if (msg[0] < 0) break;
-      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
-      const int qb = static_cast<int>(k & 1);
-      if (k >= 2) {
-        ok = __all_sync(0xffffffffu, tc_wait(&sh.q_free[qb],
-                                             static_cast<uint32_t>(((k >> 1) - 1) & 1)));
+      const bool last_unit = msg[0] < 0;
+      TcUnit w{};
+      if (!last_unit) {
+        w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+        ok = prep_unit(k, w);
         if (!ok) break;
       }
-      const int h0 = w.g * a.group + w.hb * kTcHeads;
-      const int nh = min(HR, a.group - w.hb * kTcHeads);
-      const float* crow = p.cos_t + w.pos * p.table_stride;
-      const float* srow = p.sin_t + w.pos * p.table_stride;
-      uint8_t* qs = sh.q[qb];
-      if (a.q_vec) {
-        // Full rotary, 16-byte rows: item = (head, 8-dim chunk of the first half); both halves
-        // of the rotate_half pair from one lane.
-        for (int item = lane; item < kTcHeads * 8; item += 32) {
-          const int hh = item >> 3, c = item & 7;
-          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-          if (hh < nh) {
-            const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
-                              static_cast<int64_t>(h0 + hh) * p.q_hs;
-            const uint4 x1 = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-            const uint4 x2 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
-            const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
-            const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
-            const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            float f1[8], f2[8];
-            unpack16<E>(x1, f1);
-            unpack16<E>(x2, f2);
-            uint32_t wl[4], wh[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int e0 = 2 * i, e1 = 2 * i + 1;
-              const raw a0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], true));
-              const raw a1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], true));
-              const raw b0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], false));
-              const raw b1 = E::from_f(rotate_one(f1[e1], f2[e1], cs[e1], sn[e1], false));
-              wl[i] = static_cast<uint32_t>(a0) | (static_cast<uint32_t>(a1) << 16);
-              wh[i] = static_cast<uint32_t>(b0) | (static_cast<uint32_t>(b1) << 16);
-            }
-            lo = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-            hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-            if (a.q_out != nullptr && w.chunk == 0) {
-              raw* qo =
-                  reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
-              *reinterpret_cast<uint4*>(qo + 8 * c) = lo;
-              *reinterpret_cast<uint4*>(qo + 64 + 8 * c) = hi;
-            }
-          }
-          *reinterpret_cast<uint4*>(qs + sw128(hh, c)) = lo;
-          *reinterpret_cast<uint4*>(qs + kTcHeads * 128 + sw128(hh, c)) = hi;
-        }
-      } else {
-        for (int idx = lane; idx < kTcHeads * (kTcDim / 2); idx += 32) {
-          const int hh = idx / (kTcDim / 2);
-          const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
-          raw y0 = 0, y1 = 0;
-          if (hh < nh) {
-            const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
-                              static_cast<int64_t>(h0 + hh) * p.q_hs;
-            raw ys[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int dd = d + e;
-              if (dd < p.R) {
-                const int i = dd < half_r ? dd : dd - half_r;
-                ys[e] = E::from_f(rotate_one(E::to_f(qrow[i]), E::to_f(qrow[i + half_r]),
-                                             __ldg(crow + i), __ldg(srow + i), dd < half_r));
-              } else {
-                ys[e] = qrow[dd];
-              }
-            }
-            y0 = ys[0];
-            y1 = ys[1];
-            if (a.q_out != nullptr && w.chunk == 0) {
-              raw* qo =
-                  reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
-              qo[d] = y0;
-              qo[d + 1] = y1;
-            }
-          }
-          const int box = d >> 6, db = (d & 63) * 2;     // byte within the 128-byte row
-          uint8_t* dst = qs + box * (kTcHeads * 128) + sw128(hh, db >> 4) + (db & 15);
-          *reinterpret_cast<uint32_t*>(dst) =
-              static_cast<uint32_t>(y0) | (static_cast<uint32_t>(y1) << 16);
-        }
+      if (k >= 1) {
+        ok = epilogue_unit(k - 1, prev);
+        if (!ok) break;
       }
-      if (w.pos < w.p1) {
-        const raw* krow = reinterpret_cast<const raw*>(p.k) + w.t * p.k_ts + w.g * p.k_hs;
-        const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
-        raw* kn = reinterpret_cast<raw*>(sh.kn[qb]);
-        raw* vn = reinterpret_cast<raw*>(sh.vn[qb]);
-        const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
-        for (int d = lane; d < kTcDim; d += 32) {
-          raw kr = krow[d];
-          if (d < p.R) {
-            const int i = d < half_r ? d : d - half_r;
-            kr = E::from_f(rotate_one(E::to_f(krow[i]), E::to_f(krow[i + half_r]),
-                                      __ldg(crow + i), __ldg(srow + i), d < half_r));
-          }
-          const raw vr = vrow[d];
-          kn[d] = kr;
-          vn[d] = vr;
-          if (w.hb == 0) {
-            reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
-            reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
-          }
-        }
-      }
-      proxy_fence_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.q_full[qb]);
+      if (last_unit) break;
+      prev = w;
     }
     if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
   } else if (warp == kTcMmaWarp) {
@@ -600,96 +711,46 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       }
       if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
     }
-  } else if (warp == kTcEpilogueWarp) {
-    // ---- epilogue: a unit's output, or its partial and the cross-chunk merge ----
-    bool ok = true;
-    for (int64_t k = 0; ok; ++k) {
-      ok = __all_sync(0xffffffffu, queue_wait(k));
-      if (!ok) break;
-      const int64_t* msg = sh.uq[k % kTcQueue];
-      if (msg[0] < 0) break;
-      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
-      ok = __all_sync(0xffffffffu, tc_wait(&sh.ep_full, static_cast<uint32_t>(k & 1)));
-      if (!ok) break;
-      const int h0 = w.g * a.group + w.hb * kTcHeads;
-      const int nh = min(HR, a.group - w.hb * kTcHeads);
-      const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
-      float acc[HR][4], mh[HR], lh[HR];
-#pragma unroll
-      for (int h = 0; h < HR; ++h) {
-        mh[h] = sh.ep_m[h];
-        lh[h] = sh.ep_l[h];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[h][i] = sh.ep_acc[h][lane + 32 * i];
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.ep_empty);   // the softmax warps may refill the buffer
-      raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
-      if (nchunks == 1) {
-#pragma unroll
-        for (int h = 0; h < HR; ++h)
-          if (h < nh)
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(acc[h][i] / lh[h]);
-        continue;
-      }
-      float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
-      const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
-#pragma unroll
-      for (int h = 0; h < HR; ++h) {
-        if (h >= nh) continue;
-        float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = acc[h][i];
-        if (lane == 0) {
-          dst[kTcDim] = mh[h];
-          dst[kTcDim + 1] = lh[h];
-        }
-      }
-      __syncwarp();
-      int* counter = a.counters + (w.t * p.Hkv + w.g) * a.nhb + w.hb;
-      int last = 0;
-      if (lane == 0) {
-        __threadfence();
-        last = atomicAdd(counter, 1) == nchunks - 1;
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      __threadfence();
-      for (int h = 0; h < nh; ++h) {
-        const float* hw = ws + h * ws_head;
-        float M = -INFINITY;
-        for (int c = lane; c < nchunks; c += 32) M = fmaxf(M, __ldcg(hw + c * row + kTcDim));
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1)
-          M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        float L = 0.f;
-        for (int c = lane; c < nchunks; c += 32)
-          L = fmaf(__ldcg(hw + c * row + kTcDim + 1), exp2f(__ldcg(hw + c * row + kTcDim) - M), L);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-        float O[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int c = 0; c < nchunks; ++c) {
-          const float* cb = hw + static_cast<int64_t>(c) * row;
-          const float wgt = exp2f(__ldcg(cb + kTcDim) - M);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cb + lane + 32 * i), wgt, O[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / L);
-      }
-      if (lane == 0) *counter = 0;
-    }
-    if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
   } else {
-    // ---- softmax warps (0-3): scores, P, output correction; hand the unit to the epilogue ----
+    // ---- softmax warps (0-3): scores, P, output correction; hand each unit to the epilogue.
+    //      A unit's last O^T is read during the next unit's first tile, so the tile pipeline
+    //      runs across unit boundaries. ----
     const uint32_t tmem_lane = static_cast<uint32_t>(warp * 32) << 16;
     int64_t cj = 0;                // tiles of the walk consumed so far
     bool timed_out = false;
+    bool ok = true;
     const float scale = a.scale_log2;
+    // The previous unit, complete but for its last tile's O^T: its accumulators with the last
+    // correction applied (registers), its per-warp row sums and maxima (shared memory, ordered
+    // before the hand-over by the next tile's barrier).
+    bool pending = false;
+    int64_t pend_k = 0, pend_c = 0;
+    float pend_acc[HR];
+    // Adds the pending unit's last O^T and hands the unit to the epilogue warp.
+    auto hand_over = [&]() {
+      ok = tc_wait(&sh.o_bar[pend_c & 1], pair_parity(pend_c)) && ok;
+      tc_fence_after();
+      float o[kTcHeads];
+      tc_ld16(tmem + tmem_lane + kTcOCol + static_cast<int>(pend_c & 1) * kTcHeads, o);
+#pragma unroll
+      for (int h = 0; h < HR; ++h) pend_acc[h] += o[h];
+      tc_fence_before();
+      if (pend_k >= 1) ok = tc_wait(&sh.ep_empty, static_cast<uint32_t>((pend_k - 1) & 1)) && ok;
+      if (consumer_any(!ok)) return false;
+#pragma unroll
+      for (int h = 0; h < HR; ++h) {
+        sh.ep_acc[h][tid] = pend_acc[h];
+        if (tid == 0) {
+          const int pb = static_cast<int>(pend_k & 1);
+          sh.ep_m[h] = sh.pend_m[pb][h];
+          sh.ep_l[h] = (sh.lsum[pb][0][h] + sh.lsum[pb][1][h]) +
+                       (sh.lsum[pb][2][h] + sh.lsum[pb][3][h]);
+        }
+      }
+      mbar_arrive(&sh.ep_full);
+      pending = false;
+      return true;
+    };
 
     for (int64_t k = 0; !timed_out; ++k) {
       if (consumer_any(!queue_wait(k))) {
@@ -709,7 +770,6 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         acc[h] = 0.f;
         corr_prev[h] = 0.f;
       }
-      bool ok = true;
       for (int j = 0; j < w.ntiles; ++j) {
         const int64_t c = cj + j;
         const int b = static_cast<int>(c & 1);
@@ -769,46 +829,31 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           tc_ld16(tmem + tmem_lane + kTcOCol + (b ^ 1) * kTcHeads, o);
 #pragma unroll
           for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
+        } else if (pending && !hand_over()) {
+          timed_out = true;
+          break;
         }
 #pragma unroll
         for (int h = 0; h < HR; ++h) corr_prev[h] = corr_cur[h];
       }
       if (timed_out) break;
-      {
-        const int64_t c = cj + w.ntiles - 1;
-        ok = tc_wait(&sh.o_bar[c & 1], pair_parity(c)) && ok;
-        tc_fence_after();
-        float o[kTcHeads];
-        tc_ld16(tmem + tmem_lane + kTcOCol + static_cast<int>(c & 1) * kTcHeads, o);
-#pragma unroll
-        for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
-        tc_fence_before();
-      }
-      cj += w.ntiles;
-
-      // ---- row sums per head, then the hand-over to the epilogue warp ----
+      pending = true;
+      pend_k = k;
+      pend_c = cj + w.ntiles - 1;
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
         for (int h = 0; h < HR; ++h) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
-      if (lane == 0)
-#pragma unroll
-        for (int h = 0; h < HR; ++h) sh.lsum[warp][h] = lp[h];
-      if (k >= 1) ok = tc_wait(&sh.ep_empty, static_cast<uint32_t>((k - 1) & 1)) && ok;
-      if (consumer_any(!ok)) {
-        timed_out = true;
-        break;
-      }
 #pragma unroll
       for (int h = 0; h < HR; ++h) {
-        sh.ep_acc[h][tid] = acc[h];
-        if (tid == 0) {
-          sh.ep_m[h] = m_run[h];
-          sh.ep_l[h] = (sh.lsum[0][h] + sh.lsum[1][h]) + (sh.lsum[2][h] + sh.lsum[3][h]);
-        }
+        pend_acc[h] = acc[h] * corr_prev[h];
+        // Buffer k % 2: unit k - 1's copy may not have been read yet when a one-tile unit ends.
+        if (lane == 0) sh.lsum[k & 1][warp][h] = lp[h];
+        if (tid == 0) sh.pend_m[k & 1][h] = m_run[h];
       }
-      mbar_arrive(&sh.ep_full);
+      cj += w.ntiles;
     }
+    if (!timed_out && pending && !hand_over()) timed_out = true;
     if (timed_out && tid == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
   }
 
