@@ -57,10 +57,13 @@ def parse_args():
     p.add_argument("--no-floor", action="store_true", help="skip the empty-kernel launch floor")
     p.add_argument("--no-ladder", action="store_true",
                    help="skip the per-call operator ladder at batch 8")
+    p.add_argument("--no-attention", action="store_true",
+                   help="skip the fused append + decode attention measurement")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=1234)
-    p.add_argument("--mode", choices=["full", "bw"], default="full",
-                   help="bw: only the bandwidth-bound launch loop (for profiling small cases)")
+    p.add_argument("--mode", choices=["full", "bw", "attention"], default="full",
+                   help="bw: only the bandwidth-bound launch loop (for profiling small cases); "
+                        "attention: only the fused append + decode attention measurement")
     p.add_argument("--cache-len", type=int, default=0,
                    help="override cache_alloc_len (profiling runs only: keeps a case small)")
     p.add_argument("--launches", type=int, default=400, help="bw mode: timed launches")
@@ -440,6 +443,10 @@ def run_ours(args, world, rank, local):
     partial = None
     if not args.no_bw_probe and world == 1:
         partial = single_layer_probe("phi2_partial", world, rank, device, args.seed, peak)
+    attention = None
+    if not args.no_attention and rank == 0:
+        torch.cuda.empty_cache()
+        attention = attention_probe(device, args.seed, peak)
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -465,8 +472,120 @@ def run_ours(args, world, rank, local):
             "gpu_launches": args.steps * w.layers, "launch_floor": floor,
             "operator_ladder": ladder,
             "bandwidth_config": bw, "tp_config": tp, "partial_rotary_config": partial,
+            "fused_attention": attention,
         }
         print(json.dumps(line), flush=True)
+
+
+def attention_probe(device, seed, peak, sets=2, reps=12):
+    """Fused RoPE + append + decode attention (one launch, the tensor-core kernel) against the
+    append followed by a separate attention read of the same cache, graph-timed.
+
+    Two shapes (Llama-3-8B heads, 32:8:128 bf16, 8192-position token-major caches):
+      full_cache_b32:  every token at the last position, the read-side probe's configuration
+                       (the baseline is our fused append, then SDPA over the cache viewed
+                       head-major with enable_gqa);
+      ragged_b64:      the decode loop's layer, positions U[0, 8192) (the baseline is our fused
+                       append, then flash_attn's kv-cache decode with per-sequence lengths, when
+                       flash_attn runs on this GPU).
+    Bytes per call: the K and V rows each token attends over (positions 0..pos), plus q, k, v,
+    the appended slots and attn_out. Caches rotate over `sets` sets of 1-2 GiB (> L2)."""
+    from decode_llm_kernel_b200.cuda import ops
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    Hq, Hkv, D, S, dt = 32, 8, 128, 8192, torch.bfloat16
+    cos, sin = build_rope_tables(S, D, 500000.0, device=device)
+    out = {}
+
+    def graph_us(fns):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for f in fns:
+                f()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for f in fns:
+                f()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            g.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        del g
+        return s0.elapsed_time(s1) * 1e3 / (reps * len(fns))
+
+    for label, T, full in (("full_cache_b32", 32, True), ("ragged_b64", 64, False)):
+        gen = torch.Generator(device=device).manual_seed(seed)
+        st = []
+        for _ in range(sets):
+            kc = torch.randn(T, S, Hkv, D, device=device, dtype=dt, generator=gen)
+            vc = torch.randn(T, S, Hkv, D, device=device, dtype=dt, generator=gen)
+            q = torch.randn(T, Hq, D, device=device, dtype=dt, generator=gen)
+            k = torch.randn(T, Hkv, D, device=device, dtype=dt, generator=gen)
+            v = torch.randn(T, Hkv, D, device=device, dtype=dt, generator=gen)
+            if full:
+                pos = torch.full((T,), S - 1, device=device, dtype=torch.int32)
+            else:
+                pos = torch.randint(0, S, (T,), device=device, dtype=torch.int32, generator=gen)
+            ri = torch.arange(T, device=device, dtype=torch.int32)
+            st.append(dict(q=q, k=k, v=v, p=pos, ri=ri, kc=kc, vc=vc,
+                           out=torch.empty_like(q), qo=torch.empty_like(q)))
+        attended = sum(int(x["p"].sum().item()) + T for x in st) / sets
+        bytes_call = (2 * Hkv * D * 2 * attended + 2 * T * Hq * D * 2 + 4 * T * Hkv * D * 2)
+
+        def fused(x):
+            return lambda: ops.fused_rope_kv_append_attention(
+                x["q"], x["k"], x["v"], x["p"], cos, sin, x["kc"], x["vc"], x["ri"],
+                attn_out=x["out"])
+
+        def append(x):
+            return lambda: ops.fused_rope_kv_append_ex(x["q"], x["k"], x["v"], x["p"], cos, sin,
+                                                       x["kc"], x["vc"], x["ri"], q_out=x["qo"])
+        us = graph_us([fused(x) for x in st])
+        res = {"T": T, "Hq": Hq, "Hkv": Hkv, "D": D, "cache_alloc_len": S, "dtype": "bf16",
+               "positions": "all at S-1" if full else "U[0, S)",
+               "bytes_per_call": bytes_call, "fused_us": us,
+               "fused_gbs": bytes_call / us / 1e3, "frac_of_hbm_peak": bytes_call / us / 1e3 / peak,
+               "kernel": "drk::rope_kv_attention_tc_kernel (tcgen05 + TMA, warp-specialized)"}
+        try:
+            if full:
+                import torch.nn.functional as F
+
+                def read(x):
+                    qh = x["qo"].view(T, Hq, 1, D)
+                    kt, vt = x["kc"].transpose(1, 2), x["vc"].transpose(1, 2)
+                    return lambda: F.scaled_dot_product_attention(qh, kt, vt, enable_gqa=True)
+                base = "fused append, then torch SDPA over the token-major cache viewed head-major"
+            else:
+                from flash_attn import flash_attn_with_kvcache
+
+                def read(x):
+                    qh = x["qo"].view(T, 1, Hq, D)
+                    lens = x["p"] + 1
+                    return lambda: flash_attn_with_kvcache(qh, x["kc"], x["vc"],
+                                                           cache_seqlens=lens)
+                base = "fused append, then flash_attn_with_kvcache (per-sequence lengths)"
+
+            def both(x):
+                f1, f2 = append(x), read(x)
+                return lambda: (f1(), f2())
+            res["separate_us"] = graph_us([both(x) for x in st])
+            res["separate"] = base
+            res["speedup_vs_separate"] = res["separate_us"] / us
+        except Exception as e:  # noqa: BLE001 -- an unavailable baseline is reported, not fatal
+            res["separate"] = f"unavailable: {type(e).__name__}: {str(e)[:160]}"
+        out[label] = res
+        del st
+        torch.cuda.empty_cache()
+    return out
 
 
 def operator_ladder(device, seed):
@@ -663,6 +782,14 @@ def main():
                                   args.launches)
             if rank == 0:
                 print(json.dumps(out), flush=True)
+        elif args.mode == "attention":
+            from decode_llm_kernel_b200 import cuda
+            cuda.require()
+            local_dev = torch.device("cuda", local)
+            torch.cuda.set_device(local_dev)
+            peak, _ = measured_hbm_peak()
+            if rank == 0:
+                print(json.dumps(attention_probe(local_dev, args.seed, peak)), flush=True)
         else:
             run_ours(args, world, rank, local)
     finally:
