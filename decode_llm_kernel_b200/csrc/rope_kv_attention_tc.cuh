@@ -438,7 +438,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
               unpack16<E>(x1, f1);
               unpack16<E>(x2, f2);
               uint32_t wl[4], wh[4];
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const int e0 = 2 * i, e1 = 2 * i + 1;
                 const raw a0 = E::from_f(rotate_one(f1[e0], f2[e0], cs[e0], sn[e0], true));
@@ -469,7 +469,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
               const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
                                 static_cast<int64_t>(h0 + hh) * p.q_hs;
               raw ys[2];
-  #pragma unroll
+#pragma unroll
               for (int e = 0; e < 2; ++e) {
                 const int dd = d + e;
                 if (dd < p.R) {
@@ -522,40 +522,42 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         if (lane == 0) mbar_arrive(&sh.q_full[qb]);
       return true;
     };
-    // Epilogue: the unit's output, or its partial and the cross-chunk merge.
-    auto epilogue_unit = [&](int64_t k, const TcUnit& w) {
+    // Epilogue: read the unit's accumulators (freeing the hand-over buffer), write its output,
+    // or its partial and its arrival; `merge` is set when it arrived last of its chunks.
+    auto epilogue_fast = [&](int64_t k, const TcUnit& w, bool& merge) {
+      merge = false;
       if (!__all_sync(0xffffffffu, tc_wait(&sh.ep_full, static_cast<uint32_t>(k & 1))))
         return false;
         const int h0 = w.g * a.group + w.hb * kTcHeads;
         const int nh = min(HR, a.group - w.hb * kTcHeads);
         const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
         float acc[HR][4], mh[HR], lh[HR];
-  #pragma unroll
+#pragma unroll
         for (int h = 0; h < HR; ++h) {
           mh[h] = sh.ep_m[h];
           lh[h] = sh.ep_l[h];
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i) acc[h][i] = sh.ep_acc[h][lane + 32 * i];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.ep_empty);   // the softmax warps may refill the buffer
         raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
         if (nchunks == 1) {
-  #pragma unroll
+#pragma unroll
           for (int h = 0; h < HR; ++h)
             if (h < nh)
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 4; ++i)
                 out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(acc[h][i] / lh[h]);
           return true;
         }
         float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
         const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
-  #pragma unroll
+#pragma unroll
         for (int h = 0; h < HR; ++h) {
           if (h >= nh) continue;
           float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = acc[h][i];
           if (lane == 0) {
             dst[kTcDim] = mh[h];
@@ -570,35 +572,59 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           last = atomicAdd(counter, 1) == nchunks - 1;
         }
         last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) return true;
-        __threadfence();
-        for (int h = 0; h < nh; ++h) {
-          const float* hw = ws + h * ws_head;
-          float M = -INFINITY;
-          for (int c = lane; c < nchunks; c += 32) M = fmaxf(M, __ldcg(hw + c * row + kTcDim));
-  #pragma unroll
-          for (int off = 16; off >= 1; off >>= 1)
-            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-          float L = 0.f;
-          for (int c = lane; c < nchunks; c += 32)
-            L = fmaf(__ldcg(hw + c * row + kTcDim + 1), exp2f(__ldcg(hw + c * row + kTcDim) - M), L);
-  #pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-          float O[4] = {0.f, 0.f, 0.f, 0.f};
-  #pragma unroll 4
-          for (int c = 0; c < nchunks; ++c) {
-            const float* cb = hw + static_cast<int64_t>(c) * row;
-            const float wgt = exp2f(__ldcg(cb + kTcDim) - M);
-  #pragma unroll
-            for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cb + lane + 32 * i), wgt, O[i]);
-          }
-  #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / L);
-        }
-        if (lane == 0) *counter = 0;
+        merge = last != 0;
       return true;
     };
+    // Merges every chunk of the unit's (token, KV head, head block): the (m, l) of 32 chunks at
+    // a time into lanes, then each lane folds its 4 dims of each chunk of the group with the
+    // group's loads in flight together.
+    auto merge_unit = [&](const TcUnit& w) {
+      __threadfence();
+      const int h0 = w.g * a.group + w.hb * kTcHeads;
+      const int nh = min(HR, a.group - w.hb * kTcHeads);
+      const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
+      const float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
+      const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
+      raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+      for (int h = 0; h < nh; ++h) {
+        const float* hw = ws + h * ws_head;
+        float M = -INFINITY, Ls = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int cb = 0; cb < nchunks; cb += 32) {
+          const int c = cb + lane;
+          const float mc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim)
+                                       : -INFINITY;
+          const float lc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim + 1)
+                                       : 0.f;
+          float mg = fmaxf(M, mc);
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1)
+            mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+          const float rescale = exp2f(M - mg);
+          const float wc = c < nchunks ? exp2f(mc - mg) : 0.f;
+          float lg = lc * wc;
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
+          Ls = fmaf(Ls, rescale, lg);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) O[i] *= rescale;
+          const int nc = min(32, nchunks - cb);
+#pragma unroll 8
+          for (int j = 0; j < nc; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, wc, j);
+            const float* cp = hw + static_cast<int64_t>(cb + j) * row + lane;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cp + 32 * i), wj, O[i]);
+          }
+          M = mg;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / Ls);
+      }
+      if (lane == 0) a.counters[(w.t * p.Hkv + w.g) * a.nhb + w.hb] = 0;
+    };
+    // Per queued unit k: prepare unit k, then finish unit k - 1 (its merge too, if it
+    // arrived last of its chunks).
     bool ok = true;
     TcUnit prev{};
     for (int64_t k = 0; ok; ++k) {
@@ -613,8 +639,10 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         if (!ok) break;
       }
       if (k >= 1) {
-        ok = epilogue_unit(k - 1, prev);
+        bool merge = false;
+        ok = epilogue_fast(k - 1, prev, merge);
         if (!ok) break;
+        if (merge) merge_unit(prev);
       }
       if (last_unit) break;
       prev = w;
