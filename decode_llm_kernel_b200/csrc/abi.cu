@@ -662,9 +662,12 @@ drk_attention_options attention_or_default(const drk_attention_options* a) {
   return o;
 }
 
+// The body of both fused attention entry points; block_table is NULL for a contiguous (or
+// strided) cache and the page table of a paged one.
 void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
                     const drk_tensor* positions, const drk_tensor* cos, const drk_tensor* sin,
                     const drk_tensor* k_cache, const drk_tensor* v_cache,
+                    const drk_tensor* block_table,
                     const drk_tensor* request_indices, const drk_tensor* q_out,
                     const drk_tensor* attn_out, const drk_attention_options* attn,
                     void* workspace, size_t workspace_bytes, const drk_options* opts,
@@ -691,15 +694,32 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
             dtype_name(positions->dtype), "/", dtype_name(request_indices->dtype));
   const int32_t rot = resolve_rotary(o, D);
   check_rope_tables(cos, sin, D, rot, device);
-  const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0;
-  check_cache(k_cache, "k_cache", k->dtype, Hkv, D, device, strided_ok);
-  check_cache(v_cache, "v_cache", v->dtype, Hkv, D, device, strided_ok);
+  const bool paged = block_table != nullptr;
+  const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0 && !paged;
+  check_cache(k_cache, paged ? "k_pages" : "k_cache", k->dtype, Hkv, D, device, strided_ok);
+  check_cache(v_cache, paged ? "v_pages" : "v_cache", v->dtype, Hkv, D, device, strided_ok);
   check_caches_are_distinct(k_cache, v_cache);
+  int64_t block_size = 0;
+  if (paged) {
+    check_device(block_table, "block_table", device);
+    if (block_table->dtype != positions->dtype)
+      invalid("block_table must share the index dtype of positions, got ",
+              dtype_name(block_table->dtype), "/", dtype_name(positions->dtype));
+    if (block_table->ndim != 2 || !is_contiguous(block_table))
+      invalid("block_table must be a contiguous [num_requests, max_blocks_per_request] tensor");
+    block_size = k_cache->sizes[1];
+    if (block_size <= 0 || block_size % 8 || (128 % block_size && block_size % 128))
+      throw Unsupported(cat("paged fused attention takes block sizes that are multiples of 8 ",
+                            "dividing 128, or multiples of 128; got ", block_size));
+  }
   if (q_out != nullptr) check_output(q_out, "q_out", q->dtype, T, Hq, D, device);
   check_output(attn_out, "attn_out", q->dtype, T, Hq, D, device);
   check_float_dtype(q->dtype, "fused_rope_kv_append_attention");
-  const int64_t S = k_cache->sizes[1];
+  const int64_t S = paged ? block_table->sizes[1] * block_size : k_cache->sizes[1];
   const AttentionPlan pl = plan_attention(T, Hq, Hkv, D, S, q->dtype, ao, device);
+  if (paged && !pl.tc)
+    throw Unsupported("paged fused attention takes fp16/bf16 with head_dim 128 (the tensor-core "
+                      "kernel)");
   if (T == 0) return;
   const int64_t es = elem_size(q->dtype);
   uintptr_t addr = reinterpret_cast<uintptr_t>(k_cache->data) |
@@ -731,8 +751,14 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
   p.k_ts = k->strides[0]; p.k_hs = k->strides[1];
   p.v_ts = v->strides[0]; p.v_hs = v->strides[1];
   p.c_bs = k_cache->strides[0]; p.c_ss = k_cache->strides[1]; p.c_hs = k_cache->strides[2];
-  p.B = k_cache->sizes[0];
+  p.B = paged ? block_table->sizes[0] : k_cache->sizes[0];
   p.S = S;
+  if (paged) {
+    p.block_table = block_table->data;
+    p.num_blocks = k_cache->sizes[0];
+    p.block_size = block_size;
+    p.bt_stride = block_table->sizes[1];
+  }
   p.Hq = static_cast<int32_t>(Hq);
   p.Hkv = static_cast<int32_t>(Hkv);
   p.D = static_cast<int32_t>(D);
@@ -740,6 +766,7 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
   fill_table(p, cos, sin, o, R);
 
   drk::AttentionParams a{};
+  a.box_rows = paged ? static_cast<int32_t>(std::min<int64_t>(block_size, 128)) : 128;
   char* ws = static_cast<char*>(workspace);
   a.counters = reinterpret_cast<int*>(ws);
   a.workspace = reinterpret_cast<float*>(ws + pl.counter_bytes);
@@ -1026,8 +1053,22 @@ int drk_fused_rope_kv_append_attention(
     const drk_tensor* attn_out, const drk_attention_options* attn, void* workspace,
     size_t workspace_bytes, const drk_options* opts, uint32_t* status, drk_stream_t stream) {
   return guarded([&] {
-    attention_impl(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices, q_out,
-                   attn_out, attn, workspace, workspace_bytes, opts, status, stream);
+    attention_impl(q, k, v, positions, cos, sin, k_cache, v_cache, nullptr, request_indices,
+                   q_out, attn_out, attn, workspace, workspace_bytes, opts, status, stream);
+  });
+}
+
+int drk_paged_rope_kv_append_attention(
+    const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,
+    const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* k_pages,
+    const drk_tensor* v_pages, const drk_tensor* block_table,
+    const drk_tensor* request_indices, const drk_tensor* q_out, const drk_tensor* attn_out,
+    const drk_attention_options* attn, void* workspace, size_t workspace_bytes,
+    const drk_options* opts, uint32_t* status, drk_stream_t stream) {
+  return guarded([&] {
+    require(block_table, "block_table");
+    attention_impl(q, k, v, positions, cos, sin, k_pages, v_pages, block_table, request_indices,
+                   q_out, attn_out, attn, workspace, workspace_bytes, opts, status, stream);
   });
 }
 

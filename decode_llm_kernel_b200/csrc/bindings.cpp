@@ -322,6 +322,51 @@ at::Tensor fused_rope_kv_append_attention(
   return attn_out;
 }
 
+// Fused append + decode attention over a paged cache ([num_blocks, block_size, Hkv, D] pages
+// and a block table); attn_out and the workspace come from the caching allocator unless given.
+at::Tensor paged_rope_kv_append_attention(
+    at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor positions, at::Tensor cos,
+    at::Tensor sin, at::Tensor k_pages, at::Tensor v_pages, at::Tensor block_table,
+    at::Tensor request_indices, double scale, c10::optional<at::Tensor> q_out_opt,
+    c10::optional<at::Tensor> attn_out_opt, int64_t chunk, int64_t rotary_dim, bool pdl,
+    c10::optional<at::Tensor> workspace_opt) {
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && k_pages.dim() == 4 && block_table.dim() == 2,
+              "q must be [num_tokens, num_q_heads, head_dim], k [num_tokens, num_kv_heads, "
+              "head_dim], k_pages [num_blocks, block_size, num_kv_heads, head_dim] and "
+              "block_table [num_requests, max_blocks_per_request]");
+  at::Tensor attn_out;
+  if (attn_out_opt.has_value() && attn_out_opt->defined()) attn_out = *attn_out_opt;
+  else attn_out = empty_like_rows(q, q.size(1));
+  drk_attention_options ao{};
+  ao.scale = scale;
+  ao.chunk = static_cast<int32_t>(chunk);
+  ao.path = DRK_ATTN_PATH_TENSOR_CORES;
+  const int32_t device = q.is_cuda() ? q.get_device() : -1;
+  const int64_t need = drk_attention_workspace_bytes(
+      q.size(0), static_cast<int32_t>(q.size(1)), static_cast<int32_t>(k.size(1)),
+      static_cast<int32_t>(q.size(2)), block_table.size(1) * k_pages.size(1),
+      dtype_code(q.scalar_type()), &ao, device < 0 ? 0 : device);
+  if (need < 0) raise_on_error(static_cast<int>(need));
+  at::Tensor workspace;
+  if (workspace_opt.has_value() && workspace_opt->defined()) workspace = *workspace_opt;
+  else workspace = at::empty({std::max<int64_t>(need, 16)}, q.options().dtype(at::kByte));
+  TORCH_CHECK(workspace.is_contiguous(), "workspace must be contiguous");
+  const drk_options o = make_options(pdl ? DRK_FLAG_PDL : 0u, rotary_dim, c10::nullopt);
+  const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
+                   dp = describe(positions), dc = describe(cos), ds = describe(sin),
+                   dkp = describe(k_pages), dvp = describe(v_pages), dbt = describe(block_table),
+                   dri = describe(request_indices), dao = describe(attn_out);
+  drk_tensor dqo{};
+  const bool has_q_out = q_out_opt.has_value() && q_out_opt->defined();
+  if (has_q_out) dqo = describe(*q_out_opt);
+  raise_on_error(drk_paged_rope_kv_append_attention(
+      &dq, &dk, &dv, &dp, &dc, &ds, &dkp, &dvp, &dbt, &dri, has_q_out ? &dqo : nullptr, &dao,
+      &ao, workspace.data_ptr(),
+      static_cast<size_t>(workspace.numel() * workspace.element_size()), &o, status_for(q),
+      stream_for(q)));
+  return attn_out;
+}
+
 int64_t attention_workspace_bytes(int64_t num_tokens, int64_t num_q_heads, int64_t num_kv_heads,
                                   int64_t head_dim, int64_t cache_alloc_len,
                                   at::ScalarType dtype, int64_t chunk, int64_t heads_per_cta,
@@ -416,6 +461,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pdl") = false, py::arg("strided_cache") = false,
         py::arg("workspace") = py::none(), py::arg("path") = "auto",
         "Fused RoPE + KV append + decode attention over positions [0, pos]; returns attn_out.");
+  m.def("paged_rope_kv_append_attention", &paged_rope_kv_append_attention, py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"),
+        py::arg("k_pages"), py::arg("v_pages"), py::arg("block_table"),
+        py::arg("request_indices"), py::arg("scale") = 0.0, py::arg("q_out") = py::none(),
+        py::arg("attn_out") = py::none(), py::arg("chunk") = 0, py::arg("rotary_dim") = 0,
+        py::arg("pdl") = false, py::arg("workspace") = py::none(),
+        "Fused RoPE + append + decode attention over a paged (block-table) KV cache.");
   m.def("attention_workspace_bytes", &attention_workspace_bytes, py::arg("num_tokens"),
         py::arg("num_q_heads"), py::arg("num_kv_heads"), py::arg("head_dim"),
         py::arg("cache_alloc_len"), py::arg("dtype"), py::arg("chunk") = 0,

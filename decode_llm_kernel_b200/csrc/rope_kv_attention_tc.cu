@@ -31,16 +31,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// The cache as a 4-D tensor (dims, kv heads, positions, rows): rows are requests for a
+// contiguous cache and pages for a paged one (positions then run within a page).
 cudaError_t encode_cache_map(CUtensorMap* map, const void* base, bool bf16,
-                             const KernelParams& p) {
+                             const KernelParams& p, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return cudaErrorNotSupported;
+  const bool paged = p.block_table != nullptr;
   const cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.D), static_cast<cuuint64_t>(p.Hkv),
-                              static_cast<cuuint64_t>(p.S), static_cast<cuuint64_t>(p.B)};
+                              static_cast<cuuint64_t>(paged ? p.block_size : p.S),
+                              static_cast<cuuint64_t>(paged ? p.num_blocks : p.B)};
   const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.c_hs) * 2,
                                  static_cast<cuuint64_t>(p.c_ss) * 2,
                                  static_cast<cuuint64_t>(p.c_bs) * 2};
-  const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(kTcTile), 1};
+  const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
   const cuuint32_t estride[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                         4, const_cast<void*>(base), dims, strides, box, estride,
@@ -69,9 +73,9 @@ cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t u
   }
   CUtensorMap kmap, vmap;
   constexpr bool bf16 = std::is_same<E, BF16>::value;
-  err = encode_cache_map(&kmap, p.k_dst, bf16, p);
+  err = encode_cache_map(&kmap, p.k_dst, bf16, p, a.box_rows);
   if (err != cudaSuccess) return err;
-  err = encode_cache_map(&vmap, p.v_dst, bf16, p);
+  err = encode_cache_map(&vmap, p.v_dst, bf16, p, a.box_rows);
   if (err != cudaSuccess) return err;
   const int64_t sms = device_sm_count(device);
   const int grid = static_cast<int>(units < sms ? units : sms);

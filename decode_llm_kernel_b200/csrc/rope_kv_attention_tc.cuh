@@ -47,6 +47,10 @@
 // At a unit's end the partial (acc, m, l) per head goes to the workspace; the last chunk of a
 // (token, KV head, head block) to arrive merges them, exactly as in rope_kv_attention.cuh.
 //
+// A paged cache ([num_blocks, block_size, Hkv, D] pages and a block table) takes the same kernel:
+// a tile is gathered as one TMA box per page slice and lands in shared memory exactly like a
+// contiguous tile; entries outside the pool read zeros and set DRK_STATUS_BLOCK_OUT_OF_RANGE.
+//
 // The new token's rotated K and raw V row is written to the cache slot by head block 0 of the
 // unit holding pos and patched into the shared-memory tile that holds pos by every unit that
 // reads it, so no unit depends on another's global write (the tile may have been fetched before
@@ -386,13 +390,37 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             ok = tc_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
           if (!ok) break;
           uint8_t* st = sh.stage[s];
-          const int z = static_cast<int>(w.p0 + static_cast<int64_t>(tile) * kTcTile);
-          const int ri = static_cast<int>(w.ri);
+          const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTcTile;
           mbar_expect_tx(&sh.full[s], kTcStageBytes);
-          tma_load_4d(st, &kmap, 0, w.g, z, ri, &sh.full[s]);
-          tma_load_4d(st + kTcBoxBytes, &kmap, 64, w.g, z, ri, &sh.full[s]);
-          tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, w.g, z, ri, &sh.full[s]);
-          tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, w.g, z, ri, &sh.full[s]);
+          if (p.block_table == nullptr) {
+            const int zi = static_cast<int>(z), ri = static_cast<int>(w.ri);
+            tma_load_4d(st, &kmap, 0, w.g, zi, ri, &sh.full[s]);
+            tma_load_4d(st + kTcBoxBytes, &kmap, 64, w.g, zi, ri, &sh.full[s]);
+            tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, w.g, zi, ri, &sh.full[s]);
+            tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, w.g, zi, ri, &sh.full[s]);
+          } else {
+            // Paged cache: one box per page slice of the tile, stacked in the stage exactly
+            // as one 128-row box would be (each box is a multiple of 8 rows, so the 128-byte
+            // swizzle pattern continues across boxes).
+            const int rows = a.box_rows;
+            for (int r0 = 0; r0 < kTcTile; r0 += rows) {
+              const int64_t pp = z + r0;
+              const int64_t blk_i = pp / p.block_size;
+              int64_t blk = p.num_blocks;   // past the pool: TMA fills zeros
+              if (blk_i < p.bt_stride) {
+                const int64_t b = load_index<Idx>(p.block_table, w.ri * p.bt_stride + blk_i);
+                if (b >= 0 && b < p.num_blocks) blk = b;
+                else if (pp < w.p1 && p.status != nullptr) atomicOr(p.status, kStatusBlock);
+              }
+              const int row = static_cast<int>(pp - blk_i * p.block_size);
+              const int bi = static_cast<int>(blk);
+              const uint32_t off = static_cast<uint32_t>(r0) * 128u;
+              tma_load_4d(st + off, &kmap, 0, w.g, row, bi, &sh.full[s]);
+              tma_load_4d(st + kTcBoxBytes + off, &kmap, 64, w.g, row, bi, &sh.full[s]);
+              tma_load_4d(st + 2 * kTcBoxBytes + off, &vmap, 0, w.g, row, bi, &sh.full[s]);
+              tma_load_4d(st + 3 * kTcBoxBytes + off, &vmap, 64, w.g, row, bi, &sh.full[s]);
+            }
+          }
           ++issued;
         }
       }
@@ -500,7 +528,19 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           const raw* vrow = reinterpret_cast<const raw*>(p.v) + w.t * p.v_ts + w.g * p.v_hs;
           raw* kn = reinterpret_cast<raw*>(sh.kn[qb]);
           raw* vn = reinterpret_cast<raw*>(sh.vn[qb]);
-          const int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
+          // The cache slot (through the block table for a paged cache; -1 when that entry is
+          // outside the pool, which skips the append and is reported).
+          int64_t slot = w.ri * p.c_bs + w.pos * p.c_ss + w.g * p.c_hs;
+          if (p.block_table != nullptr) {
+            const int64_t blk_i = w.pos / p.block_size;
+            const int64_t blk = load_index<Idx>(p.block_table, w.ri * p.bt_stride + blk_i);
+            if (blk >= 0 && blk < p.num_blocks) {
+              slot = blk * p.c_bs + (w.pos - blk_i * p.block_size) * p.c_ss + w.g * p.c_hs;
+            } else {
+              slot = -1;
+              if (lane == 0 && w.hb == 0 && p.status != nullptr) atomicOr(p.status, kStatusBlock);
+            }
+          }
           for (int d = lane; d < kTcDim; d += 32) {
             raw kr = krow[d];
             if (d < p.R) {
@@ -511,7 +551,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             const raw vr = vrow[d];
             kn[d] = kr;
             vn[d] = vr;
-            if (w.hb == 0) {
+            if (w.hb == 0 && slot >= 0) {
               reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
               reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
             }

@@ -92,6 +92,8 @@ struct AttentionParams {
   int32_t group;         // Hq / Hkv
   int32_t nhb;           // head blocks per KV head
   int32_t q_vec;         // tensor-core kernel: full rotary with 16-byte q rows and table rows
+  int32_t box_rows;      // tensor-core kernel: positions per TMA box (128, or the page size of
+                         // a paged cache when it is smaller)
 };
 
 struct AttentionShape {

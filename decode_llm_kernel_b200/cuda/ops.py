@@ -103,6 +103,21 @@ def fused_rope_kv_append_attention(q, k, v, positions, cos, sin, k_cache, v_cach
         rotary_dim, pdl, strided_cache, workspace, path)
 
 
+def paged_rope_kv_append_attention(q, k, v, positions, cos, sin, k_pages, v_pages, block_table,
+                                   request_indices, *, scale=None, q_out=None, attn_out=None,
+                                   chunk=0, rotary_dim=0, pdl=False, workspace=None):
+    """fused_rope_kv_append_attention over a paged cache: k_pages/v_pages
+    [num_blocks, block_size, Hkv, D], block_table [num_requests, max_blocks] (positions' dtype);
+    position p of request r lives in block block_table[r, p // block_size], row
+    p % block_size. fp16/bf16 with head_dim 128; block_size a multiple of 8 dividing 128, or a
+    multiple of 128. A workspace, when given, holds at least attention_workspace_bytes(...,
+    cache_alloc_len=max_blocks * block_size, path="tensor_cores") bytes."""
+    return require().paged_rope_kv_append_attention(
+        q, k, v, positions, cos, sin, k_pages, v_pages, block_table, request_indices,
+        0.0 if scale is None else float(scale), q_out, attn_out, chunk, rotary_dim, pdl,
+        workspace)
+
+
 def attention_workspace_bytes(num_tokens, num_q_heads, num_kv_heads, head_dim, cache_alloc_len,
                               dtype, *, chunk=0, heads_per_cta=0, device=0, path="auto"):
     """Workspace bytes fused_rope_kv_append_attention needs for this shape and tuning."""
@@ -113,5 +128,6 @@ def attention_workspace_bytes(num_tokens, num_q_heads, num_kv_heads, head_dim, c
 
 __all__ = ["advance_positions", "attention_workspace_bytes", "fused_rope_kv_append",
            "fused_rope_kv_append_attention", "fused_rope_kv_append_ex", "kv_append",
-           "kv_append_ex", "paged_rope_kv_append", "rope_forward", "rope_forward_ex",
+           "kv_append_ex", "paged_rope_kv_append", "paged_rope_kv_append_attention",
+           "rope_forward", "rope_forward_ex",
            "separate_rope_kv_append"]

@@ -253,6 +253,25 @@ DRK_API int drk_fused_rope_kv_append_attention(
     size_t workspace_bytes, const drk_options* opts, uint32_t* status, drk_stream_t stream);
 
 /*
+ * drk_fused_rope_kv_append_attention over a paged KV cache: k_pages and v_pages are
+ * [num_blocks, block_size, Hkv, D] contiguous, block_table [num_requests, max_blocks_per_request]
+ * contiguous of the index dtype; position p of request r lives in block block_table[r, p /
+ * block_size], row p % block_size (the layout of drk_paged_rope_kv_append). No counterpart in
+ * the reference, whose cache is one contiguous row per request and whose notes name the
+ * block-table layout as the next step. fp16/bf16 with head_dim 128; block_size a multiple of 8
+ * that divides 128, or a multiple of 128. Size the workspace with drk_attention_workspace_bytes
+ * for cache_alloc_len = max_blocks_per_request * block_size. Block-table entries outside the
+ * pool are read as zeros, skip the append, and set DRK_STATUS_BLOCK_OUT_OF_RANGE.
+ */
+DRK_API int drk_paged_rope_kv_append_attention(
+    const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,
+    const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* k_pages,
+    const drk_tensor* v_pages, const drk_tensor* block_table,
+    const drk_tensor* request_indices, const drk_tensor* q_out, const drk_tensor* attn_out,
+    const drk_attention_options* attn, void* workspace, size_t workspace_bytes,
+    const drk_options* opts, uint32_t* status, drk_stream_t stream);
+
+/*
  * positions[t] += delta for every token: the device-side step of a decode loop, so a captured
  * step ending with this call replays without a host-side position copy. No counterpart in the
  * reference, whose graph runner copies new positions in before every replay

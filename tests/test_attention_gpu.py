@@ -268,3 +268,76 @@ def test_tensor_core_out_of_range_position_sets_status_and_writes_nothing():
     assert torch.equal(kc[bad_row].cpu(), kc0[bad_row].cpu())
     assert torch.all(attn[1] == 7.0)
     assert not torch.any(attn[0] == 7.0) and not torch.any(attn[2] == 7.0)
+
+
+def paged_from(case, block_size, seed, spare=3):
+    """A page pool holding the case's contiguous caches through a shuffled block table."""
+    q, k, v, p, cos, sin, kc, vc, ri = case
+    B, S, Hkv, D = kc.shape
+    nblk = S // block_size
+    g = torch.Generator().manual_seed(seed)
+    num_blocks = B * nblk + spare
+    table = torch.randperm(num_blocks, generator=g)[:B * nblk].view(B, nblk)
+    kp = torch.randn(num_blocks, block_size, Hkv, D, generator=g).to(kc.dtype)
+    vp = torch.randn(num_blocks, block_size, Hkv, D, generator=g).to(kc.dtype)
+    for b in range(B):
+        for j in range(nblk):
+            kp[table[b, j]] = kc[b, j * block_size:(j + 1) * block_size]
+            vp[table[b, j]] = vc[b, j * block_size:(j + 1) * block_size]
+    return kp, vp, table.to(p.dtype)
+
+
+def gather(pages, table):
+    B, nblk = table.shape
+    return pages[table.long().flatten()].view(B, nblk * pages.shape[1], *pages.shape[2:])
+
+
+@pytest.mark.parametrize("block_size", [16, 64, 128, 256])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_paged_cache_matches_oracle(block_size, dtype):
+    from decode_llm_kernel_b200 import cuda
+    case = make_case(35, 5, 32, 8, 128, 512, dtype, B=7)
+    kp, vp, table = paged_from(case, block_size, 36)
+    q, k, v, p, cos, sin, _, _, ri = [t.cuda() for t in case]
+    kpd, vpd, tbl = kp.cuda(), vp.cuda(), table.cuda()
+    used = set(table.flatten().tolist())
+    spare = [b for b in range(kp.shape[0]) if b not in used]
+    cuda.read_status()
+    q_out = torch.empty_like(q)
+    attn = ops().paged_rope_kv_append_attention(q, k, v, p, cos, sin, kpd, vpd, tbl, ri,
+                                                q_out=q_out)
+    torch.cuda.synchronize()
+    q_rot, kc_ref, vc_ref, attn_ref = oracle_result(case)
+    assert torch.equal(q_out.cpu(), q_rot)
+    assert torch.equal(gather(kpd.cpu(), table), kc_ref)
+    assert torch.equal(gather(vpd.cpu(), table), vc_ref)
+    assert torch.equal(kpd.cpu()[spare], kp[spare]) and torch.equal(vpd.cpu()[spare], vp[spare])
+    atol, rtol = ATTN_TOL[dtype]
+    torch.testing.assert_close(attn.cpu().double(), attn_ref.double(), atol=atol, rtol=rtol)
+    assert cuda.read_status() == 0
+
+
+def test_paged_cache_block_out_of_pool_sets_status():
+    from decode_llm_kernel_b200 import cuda
+    case = make_case(37, 3, 16, 4, 128, 256, torch.bfloat16, positions=[10, 200, 255])
+    kp, vp, table = paged_from(case, 64, 38)
+    table[int(case[8][1]), 3] = kp.shape[0] + 5        # the page holding token 1's position 200
+    q, k, v, p, cos, sin, _, _, ri = [t.cuda() for t in case]
+    cuda.read_status()
+    ops().paged_rope_kv_append_attention(q, k, v, p, cos, sin, kp.cuda(), vp.cuda(),
+                                         table.cuda(), ri)
+    status = cuda.read_status()
+    assert status & 8, cuda.require().status_string(status)
+
+
+def test_paged_cache_rejects_unsupported_shapes():
+    case = make_case(39, 2, 8, 2, 64, 128, torch.bfloat16)
+    kp, vp, table = paged_from(case, 16, 40)
+    with pytest.raises(RuntimeError, match="head_dim 128"):
+        ops().paged_rope_kv_append_attention(*[t.cuda() for t in case[:6]], kp.cuda(), vp.cuda(),
+                                             table.cuda(), case[8].cuda())
+    case = make_case(41, 2, 8, 2, 128, 120, torch.bfloat16)
+    kp, vp, table = paged_from(case, 24, 42)
+    with pytest.raises(RuntimeError, match="block sizes"):
+        ops().paged_rope_kv_append_attention(*[t.cuda() for t in case[:6]], kp.cuda(), vp.cuda(),
+                                             table.cuda(), case[8].cuda())
