@@ -487,7 +487,10 @@ def attention_probe(device, seed, peak, sets=2, reps=12):
                        head-major with enable_gqa);
       ragged_b64:      the decode loop's layer, positions U[0, 8192) (the baseline is our fused
                        append, then flash_attn's kv-cache decode with per-sequence lengths, when
-                       flash_attn runs on this GPU).
+                       flash_attn runs on this GPU);
+      ragged_b64_paged{16,256}: the same over a paged cache (pages shuffled through the block
+                       table; the baseline is our paged append, then flash_attn's kv-cache
+                       decode with the block table, which takes pages of 256 positions).
     Bytes per call: the K and V rows each token attends over (positions 0..pos), plus q, k, v,
     the appended slots and attn_out. Caches rotate over `sets` sets of 1-2 GiB (> L2)."""
     from decode_llm_kernel_b200.cuda import ops
@@ -583,6 +586,55 @@ def attention_probe(device, seed, peak, sets=2, reps=12):
         except Exception as e:  # noqa: BLE001 -- an unavailable baseline is reported, not fatal
             res["separate"] = f"unavailable: {type(e).__name__}: {str(e)[:160]}"
         out[label] = res
+        del st
+        torch.cuda.empty_cache()
+
+    # the decode layer over a paged cache: pages shuffled through the block table
+    for bs in (16, 256):
+        T = 64
+        gen = torch.Generator(device=device).manual_seed(seed + bs)
+        nblk = S // bs
+        st = []
+        for _ in range(sets):
+            kp = torch.randn(T * nblk, bs, Hkv, D, device=device, dtype=dt, generator=gen)
+            vp = torch.randn(T * nblk, bs, Hkv, D, device=device, dtype=dt, generator=gen)
+            table = torch.randperm(T * nblk, device=device, generator=gen).view(T, nblk)
+            st.append(dict(q=torch.randn(T, Hq, D, device=device, dtype=dt, generator=gen),
+                           k=torch.randn(T, Hkv, D, device=device, dtype=dt, generator=gen),
+                           v=torch.randn(T, Hkv, D, device=device, dtype=dt, generator=gen),
+                           p=torch.randint(0, S, (T,), device=device, dtype=torch.int32,
+                                           generator=gen),
+                           ri=torch.arange(T, device=device, dtype=torch.int32),
+                           kp=kp, vp=vp, table=table.to(torch.int32),
+                           out=torch.empty(T, Hq, D, device=device, dtype=dt),
+                           qo=torch.empty(T, Hq, D, device=device, dtype=dt)))
+        attended = sum(int(x["p"].sum().item()) + T for x in st) / sets
+        bytes_call = (2 * Hkv * D * 2 * attended + 2 * T * Hq * D * 2 + 4 * T * Hkv * D * 2)
+
+        def fused_paged(x):
+            return lambda: ops.paged_rope_kv_append_attention(
+                x["q"], x["k"], x["v"], x["p"], cos, sin, x["kp"], x["vp"], x["table"], x["ri"],
+                attn_out=x["out"])
+        us = graph_us([fused_paged(x) for x in st])
+        res = {"T": T, "block_size": bs, "positions": "U[0, S)", "bytes_per_call": bytes_call,
+               "fused_us": us, "fused_gbs": bytes_call / us / 1e3,
+               "frac_of_hbm_peak": bytes_call / us / 1e3 / peak}
+        try:
+            from flash_attn import flash_attn_with_kvcache
+
+            def both(x):
+                def run():
+                    ops.paged_rope_kv_append(x["q"], x["k"], x["v"], x["p"], cos, sin, x["kp"],
+                                             x["vp"], x["table"], x["ri"])
+                    flash_attn_with_kvcache(x["qo"].view(T, 1, Hq, D), x["kp"], x["vp"],
+                                            cache_seqlens=x["p"] + 1, block_table=x["table"])
+                return run
+            res["separate_us"] = graph_us([both(x) for x in st])
+            res["separate"] = "paged append, then flash_attn_with_kvcache with the block table"
+            res["speedup_vs_separate"] = res["separate_us"] / us
+        except Exception as e:  # noqa: BLE001 -- an unavailable baseline is reported, not fatal
+            res["separate"] = f"unavailable: {type(e).__name__}: {str(e)[:160]}"
+        out[f"ragged_b64_paged{bs}"] = res
         del st
         torch.cuda.empty_cache()
     return out

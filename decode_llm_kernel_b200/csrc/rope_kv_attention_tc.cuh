@@ -402,17 +402,34 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             // Paged cache: one box per page slice of the tile, stacked in the stage exactly
             // as one 128-row box would be (each box is a multiple of 8 rows, so the 128-byte
             // swizzle pattern continues across boxes).
+            // The tile's block-table entries are all loaded before the first box is issued,
+            // so the lookups cost one memory latency per tile, not one per page. A tile starts
+            // on a multiple of 128 positions: with pages of at most 128 rows box i is page
+            // first + i from row 0; a larger page holds the whole tile from row z - first * bs.
             const int rows = a.box_rows;
-            for (int r0 = 0; r0 < kTcTile; r0 += rows) {
-              const int64_t pp = z + r0;
-              const int64_t blk_i = pp / p.block_size;
-              int64_t blk = p.num_blocks;   // past the pool: TMA fills zeros
-              if (blk_i < p.bt_stride) {
-                const int64_t b = load_index<Idx>(p.block_table, w.ri * p.bt_stride + blk_i);
-                if (b >= 0 && b < p.num_blocks) blk = b;
-                else if (pp < w.p1 && p.status != nullptr) atomicOr(p.status, kStatusBlock);
+            const int nbox = kTcTile / rows;
+            const int64_t first = z / p.block_size;
+            const int row0 = static_cast<int>(z - first * p.block_size);
+            constexpr int64_t kPastTable = INT64_MIN;   // a page past the request's table
+            int64_t blks[kTcTile / 8];
+#pragma unroll
+            for (int i = 0; i < kTcTile / 8; ++i) {
+              blks[i] = kPastTable;
+              if (i < nbox && first + i < p.bt_stride)
+                blks[i] = load_index<Idx>(p.block_table, w.ri * p.bt_stride + first + i);
+            }
+#pragma unroll
+            for (int i = 0; i < kTcTile / 8; ++i) {
+              if (i >= nbox) break;
+              const int r0 = i * rows;
+              int64_t blk = blks[i];
+              if (blk < 0 || blk >= p.num_blocks) {
+                // Outside the pool: TMA reads zeros there (coordinate past the last page).
+                if (blk != kPastTable && z + r0 < w.p1 && p.status != nullptr)
+                  atomicOr(p.status, kStatusBlock);
+                blk = p.num_blocks;
               }
-              const int row = static_cast<int>(pp - blk_i * p.block_size);
+              const int row = row0;
               const int bi = static_cast<int>(blk);
               const uint32_t off = static_cast<uint32_t>(r0) * 128u;
               tma_load_4d(st + off, &kmap, 0, w.g, row, bi, &sh.full[s]);
