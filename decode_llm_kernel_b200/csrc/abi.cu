@@ -608,12 +608,31 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
     int64_t chunk = ao.chunk;
     if (chunk < 0) invalid("chunk must be >= 0, got ", chunk);
     if (chunk == 0) {
-      // The grid takes units dynamically, so about two units per SM keep it busy; longer
-      // chunks mean fewer cross-chunk merges. At least 512 positions (four tiles) per unit.
+      // Cost model of the persistent grid, fitted to B200 sweeps (batch 4..64, 2048..32768
+      // positions, GQA and MQA): units of one chunk run in rounds of one per SM; a full round
+      // streams at the HBM rate, a partial round of r units at min(HBM, r x one SM's TMA
+      // rate, ~90 GB/s with three 64 KB stages in flight); every round adds ~3 us of unit
+      // start and epilogue, and ~3 us more when chunks are merged. Positions live on the
+      // device, so every sequence is taken as S long. Candidates: 512 (four tiles) doubling
+      // up to S, then S itself (no merge).
+      constexpr double kHbm = 6.6e12, kPerSm = 90e9, kRound = 3e-6, kMerge = 3e-6;
       const int64_t heads = std::max<int64_t>(1, T * Hkv * pl.nhb);
-      const int64_t target = 2LL * drk::device_sm_count(device);
-      chunk = 512;
-      while (chunk < S && heads * ((S + 2 * chunk - 1) / (2 * chunk)) >= target) chunk <<= 1;
+      const int64_t sms = std::max(1, drk::device_sm_count(device));
+      const double row_bytes = 2.0 * D * es;
+      const int64_t whole = (std::max<int64_t>(S, 1) + 127) / 128 * 128;
+      double best = 0;
+      for (int64_t c = 512;; c <<= 1) {
+        const int64_t cand = std::min(c, whole);
+        const int64_t nch = (S + cand - 1) / cand;
+        const int64_t units = heads * std::max<int64_t>(nch, 1);
+        const int64_t rounds = units / sms, rem = units % sms;
+        const double unit_bytes = row_bytes * cand;
+        double t = rounds * (sms * unit_bytes / kHbm);
+        if (rem) t += rem * unit_bytes / std::min(kHbm, rem * kPerSm);
+        t += (rounds + (rem ? 1 : 0)) * (kRound + (nch > 1 ? kMerge : 0.0));
+        if (chunk == 0 || t < best) { best = t; chunk = cand; }
+        if (cand >= whole) break;
+      }
     }
     pl.chunk = (chunk + 127) / 128 * 128;
     pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);

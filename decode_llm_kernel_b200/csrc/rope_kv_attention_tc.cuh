@@ -92,6 +92,8 @@ constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 hea
 // and the epilogue warp at most one unit behind the consumers, so fewer than 8 queued units are
 // ever unread.
 constexpr int kTcQueue = 16;
+constexpr int kTcSortMax = 2048;                   // tokens ordered longest-first up to this
+constexpr int kTcSortBuckets = 256;                // length buckets of that order
 constexpr int kTcSBufs = 3;                        // S^T accumulators in flight
 constexpr uint32_t kTcOCol = kTcSBufs * 16;        // first O^T column
 constexpr uint32_t kTcTmemCols = 128;              // S^T at 0, 16, 32; O^T at 48, 64
@@ -121,6 +123,7 @@ struct TcShared {
   int64_t uq[kTcQueue][3];                         // (unit, position, request) taken by the
                                                    // producer; unit -1 ends the walk
   uint64_t uq_bar[kTcQueue];                       // a queue slot was written (producer)
+  uint16_t order[kTcSortMax];                      // tokens, longest first (producer)
   uint32_t tmem_base;
 };
 constexpr size_t kTcSmemBytes = sizeof(TcShared) + 1024;   // + alignment slack
@@ -337,8 +340,67 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   const int row = p.D + 2;
 
   if (warp == kTcProducerWarp) {
-    // ---- producer (one lane): take units, queue them, refill each stage once its last MMA
-    //      has read it ----
+    // ---- producer: order the tokens longest first, then (one lane) take units, queue them,
+    //      and refill each stage once its last MMA has read it ----
+    // Units are handed out in the order of a stable counting sort of the tokens on 256 buckets
+    // of position / S, descending, so the grid starts the longest units first and fills the
+    // tail with short ones (a longest-processing-time schedule). Every CTA computes the same
+    // order. The last stage buffer holds the bucket cursors and keys until its first load.
+    const int64_t per_token = static_cast<int64_t>(p.Hkv) * a.nhb * a.max_chunks;
+    const bool sorted = p.T > 1 && p.T <= kTcSortMax;
+    if (sorted) {
+      const int n = static_cast<int>(p.T);
+      int* cursor = reinterpret_cast<int*>(sh.stage[kTcStages - 1]);
+      uint8_t* key = reinterpret_cast<uint8_t*>(cursor + kTcSortBuckets);
+      for (int b = lane; b < kTcSortBuckets; b += 32) cursor[b] = 0;
+      __syncwarp();
+      for (int i = lane; i < n; i += 32) {
+        const int64_t pos = load_index<Idx>(p.positions, i);
+        const int k = (pos >= 0 && pos < p.S) ? static_cast<int>(pos * kTcSortBuckets / p.S) : 0;
+        key[i] = static_cast<uint8_t>(k);
+        atomicAdd(&cursor[k], 1);
+      }
+      __syncwarp();
+      // Exclusive prefix over the buckets from the longest down: lane l owns buckets
+      // 255 - 8l down to 248 - 8l.
+      constexpr int kPer = kTcSortBuckets / 32;
+      int cnt[kPer], local = 0;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        cnt[j] = cursor[kTcSortBuckets - 1 - kPer * lane - j];
+        local += cnt[j];
+      }
+      int incl = local;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+      }
+      int run = incl - local;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        cursor[kTcSortBuckets - 1 - kPer * lane - j] = run;
+        run += cnt[j];
+      }
+      __syncwarp();
+      // Scatter 32 tokens at a time; lanes with equal keys take consecutive slots in lane
+      // order, which keeps the sort stable.
+      const uint32_t below = (1u << lane) - 1u;
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const int k = i < n ? key[i] : kTcSortBuckets + lane;   // past-the-end lanes: unique
+        const uint32_t grp = __match_any_sync(0xffffffffu, k);
+        const int base = i < n ? cursor[k] : 0;
+        __syncwarp();
+        if (i < n) {
+          sh.order[base + __popc(grp & below)] = static_cast<uint16_t>(i);
+          if ((grp & below) == 0u) cursor[k] = base + __popc(grp);
+        }
+        __syncwarp();
+      }
+      proxy_fence_shared();   // generic writes to the stage before its first TMA load
+      __syncwarp();
+    }
     if (lane == 0) {
       int* next_unit = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
       int64_t issued = 0, queued = 0;
@@ -355,8 +417,12 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       // The next unit with work, reporting bad indices on the way; t = -1 when none is left.
       auto take = [&]() {
         while (true) {
-          const int64_t u = atomicAdd(next_unit, 1);
+          int64_t u = atomicAdd(next_unit, 1);
           if (u >= units) return TcUnit{-1, 0, 0, 0, 0, 0, 0, 0, 0, false};
+          if (sorted) {
+            const int64_t r = u / per_token;
+            u = static_cast<int64_t>(sh.order[r]) * per_token + (u - r * per_token);
+          }
           const TcUnit w = tc_unit<Idx>(p, a, u);
           if (w.bad) {
             if (w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
