@@ -340,8 +340,8 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   const int row = p.D + 2;
 
   if (warp == kTcProducerWarp) {
-    // ---- producer: order the tokens longest first, then (one lane) take units, queue them,
-    //      and refill each stage once its last MMA has read it ----
+    // ---- producer: order the tokens longest first, then take units, queue them, and refill
+    //      each stage once its last MMA has read it ----
     // Units are handed out in the order of a stable counting sort of the tokens on 256 buckets
     // of position / S, descending, so the grid starts the longest units first and fills the
     // tail with short ones (a longest-processing-time schedule). Every CTA computes the same
@@ -401,24 +401,28 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       proxy_fence_shared();   // generic writes to the stage before its first TMA load
       __syncwarp();
     }
-    if (lane == 0) {
-      int* next_unit = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
-      int64_t issued = 0, queued = 0;
-      bool ok = true;
-      auto enqueue = [&](int64_t u, int64_t pos, int64_t ri) {
-        const int slot = static_cast<int>(queued % kTcQueue);
-        sh.uq[slot][0] = u;
-        sh.uq[slot][1] = pos;
-        sh.uq[slot][2] = ri;
-        mbar_arrive(&sh.uq_bar[slot]);
-        ++queued;
-      };
-      int64_t unit_index = -1;   // index of the unit take() last returned
-      // The next unit with work, reporting bad indices on the way; t = -1 when none is left.
-      auto take = [&]() {
+    // All 32 lanes walk the units: lane 0 takes and queues them; the TMA boxes of a paged
+    // tile are issued by as many lanes as there are boxes (one instruction for up to 32 page
+    // slices), the four boxes of a contiguous tile by lane 0.
+    int* next_unit = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
+    int64_t issued = 0, queued = 0;
+    bool ok = true;
+    auto enqueue = [&](int64_t u, int64_t pos, int64_t ri) {   // lane 0
+      const int slot = static_cast<int>(queued % kTcQueue);
+      sh.uq[slot][0] = u;
+      sh.uq[slot][1] = pos;
+      sh.uq[slot][2] = ri;
+      mbar_arrive(&sh.uq_bar[slot]);
+      ++queued;
+    };
+    // The next unit with work: lane 0 takes it, reporting bad indices on the way, and the
+    // warp gets its index, position and request index; t = -1 when none is left.
+    auto take = [&](int64_t& index) {
+      int64_t tu = -1, tpos = 0, tri = 0;
+      if (lane == 0) {
         while (true) {
           int64_t u = atomicAdd(next_unit, 1);
-          if (u >= units) return TcUnit{-1, 0, 0, 0, 0, 0, 0, 0, 0, false};
+          if (u >= units) break;
           if (sorted) {
             const int64_t r = u / per_token;
             u = static_cast<int64_t>(sh.order[r]) * per_token + (u - r * per_token);
@@ -435,78 +439,96 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             continue;
           }
           if (w.ntiles > 0) {
-            unit_index = u;
-            return w;
+            tu = u;
+            tpos = w.pos;
+            tri = w.ri;
+            break;
           }
         }
-      };
-      // Units are queued one ahead of the one being streamed, so the prep warp has a whole
-      // unit's time to rotate the next unit's queries.
-      TcUnit next = take();
-      int64_t next_index = unit_index;
-      if (next.t >= 0) enqueue(next_index, next.pos, next.ri);
-      while (ok && next.t >= 0) {
-        const TcUnit w = next;
-        next = take();
-        next_index = unit_index;
-        if (next.t >= 0) enqueue(next_index, next.pos, next.ri);
-        for (int tile = 0; tile < w.ntiles; ++tile) {
-          const int s = static_cast<int>(issued % kTcStages);
-          if (issued >= kTcStages)
-            ok = tc_wait(&sh.empty[s], static_cast<uint32_t>(((issued / kTcStages) + 1) & 1));
-          if (!ok) break;
-          uint8_t* st = sh.stage[s];
-          const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTcTile;
-          mbar_expect_tx(&sh.full[s], kTcStageBytes);
-          if (p.block_table == nullptr) {
+      }
+      tu = __shfl_sync(0xffffffffu, tu, 0);
+      tpos = __shfl_sync(0xffffffffu, tpos, 0);
+      tri = __shfl_sync(0xffffffffu, tri, 0);
+      index = tu;
+      if (tu < 0) return TcUnit{-1, 0, 0, 0, 0, 0, 0, 0, 0, false};
+      return tc_unit_at(p, a, tu, tpos, tri);
+    };
+    // Units are queued one ahead of the one being streamed, so the prep warp has a whole
+    // unit's time to rotate the next unit's queries.
+    int64_t next_index = -1;
+    TcUnit next = take(next_index);
+    if (lane == 0 && next.t >= 0) enqueue(next_index, next.pos, next.ri);
+    while (ok && next.t >= 0) {
+      const TcUnit w = next;
+      next = take(next_index);
+      if (lane == 0 && next.t >= 0) enqueue(next_index, next.pos, next.ri);
+      for (int tile = 0; tile < w.ntiles; ++tile) {
+        const int s = static_cast<int>(issued % kTcStages);
+        const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTcTile;
+        // Paged cache: box b of the tile is slice b / 4 of the tile's pages, K lo, K hi, V lo
+        // or V hi by b % 4, issued by lane b % 32. A lane loads the block-table entries of its
+        // boxes before the wait for a free stage, so their latency hides behind it. A tile
+        // starts on a multiple of 128 positions: with pages of at most 128 rows slice i is
+        // page first + i from row 0; a larger page holds the whole tile from row
+        // z - first * bs.
+        constexpr int64_t kPastTable = INT64_MIN;   // a page past the request's table
+        int nbox = 0, row0 = 0;
+        int64_t blk0 = kPastTable, blk1 = kPastTable;   // pages of boxes lane and lane + 32
+        if (p.block_table != nullptr) {
+          nbox = kTcTile / a.box_rows;
+          const int64_t first = z / p.block_size;
+          row0 = static_cast<int>(z - first * p.block_size);
+          const int64_t i0 = first + (lane >> 2), i1 = first + ((lane + 32) >> 2);
+          const int64_t row_base = w.ri * p.bt_stride;
+          if (lane < 4 * nbox && i0 < p.bt_stride)
+            blk0 = load_index<Idx>(p.block_table, row_base + i0);
+          if (lane + 32 < 4 * nbox && i1 < p.bt_stride)
+            blk1 = load_index<Idx>(p.block_table, row_base + i1);
+        }
+        if (issued >= kTcStages)
+          ok = __all_sync(0xffffffffu,
+                          tc_wait(&sh.empty[s],
+                                  static_cast<uint32_t>(((issued / kTcStages) + 1) & 1)));
+        if (!ok) break;
+        uint8_t* st = sh.stage[s];
+        if (p.block_table == nullptr) {
+          if (lane == 0) {
+            mbar_expect_tx(&sh.full[s], kTcStageBytes);
             const int zi = static_cast<int>(z), ri = static_cast<int>(w.ri);
             tma_load_4d(st, &kmap, 0, w.g, zi, ri, &sh.full[s]);
             tma_load_4d(st + kTcBoxBytes, &kmap, 64, w.g, zi, ri, &sh.full[s]);
             tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, w.g, zi, ri, &sh.full[s]);
             tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, w.g, zi, ri, &sh.full[s]);
-          } else {
-            // Paged cache: one box per page slice of the tile, stacked in the stage exactly
-            // as one 128-row box would be (each box is a multiple of 8 rows, so the 128-byte
-            // swizzle pattern continues across boxes).
-            // The tile's block-table entries are all loaded before the first box is issued,
-            // so the lookups cost one memory latency per tile, not one per page. A tile starts
-            // on a multiple of 128 positions: with pages of at most 128 rows box i is page
-            // first + i from row 0; a larger page holds the whole tile from row z - first * bs.
-            const int rows = a.box_rows;
-            const int nbox = kTcTile / rows;
-            const int64_t first = z / p.block_size;
-            const int row0 = static_cast<int>(z - first * p.block_size);
-            constexpr int64_t kPastTable = INT64_MIN;   // a page past the request's table
-            int64_t blks[kTcTile / 8];
-#pragma unroll
-            for (int i = 0; i < kTcTile / 8; ++i) {
-              blks[i] = kPastTable;
-              if (i < nbox && first + i < p.bt_stride)
-                blks[i] = load_index<Idx>(p.block_table, w.ri * p.bt_stride + first + i);
-            }
-#pragma unroll
-            for (int i = 0; i < kTcTile / 8; ++i) {
-              if (i >= nbox) break;
-              const int r0 = i * rows;
-              int64_t blk = blks[i];
-              if (blk < 0 || blk >= p.num_blocks) {
-                // Outside the pool: TMA reads zeros there (coordinate past the last page).
-                if (blk != kPastTable && z + r0 < w.p1 && p.status != nullptr)
-                  atomicOr(p.status, kStatusBlock);
-                blk = p.num_blocks;
-              }
-              const int row = row0;
-              const int bi = static_cast<int>(blk);
-              const uint32_t off = static_cast<uint32_t>(r0) * 128u;
-              tma_load_4d(st + off, &kmap, 0, w.g, row, bi, &sh.full[s]);
-              tma_load_4d(st + kTcBoxBytes + off, &kmap, 64, w.g, row, bi, &sh.full[s]);
-              tma_load_4d(st + 2 * kTcBoxBytes + off, &vmap, 0, w.g, row, bi, &sh.full[s]);
-              tma_load_4d(st + 3 * kTcBoxBytes + off, &vmap, 64, w.g, row, bi, &sh.full[s]);
-            }
           }
-          ++issued;
+        } else {
+          // Page slices stack in the stage exactly as one 128-row box would (each is a
+          // multiple of 8 rows, so the 128-byte swizzle pattern continues across them).
+          if (lane == 0) mbar_expect_tx(&sh.full[s], kTcStageBytes);
+          __syncwarp();
+          const int rows = a.box_rows;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int b = lane + 32 * h;
+            if (b >= 4 * nbox) break;
+            const int i = b >> 2, kind = b & 3;
+            const int r0 = i * rows;
+            int64_t blk = h ? blk1 : blk0;
+            if (blk < 0 || blk >= p.num_blocks) {
+              // Outside the pool: TMA reads zeros there (coordinate past the last page).
+              if (kind == 0 && blk != kPastTable && z + r0 < w.p1 && p.status != nullptr)
+                atomicOr(p.status, kStatusBlock);
+              blk = p.num_blocks;
+            }
+            const uint32_t off = static_cast<uint32_t>(kind) * kTcBoxBytes +
+                                 static_cast<uint32_t>(r0) * 128u;
+            tma_load_4d(st + off, kind < 2 ? &kmap : &vmap, (kind & 1) * 64, w.g, row0,
+                        static_cast<int>(blk), &sh.full[s]);
+          }
         }
+        ++issued;
       }
+    }
+    if (lane == 0) {
       enqueue(-1, 0, 0);
       if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
       // Every copy this CTA issued lands before its shared memory goes away.

@@ -151,6 +151,14 @@ def test_chunks_and_head_blocks(chunk, heads_per_cta):
     check(case, run_gpu(case, chunk=chunk, heads_per_cta=heads_per_cta))
 
 
+@pytest.mark.parametrize("T", [300, 2100])
+def test_tensor_core_many_ragged_tokens(T):
+    """The grid hands out tokens longest first up to 2048 tokens (300: many equal positions,
+    so the order's ties matter) and in index order beyond (2100)."""
+    case = make_case(41, T, 4, 1, 128, 200, torch.bfloat16)
+    check(case, run_gpu(case, path="tensor_cores"))
+
+
 def test_head_major_cache_and_int64_indices():
     case = make_case(13, 7, 32, 8, 128, 257, torch.float16, index_dtype=torch.int64)
     check(case, run_gpu(case, strided=True, chunk=32))
@@ -292,7 +300,7 @@ def gather(pages, table):
     return pages[table.long().flatten()].view(B, nblk * pages.shape[1], *pages.shape[2:])
 
 
-@pytest.mark.parametrize("block_size", [16, 64, 128, 256])
+@pytest.mark.parametrize("block_size", [8, 16, 32, 64, 128, 256])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_paged_cache_matches_oracle(block_size, dtype):
     from decode_llm_kernel_b200 import cuda
