@@ -37,19 +37,37 @@ cudaError_t encode_cache_map(CUtensorMap* map, const void* base, bool bf16,
                              const KernelParams& p, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return cudaErrorNotSupported;
-  const bool paged = p.block_table != nullptr;
-  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.D), static_cast<cuuint64_t>(p.Hkv),
-                              static_cast<cuuint64_t>(paged ? p.block_size : p.S),
-                              static_cast<cuuint64_t>(paged ? p.num_blocks : p.B)};
-  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.c_hs) * 2,
-                                 static_cast<cuuint64_t>(p.c_ss) * 2,
-                                 static_cast<cuuint64_t>(p.c_bs) * 2};
-  const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
-  const cuuint32_t estride[4] = {1, 1, 1, 1};
-  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        4, const_cast<void*>(base), dims, strides, box, estride,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapDataType type =
+      bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
+  CUresult r;
+  if (p.block_table != nullptr) {
+    // Page pool [num_blocks, block_size, Hkv, 128], contiguous, as
+    // {64 dims, 8 rows, 2 * Hkv half rows, block_size / 8 row groups, pages}: one box holds
+    // a page slice's whole rows of one head (half rows 2g and 2g + 1) as 1024-byte swizzle
+    // atoms [row group][half][8 rows][128 bytes].
+    const cuuint64_t dims[5] = {64, 8, static_cast<cuuint64_t>(2 * p.Hkv),
+                                static_cast<cuuint64_t>(p.block_size / 8),
+                                static_cast<cuuint64_t>(p.num_blocks)};
+    const cuuint64_t strides[4] = {static_cast<cuuint64_t>(p.c_ss) * 2, 128,
+                                   static_cast<cuuint64_t>(p.c_ss) * 16,
+                                   static_cast<cuuint64_t>(p.c_bs) * 2};
+    const cuuint32_t box[5] = {64, 8, 2, static_cast<cuuint32_t>(box_rows / 8), 1};
+    r = fn(map, type, 5, const_cast<void*>(base), dims, strides, box, estride,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // Cache [B, S, Hkv, D] over its own strides as {D, Hkv, S, B}; boxes of 64 dims x 128 rows.
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.D), static_cast<cuuint64_t>(p.Hkv),
+                                static_cast<cuuint64_t>(p.S), static_cast<cuuint64_t>(p.B)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.c_hs) * 2,
+                                   static_cast<cuuint64_t>(p.c_ss) * 2,
+                                   static_cast<cuuint64_t>(p.c_bs) * 2};
+    const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
+    r = fn(map, type, 4, const_cast<void*>(base), dims, strides, box, estride,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 

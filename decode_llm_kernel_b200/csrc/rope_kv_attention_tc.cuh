@@ -230,6 +230,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, int c4, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3), "r"(c4), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled box (box base 1024-aligned).
 __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
@@ -328,6 +338,13 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   pdl_wait();
 
   auto stage_of = [&](int64_t c) { return sh.stage[static_cast<int>(c % kTcStages)]; };
+  // Tile layout in a stage: K in the first 32 KB, V in the second, each as 128-byte swizzle
+  // atoms of 8 rows x 64 dims. Contiguous caches: [half][128 rows] (two 16 KB boxes); paged:
+  // [row group][half][8 rows] (one box per page slice). t_half is the offset of the upper 64
+  // dims, t_group the stride of 8-row groups.
+  const bool paged = p.block_table != nullptr;
+  const uint32_t t_half = paged ? 1024u : kTcBoxBytes;
+  const uint32_t t_group = paged ? 2048u : 1024u;
   auto full_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kTcStages) & 1); };
   auto pair_parity = [&](int64_t c) { return static_cast<uint32_t>((c >> 1) & 1); };
   auto sbuf = [&](int64_t c) { return static_cast<int>(c % kTcSBufs); };
@@ -402,8 +419,8 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       __syncwarp();
     }
     // All 32 lanes walk the units: lane 0 takes and queues them; the TMA boxes of a paged
-    // tile are issued by as many lanes as there are boxes (one instruction for up to 32 page
-    // slices), the four boxes of a contiguous tile by lane 0.
+    // tile are issued by as many lanes as there are boxes (one instruction for the K and V
+    // boxes of up to 16 page slices), the four boxes of a contiguous tile by lane 0.
     int* next_unit = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
     int64_t issued = 0, queued = 0;
     bool ok = true;
@@ -465,25 +482,21 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       for (int tile = 0; tile < w.ntiles; ++tile) {
         const int s = static_cast<int>(issued % kTcStages);
         const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTcTile;
-        // Paged cache: box b of the tile is slice b / 4 of the tile's pages, K lo, K hi, V lo
-        // or V hi by b % 4, issued by lane b % 32. A lane loads the block-table entries of its
-        // boxes before the wait for a free stage, so their latency hides behind it. A tile
-        // starts on a multiple of 128 positions: with pages of at most 128 rows slice i is
-        // page first + i from row 0; a larger page holds the whole tile from row
-        // z - first * bs.
+        // Paged cache: box b of the tile holds the K (b even) or V rows of slice b / 2 of the
+        // tile's pages and is issued by lane b. A lane loads its page's block-table entry
+        // before the wait for a free stage, so the latency hides behind it. A tile starts on
+        // a multiple of 128 positions: with pages of at most 128 rows slice i is page
+        // first + i from row 0; a larger page holds the whole tile from row z - first * bs.
         constexpr int64_t kPastTable = INT64_MIN;   // a page past the request's table
         int nbox = 0, row0 = 0;
-        int64_t blk0 = kPastTable, blk1 = kPastTable;   // pages of boxes lane and lane + 32
+        int64_t blk = kPastTable;
         if (p.block_table != nullptr) {
           nbox = kTcTile / a.box_rows;
           const int64_t first = z / p.block_size;
           row0 = static_cast<int>(z - first * p.block_size);
-          const int64_t i0 = first + (lane >> 2), i1 = first + ((lane + 32) >> 2);
-          const int64_t row_base = w.ri * p.bt_stride;
-          if (lane < 4 * nbox && i0 < p.bt_stride)
-            blk0 = load_index<Idx>(p.block_table, row_base + i0);
-          if (lane + 32 < 4 * nbox && i1 < p.bt_stride)
-            blk1 = load_index<Idx>(p.block_table, row_base + i1);
+          const int64_t i = first + (lane >> 1);
+          if (lane < 2 * nbox && i < p.bt_stride)
+            blk = load_index<Idx>(p.block_table, w.ri * p.bt_stride + i);
         }
         if (issued >= kTcStages)
           ok = __all_sync(0xffffffffu,
@@ -501,27 +514,22 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, w.g, zi, ri, &sh.full[s]);
           }
         } else {
-          // Page slices stack in the stage exactly as one 128-row box would (each is a
-          // multiple of 8 rows, so the 128-byte swizzle pattern continues across them).
+          // A slice's box holds its rows' 1024-byte swizzle atoms in the paged tile layout
+          // [row group][half][8 rows][128 bytes], K at 0 and V at 32 KB.
           if (lane == 0) mbar_expect_tx(&sh.full[s], kTcStageBytes);
           __syncwarp();
-          const int rows = a.box_rows;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int b = lane + 32 * h;
-            if (b >= 4 * nbox) break;
-            const int i = b >> 2, kind = b & 3;
-            const int r0 = i * rows;
-            int64_t blk = h ? blk1 : blk0;
+          if (lane < 2 * nbox) {
+            const int i = lane >> 1, kind = lane & 1;
+            const int r0 = i * a.box_rows;
             if (blk < 0 || blk >= p.num_blocks) {
               // Outside the pool: TMA reads zeros there (coordinate past the last page).
               if (kind == 0 && blk != kPastTable && z + r0 < w.p1 && p.status != nullptr)
                 atomicOr(p.status, kStatusBlock);
               blk = p.num_blocks;
             }
-            const uint32_t off = static_cast<uint32_t>(kind) * kTcBoxBytes +
-                                 static_cast<uint32_t>(r0) * 128u;
-            tma_load_4d(st + off, kind < 2 ? &kmap : &vmap, (kind & 1) * 64, w.g, row0,
+            const uint32_t off = static_cast<uint32_t>(kind) * (kTcStageBytes / 2) +
+                                 static_cast<uint32_t>(r0) * 256u;
+            tma_load_5d(st + off, kind ? &vmap : &kmap, 0, 0, 2 * w.g, row0 >> 3,
                         static_cast<int>(blk), &sh.full[s]);
           }
         }
@@ -827,9 +835,9 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
           const int ch = lane & 15;
           const bool is_v = lane >= 16;
-          uint8_t* base = stage_of(c) + (is_v ? 2 : 0) * kTcBoxBytes + (ch >> 3) * kTcBoxBytes;
-          *reinterpret_cast<uint4*>(base + sw128(r, ch & 7)) =
-              is_v ? sh.vn[qb][ch] : sh.kn[qb][ch];
+          uint8_t* base = stage_of(c) + (is_v ? 2 : 0) * kTcBoxBytes;
+          const uint32_t at = (r >> 3) * t_group + (ch >> 3) * t_half + sw128(r & 7u, ch & 7);
+          *reinterpret_cast<uint4*>(base + at) = is_v ? sh.vn[qb][ch] : sh.kn[qb][ch];
           proxy_fence_shared();
           __syncwarp();
         }
@@ -840,7 +848,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
 #pragma unroll
           for (int ks = 0; ks < kTcDim / 16; ++ks) {
             const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
-            const uint64_t ad = tc_sdesc(kb + (ks >> 2) * kTcBoxBytes + off, 16, 1024);
+            const uint64_t ad = tc_sdesc(kb + (ks >> 2) * t_half + off, 16, t_group);
             const uint64_t bd = tc_sdesc(qaddr + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
             tc_mma(tmem + b * kTcHeads, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
           }
@@ -873,7 +881,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           const uint32_t vb = smem_u32(stage_of(c) + 2 * kTcBoxBytes), pb = smem_u32(sh.pm[b]);
 #pragma unroll
           for (int ks = 0; ks < kTcTile / 16; ++ks) {
-            const uint64_t ad = tc_sdesc(vb + ks * 2048, kTcBoxBytes, 1024);
+            const uint64_t ad = tc_sdesc(vb + ks * 2 * t_group, t_half, t_group);
             const uint64_t bd =
                 tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
             tc_mma(tmem + kTcOCol + b * kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
