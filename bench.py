@@ -67,6 +67,8 @@ def parse_args():
     p.add_argument("--cache-len", type=int, default=0,
                    help="override cache_alloc_len (profiling runs only: keeps a case small)")
     p.add_argument("--launches", type=int, default=400, help="bw mode: timed launches")
+    p.add_argument("--attention-case", choices=ATTENTION_CASES, default=None,
+                   help="attention mode: run this case alone")
     return p.parse_args()
 
 
@@ -477,7 +479,10 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-def attention_probe(device, seed, peak, sets=2, reps=12):
+ATTENTION_CASES = ("full_cache_b32", "ragged_b64", "ragged_b64_paged16", "ragged_b64_paged256")
+
+
+def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
     """Fused RoPE + append + decode attention (one launch, the tensor-core kernel) against the
     append followed by a separate attention read of the same cache, graph-timed.
 
@@ -492,7 +497,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12):
                        table; the baseline is our paged append, then flash_attn's kv-cache
                        decode with the block table, which takes pages of 256 positions).
     Bytes per call: the K and V rows each token attends over (positions 0..pos), plus q, k, v,
-    the appended slots and attn_out. Caches rotate over `sets` sets of 1-2 GiB (> L2)."""
+    the appended slots and attn_out. Caches rotate over `sets` sets of 1-2 GiB (> L2).
+    `only` names one case to run alone (for a profiler capture)."""
     from decode_llm_kernel_b200.cuda import ops
     from decode_llm_kernel_b200.rope_tables import build_rope_tables
     Hq, Hkv, D, S, dt = 32, 8, 128, 8192, torch.bfloat16
@@ -526,6 +532,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12):
         return s0.elapsed_time(s1) * 1e3 / (reps * len(fns))
 
     for label, T, full in (("full_cache_b32", 32, True), ("ragged_b64", 64, False)):
+        if only is not None and label != only:
+            continue
         gen = torch.Generator(device=device).manual_seed(seed)
         st = []
         for _ in range(sets):
@@ -591,6 +599,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12):
 
     # the decode layer over a paged cache: pages shuffled through the block table
     for bs in (16, 256):
+        if only is not None and only != f"ragged_b64_paged{bs}":
+            continue
         T = 64
         gen = torch.Generator(device=device).manual_seed(seed + bs)
         nblk = S // bs
@@ -841,7 +851,8 @@ def main():
             torch.cuda.set_device(local_dev)
             peak, _ = measured_hbm_peak()
             if rank == 0:
-                print(json.dumps(attention_probe(local_dev, args.seed, peak)), flush=True)
+                print(json.dumps(attention_probe(local_dev, args.seed, peak,
+                                                 only=args.attention_case)), flush=True)
         else:
             run_ours(args, world, rank, local)
     finally:
