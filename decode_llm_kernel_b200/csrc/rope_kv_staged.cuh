@@ -68,18 +68,47 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// L2 eviction priority of the bulk copies: 0 none; bit 0: loads (q/k/v are read once) marked
+// evict-first; bit 1: stores (q_out and the cache slots, not read again in the launch) marked
+// evict-first. Measured on B200 (Mistral-shaped batch 4096, 64 GiB caches, 102.8 MB per
+// launch): none 19.73 us, loads only 20.18, stores only 19.93, both 19.28.
+#ifndef DRK_STAGED_L2_HINT
+#define DRK_STAGED_L2_HINT 3
+#endif
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                           uint64_t* bar) {
+#if DRK_STAGED_L2_HINT & 1
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)),
+      "l"(evict_first_policy())
+      : "memory");
+#else
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
       ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+#endif
 }
 
 __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+#if DRK_STAGED_L2_HINT & 2
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;"
+               ::"l"(gmem_dst), "r"(smem_u32(smem_src)), "r"(bytes), "l"(evict_first_policy())
+               : "memory");
+#else
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
                "r"(smem_u32(smem_src)), "r"(bytes)
                : "memory");
+#endif
 }
 
 __device__ __forceinline__ void bulk_commit() {
