@@ -39,6 +39,7 @@ FALLBACK_HBM_GBS = 6650.0
 # ncu captures (profiles/): DRAM bytes read + written per launch
 DECODE32_NCU_DRAM_BYTES = 878848 + 0
 MISTRAL_NCU_DRAM_BYTES = 51522560 + 5620480
+E2E_STEPS_PER_GRAPH = 32
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "achieved HBM GB/s per decode step (algorithmic bytes / device time), with us/call"
 
@@ -349,7 +350,7 @@ def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
 
 def run_ours(args, world, rank, local):
     from decode_llm_kernel_b200 import cuda
-    from decode_llm_kernel_b200.harness.decode_loop import DecodeStep, pinned_like
+    from decode_llm_kernel_b200.harness.decode_loop import DecodeStep, StepInputs, pinned_like
     cuda.require()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -403,12 +404,21 @@ def run_ours(args, world, rank, local):
                         "between the chained launches"}
 
     # end to end: the public API's pipelined host path -- one graph holding `depth` decode
-    # steps, each copying its q/k/v/positions in from pinned host memory and its q_out back
+    # steps, each copying its q/k/v/positions in from pinned host memory and its q_out back.
+    # Graph replays on one stream do not overlap, so each replay starts with a host-to-device
+    # copy alone and ends with a device-to-host copy alone; 32 steps per graph spread that
+    # over more steps (8 steps per graph: 587 us/step against 514 us of copies alone).
     e2e = None
     if not args.no_e2e:
-        depth = min(8, nsets)
-        hosts = [pinned_like(sets[i]) for i in range(depth)]
-        pipe = step.capture_host_pipeline(sets[:depth], hosts)
+        depth = E2E_STEPS_PER_GRAPH
+        hosts = [pinned_like(sets[i % nsets]) for i in range(depth)]
+        # device buffers beyond the bench's own sets: copies of them (the capture's warm-up
+        # runs on the device contents before any host copy)
+        def clone(x):
+            return StepInputs(x.q.clone(), x.k.clone(), x.v.clone(), x.positions.clone(),
+                              x.request_indices.clone())
+        dev_sets = [sets[i] if i < nsets else clone(sets[i % nsets]) for i in range(depth)]
+        pipe = step.capture_host_pipeline(dev_sets, hosts)
         h2d = sum(t.numel() * t.element_size() for t in (hosts[0].q, hosts[0].k, hosts[0].v,
                                                           hosts[0].positions,
                                                           hosts[0].request_indices))
@@ -425,15 +435,35 @@ def run_ours(args, world, rank, local):
         e2e_s = max_over_ranks(time.perf_counter() - t0, world)
         barrier(world)
         e2e_steps = replays * depth
+        # the same copies without the decode work: the step's PCIe bound on this box
+        cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        hq, dq = pipe.host_q_outs[0], pipe.q_outs[0]
+        src, dst = hosts[0], dev_sets[0]
+
+        def copies(n):
+            for _ in range(n):
+                with torch.cuda.stream(cin):
+                    for a, b in ((dst.q, src.q), (dst.k, src.k), (dst.v, src.v),
+                                 (dst.positions, src.positions),
+                                 (dst.request_indices, src.request_indices)):
+                        a.copy_(b, non_blocking=True)
+                with torch.cuda.stream(cout):
+                    hq.copy_(dq, non_blocking=True)
+            torch.cuda.synchronize()
+        copies(3)
+        t0 = time.perf_counter()
+        copies(32)
+        copy_us = (time.perf_counter() - t0) / 32 * 1e6
         e2e = {"value": world * bytes_step * e2e_steps / e2e_s / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "us_per_step": e2e_s / e2e_steps * 1e6, "steps": e2e_steps,
+               "copies_alone_us_per_step": copy_us,
                "path": f"DecodeStep.capture_host_pipeline: {depth} steps per graph, each "
                        "copying q/k/v/positions in from pinned host memory, running the 32 "
                        "fused launches and copying q_out back; copies on their own streams; "
                        "wall clock with a sync on both sides"}
         pipe.release()
-        del hosts
+        del hosts, dev_sets
 
     floor = None if args.no_floor else launch_floor(stream, w.layers)
     ladder = None if (args.no_ladder or rank != 0) else operator_ladder(device, args.seed)
