@@ -433,12 +433,17 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       ++queued;
     };
     // The next unit with work: lane 0 takes it, reporting bad indices on the way, and the
-    // warp gets its index, position and request index; t = -1 when none is left.
+    // warp gets its index, position and request index; t = -1 when none is left. A CTA's
+    // first unit is its own index (the grid never exceeds the units); later ones come from
+    // the counter, offset by the grid.
+    bool first_take = true;
     auto take = [&](int64_t& index) {
       int64_t tu = -1, tpos = 0, tri = 0;
       if (lane == 0) {
         while (true) {
-          int64_t u = atomicAdd(next_unit, 1);
+          int64_t u = first_take ? static_cast<int64_t>(blockIdx.x)
+                                 : static_cast<int64_t>(gridDim.x) + atomicAdd(next_unit, 1);
+          first_take = false;
           if (u >= units) break;
           if (sorted) {
             const int64_t r = u / per_token;
@@ -477,8 +482,15 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     if (lane == 0 && next.t >= 0) enqueue(next_index, next.pos, next.ri);
     while (ok && next.t >= 0) {
       const TcUnit w = next;
-      next = take(next_index);
-      if (lane == 0 && next.t >= 0) enqueue(next_index, next.pos, next.ri);
+      // The unit after w is taken during w's first tile: before the wait for a free stage
+      // when the ring is full, after the tile's loads are issued while it is still filling
+      // (a CTA's first tiles do not wait for a take).
+      bool need_next = true;
+      auto take_next = [&]() {
+        next = take(next_index);
+        if (lane == 0 && next.t >= 0) enqueue(next_index, next.pos, next.ri);
+        need_next = false;
+      };
       for (int tile = 0; tile < w.ntiles; ++tile) {
         const int s = static_cast<int>(issued % kTcStages);
         const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTcTile;
@@ -498,6 +510,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           if (lane < 2 * nbox && i < p.bt_stride)
             blk = load_index<Idx>(p.block_table, w.ri * p.bt_stride + i);
         }
+        if (need_next && issued >= kTcStages) take_next();
         if (issued >= kTcStages)
           ok = __all_sync(0xffffffffu,
                           tc_wait(&sh.empty[s],
@@ -534,7 +547,9 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           }
         }
         ++issued;
+        if (need_next) take_next();
       }
+      if (ok && need_next) take_next();
     }
     if (lane == 0) {
       enqueue(-1, 0, 0);
