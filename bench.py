@@ -466,6 +466,14 @@ def run_ours(args, world, rank, local):
         del hosts, dev_sets
 
     floor = None if args.no_floor else launch_floor(stream, w.layers)
+    if floor is not None:
+        # The layer launch against the graph-node floor: without PDL (an empty kernel per graph
+        # node, the floor the reference measures with no PDL in its graphs) and with PDL (the
+        # chain this step runs).
+        us_launch = per_launch_s * 1e6
+        floor["layer_us"] = us_launch
+        floor["layer_vs_graph_node"] = us_launch / floor["graph_us_per_node"]
+        floor["layer_vs_graph_node_pdl"] = us_launch / floor["graph_us_per_node_pdl"]
     ladder = None if (args.no_ladder or rank != 0) else operator_ladder(device, args.seed)
     del captured, sets, k_caches, v_caches, step
     torch.cuda.empty_cache()
