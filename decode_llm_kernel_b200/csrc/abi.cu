@@ -660,12 +660,17 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
   int64_t chunk = ao.chunk;
   if (chunk < 0) invalid("chunk must be >= 0, got ", chunk);
   if (chunk == 0) {
+    // About one wave of resident CTAs: a CTA streams its chunk at a latency-bound rate, so
+    // more, shorter chunks finish sooner until the grid fills the SMs, while each extra chunk
+    // costs a partial and a share of the merge. The power of two nearest to
+    // units * S / (SMs x resident CTAs per SM), within [128, 1024] (B200 sweeps of batch
+    // 1..32, 2048..8192 positions, GQA and MQA: the fastest chunk or within 11% of it).
     const int64_t units = std::max<int64_t>(1, T * Hkv * pl.nhb);
-    const int64_t slots =
-        2LL * drk::device_sm_count(device) * attention_ctas_per_sm(hpb, es);
-    const int64_t want = std::max<int64_t>(1, units * std::max<int64_t>(S, 1) / slots);
-    chunk = 64;
-    while (chunk * 2 <= want && chunk < 1024) chunk <<= 1;
+    const int64_t slots = static_cast<int64_t>(drk::device_sm_count(device)) *
+                          attention_ctas_per_sm(hpb, es);
+    const double want = static_cast<double>(units) * std::max<int64_t>(S, 1) / slots;
+    chunk = 128;
+    while (chunk < 1024 && want >= chunk * 1.41421356) chunk <<= 1;
   }
   pl.chunk = chunk;
   pl.max_chunks = std::max<int64_t>(1, (S + chunk - 1) / chunk);

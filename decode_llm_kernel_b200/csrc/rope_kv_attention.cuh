@@ -316,18 +316,49 @@ rope_kv_attention_kernel(const __grid_constant__ KernelParams p,
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int idx = tid; idx < nh * p.D; idx += kAttnThreads) {
-    const int hh = idx / p.D, d = idx - hh * p.D;
+  // The last chunk to arrive merges. Warp w takes heads w, w + kAttnWarps, ...; a lane holds
+  // chunk cb + lane of each batch of 32 for the (m, l) reduction and dims lane + 32 i for the
+  // sums, with 16 chunks' partial loads in flight at once.
+  for (int hh = warp; hh < nh; hh += kAttnWarps) {
     const float* hw = ws + hh * ws_head;
-    float M = -INFINITY;
-    for (int c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(hw + c * row + p.D));
-    float L = 0.f, O = 0.f;
-    for (int c = 0; c < nchunks; ++c) {
-      const float w = exp2f(__ldcg(hw + c * row + p.D) - M);
-      L = fmaf(__ldcg(hw + c * row + p.D + 1), w, L);
-      O = fmaf(__ldcg(hw + c * row + d), w, O);
+    float M = -INFINITY, Ls = 0.f, O[VL];
+#pragma unroll
+    for (int i = 0; i < VL; ++i) O[i] = 0.f;
+    for (int cb = 0; cb < nchunks; cb += 32) {
+      const int c = cb + lane;
+      const bool in = c < nchunks;
+      const float mc = in ? __ldcg(hw + static_cast<int64_t>(c) * row + p.D) : -INFINITY;
+      const float lc = in ? __ldcg(hw + static_cast<int64_t>(c) * row + p.D + 1) : 0.f;
+      float mg = fmaxf(M, mc);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+        mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+      const float rescale = exp2f(M - mg);
+      const float wc = in ? exp2f(mc - mg) : 0.f;
+      float lg = lc * wc;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
+      Ls = fmaf(Ls, rescale, lg);
+#pragma unroll
+      for (int i = 0; i < VL; ++i) O[i] *= rescale;
+      const int nc = min(32, nchunks - cb);
+#pragma unroll 4
+      for (int j = 0; j < nc; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, wc, j);
+        const float* cp = hw + static_cast<int64_t>(cb + j) * row;
+#pragma unroll
+        for (int i = 0; i < VL; ++i) {
+          const int d = lane + 32 * i;
+          if (d < p.D) O[i] = fmaf(__ldcg(cp + d), wj, O[i]);
+        }
+      }
+      M = mg;
     }
-    out[hh * static_cast<int64_t>(p.D) + d] = E::from_f(O / L);
+#pragma unroll
+    for (int i = 0; i < VL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < p.D) out[hh * static_cast<int64_t>(p.D) + d] = E::from_f(O[i] / Ls);
+    }
   }
   if (tid == 0) *counter = 0;
 }
