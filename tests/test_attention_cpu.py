@@ -105,3 +105,21 @@ def test_zero_tokens_is_a_no_op(lib):
         *[ctypes.byref(d) for d in ds], None, ctypes.byref(do), None, None, ctypes.c_size_t(0),
         None, None, None)
     assert rc == 0, lib.drk_last_error()
+
+
+def test_cuda_core_auto_chunk_fills_one_wave(lib):
+    """Auto chunk of the CUDA-core kernel: the power of two nearest units * S / (SMs x CTAs
+    per SM), within [128, 1024]. Without a GPU the plan sees one SM; one head per CTA of 16-bit
+    data leaves 8 CTAs on it."""
+    # 4 units x 600 positions / 8 slots = 300 -> 256 (3 chunks)
+    assert ws_bytes(lib, 1, 4, 4, 96, 600) == expected(1, 4, 4, 96, 600, 256, 1)
+    # 4 x 100 / 8 = 50 -> the 128 floor (one chunk)
+    assert ws_bytes(lib, 1, 4, 4, 96, 100) == expected(1, 4, 4, 96, 100, 128, 1)
+    # 4 x 3000 / 8 = 1500 -> the 1024 ceiling (3 chunks)
+    assert ws_bytes(lib, 1, 4, 4, 96, 3000) == expected(1, 4, 4, 96, 3000, 1024, 1)
+
+
+def test_tensor_core_auto_chunk_prefers_fewer_merges(lib):
+    """On one SM every unit is its own round, so the cost model takes the whole cache as one
+    chunk (no merge) rather than 512-position chunks."""
+    assert ws_bytes(lib, 2, 32, 8, 128, 1000) == expected(2, 32, 8, 128, 1000, 1024, 1, True)
