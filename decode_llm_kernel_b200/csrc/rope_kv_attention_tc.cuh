@@ -124,6 +124,8 @@ struct TcShared {
                                                    // producer; unit -1 ends the walk
   uint64_t uq_bar[kTcQueue];                       // a queue slot was written (producer)
   uint16_t order[kTcSortMax];                      // tokens, longest first (producer)
+  int64_t fin[3];                                  // the CTA's last unit, if it merges
+  int fin_merge;
   uint32_t tmem_base;
 };
 constexpr size_t kTcSmemBytes = sizeof(TcShared) + 1024;   // + alignment slack
@@ -302,6 +304,10 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   const int warp = tid >> 5, lane = tid & 31;
 
   pdl_launch_dependents();
+  if (tid == kTcProducerWarp * 32) {   // the maps are kernel parameters: fetch them early
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
+  }
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&sh.full[s], 1);
@@ -320,6 +326,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     mbar_init(&sh.ep_full, kTcThreads);
     mbar_init(&sh.ep_empty, 1);
     for (int i = 0; i < kTcQueue; ++i) mbar_init(&sh.uq_bar[i], 1);
+    sh.fin_merge = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // P rows of heads past HR are never written per tile: zero both buffers once.
@@ -355,6 +362,55 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   };
   const int half_r = p.R >> 1;
   const int row = p.D + 2;
+
+  // Merges every chunk of the unit's (token, KV head, head block): a warp takes heads
+  // h_first, h_first + h_step, ...; the (m, l) of 32 chunks at a time go into lanes, then each
+  // lane folds its 4 dims of each chunk of the group with the group's loads in flight together.
+  auto merge_unit = [&](const TcUnit& w, int h_first, int h_step) {
+    __threadfence();
+    const int h0 = w.g * a.group + w.hb * kTcHeads;
+    const int nh = min(HR, a.group - w.hb * kTcHeads);
+    const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
+    const float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
+    const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
+    raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+    for (int h = h_first; h < nh; h += h_step) {
+      const float* hw = ws + h * ws_head;
+      float M = -INFINITY, Ls = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int cb = 0; cb < nchunks; cb += 32) {
+        const int c = cb + lane;
+        const float mc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim)
+                                     : -INFINITY;
+        const float lc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim + 1)
+                                     : 0.f;
+        float mg = fmaxf(M, mc);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+          mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+        const float rescale = exp2f(M - mg);
+        const float wc = c < nchunks ? exp2f(mc - mg) : 0.f;
+        float lg = lc * wc;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
+        Ls = fmaf(Ls, rescale, lg);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) O[i] *= rescale;
+        const int nc = min(32, nchunks - cb);
+#pragma unroll 8
+        for (int j = 0; j < nc; ++j) {
+          const float wj = __shfl_sync(0xffffffffu, wc, j);
+          const float* cp = hw + static_cast<int64_t>(cb + j) * row + lane;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cp + 32 * i), wj, O[i]);
+        }
+        M = mg;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / Ls);
+    }
+    if (lane == 0 && h_first == 0) a.counters[(w.t * p.Hkv + w.g) * a.nhb + w.hb] = 0;
+  };
 
   if (warp == kTcProducerWarp) {
     // ---- producer: order the tokens longest first, then take units, queue them, and refill
@@ -743,58 +799,13 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         merge = last != 0;
       return true;
     };
-    // Merges every chunk of the unit's (token, KV head, head block): the (m, l) of 32 chunks at
-    // a time into lanes, then each lane folds its 4 dims of each chunk of the group with the
-    // group's loads in flight together.
-    auto merge_unit = [&](const TcUnit& w) {
-      __threadfence();
-      const int h0 = w.g * a.group + w.hb * kTcHeads;
-      const int nh = min(HR, a.group - w.hb * kTcHeads);
-      const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
-      const float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
-      const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
-      raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
-      for (int h = 0; h < nh; ++h) {
-        const float* hw = ws + h * ws_head;
-        float M = -INFINITY, Ls = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int cb = 0; cb < nchunks; cb += 32) {
-          const int c = cb + lane;
-          const float mc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim)
-                                       : -INFINITY;
-          const float lc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim + 1)
-                                       : 0.f;
-          float mg = fmaxf(M, mc);
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1)
-            mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
-          const float rescale = exp2f(M - mg);
-          const float wc = c < nchunks ? exp2f(mc - mg) : 0.f;
-          float lg = lc * wc;
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
-          Ls = fmaf(Ls, rescale, lg);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) O[i] *= rescale;
-          const int nc = min(32, nchunks - cb);
-#pragma unroll 8
-          for (int j = 0; j < nc; ++j) {
-            const float wj = __shfl_sync(0xffffffffu, wc, j);
-            const float* cp = hw + static_cast<int64_t>(cb + j) * row + lane;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cp + 32 * i), wj, O[i]);
-          }
-          M = mg;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / Ls);
-      }
-      if (lane == 0) a.counters[(w.t * p.Hkv + w.g) * a.nhb + w.hb] = 0;
-    };
     // Per queued unit k: prepare unit k, then finish unit k - 1 (its merge too, if it
     // arrived last of its chunks).
+    // The CTA's last unit, when it arrives last of its chunks, is merged after every role has
+    // finished, by all eight warps (a warp per head) instead of this one.
     bool ok = true;
     TcUnit prev{};
+    int64_t prev_msg[3] = {0, 0, 0};
     for (int64_t k = 0; ok; ++k) {
       ok = __all_sync(0xffffffffu, queue_wait(k));
       if (!ok) break;
@@ -810,10 +821,22 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         bool merge = false;
         ok = epilogue_fast(k - 1, prev, merge);
         if (!ok) break;
-        if (merge) merge_unit(prev);
+        if (merge && last_unit) {
+          if (lane == 0) {
+            sh.fin[0] = prev_msg[0];
+            sh.fin[1] = prev_msg[1];
+            sh.fin[2] = prev_msg[2];
+            sh.fin_merge = 1;
+          }
+        } else if (merge) {
+          merge_unit(prev, 0, 1);
+        }
       }
       if (last_unit) break;
       prev = w;
+      prev_msg[0] = msg[0];
+      prev_msg[1] = msg[1];
+      prev_msg[2] = msg[2];
     }
     if (!ok && lane == 0 && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
   } else if (warp == kTcMmaWarp) {
@@ -1060,6 +1083,8 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTcTmemCols) : "memory");
   }
+  if (sh.fin_merge) merge_unit(tc_unit_at(p, a, sh.fin[0], sh.fin[1], sh.fin[2]), warp,
+                               kTcBlock / 32);
 }
 
 }  // namespace drk
