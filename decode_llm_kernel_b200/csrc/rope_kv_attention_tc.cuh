@@ -631,24 +631,35 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         uint8_t* qs = sh.q[qb];
         if (a.q_vec) {
           // Full rotary, 16-byte rows: item = (head, 8-dim chunk of the first half); both halves
-          // of the rotate_half pair from one lane.
-          for (int item = lane; item < kTcHeads * 8; item += 32) {
-            const int hh = item >> 3, c = item & 7;
-            uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+          // of the rotate_half pair from one lane. A lane's items share their chunk c (and its
+          // cos/sin), for heads lane / 8 + 4 i; every load is issued before the first store.
+          const int c = lane & 7;
+          const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
+          const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
+          uint4 xs1[4], xs2[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int hh = (lane >> 3) + 4 * r;
+            xs1[r] = xs2[r] = make_uint4(0u, 0u, 0u, 0u);
             if (hh < nh) {
               const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
                                 static_cast<int64_t>(h0 + hh) * p.q_hs;
-              const uint4 x1 = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-              const uint4 x2 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
-              const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
-              const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
-              const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
-              const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
-              const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-              const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+              xs1[r] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+              xs2[r] = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
+            }
+          }
+          const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int hh = (lane >> 3) + 4 * r;
+            uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+            if (hh < nh) {
               float f1[8], f2[8];
-              unpack16<E>(x1, f1);
-              unpack16<E>(x2, f2);
+              unpack16<E>(xs1[r], f1);
+              unpack16<E>(xs2[r], f2);
               uint32_t wl[4], wh[4];
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
@@ -725,19 +736,37 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
               if (lane == 0 && w.hb == 0 && p.status != nullptr) atomicOr(p.status, kStatusBlock);
             }
           }
-          for (int d = lane; d < kTcDim; d += 32) {
-            raw kr = krow[d];
+          // Dims lane + 32 j: every load is issued before the first store (the cache append
+          // could alias the sources as far as the compiler knows).
+          raw kx[4], k1[4], k2[4], vx[4];
+          float cx[4], sx[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int d = lane + 32 * j;
+            const int i = d < half_r ? d : d - half_r;
+            kx[j] = krow[d];
+            vx[j] = vrow[d];
+            k1[j] = k2[j] = kx[j];
+            cx[j] = sx[j] = 0.f;
             if (d < p.R) {
-              const int i = d < half_r ? d : d - half_r;
-              kr = E::from_f(rotate_one(E::to_f(krow[i]), E::to_f(krow[i + half_r]),
-                                        __ldg(crow + i), __ldg(srow + i), d < half_r));
+              k1[j] = krow[i];
+              k2[j] = krow[i + half_r];
+              cx[j] = __ldg(crow + i);
+              sx[j] = __ldg(srow + i);
             }
-            const raw vr = vrow[d];
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int d = lane + 32 * j;
+            raw kr = kx[j];
+            if (d < p.R)
+              kr = E::from_f(rotate_one(E::to_f(k1[j]), E::to_f(k2[j]), cx[j], sx[j],
+                                        d < half_r));
             kn[d] = kr;
-            vn[d] = vr;
+            vn[d] = vx[j];
             if (w.hb == 0 && slot >= 0) {
               reinterpret_cast<raw*>(p.k_dst)[slot + d] = kr;
-              reinterpret_cast<raw*>(p.v_dst)[slot + d] = vr;
+              reinterpret_cast<raw*>(p.v_dst)[slot + d] = vx[j];
             }
           }
         }
