@@ -12,11 +12,22 @@ half-rows of cos/sin, writes of q_out and the K and V cache slots) / device time
 whole job's total over all ranks. us_per_step and us_per_call (per layer launch) are reported
 beside it.
 
+Every timed configuration is checked after its timed region: one sampled input set's call is
+issued again and its q_out and K/V slots are compared bit for bit with a PyTorch fp32
+restatement on the GPU ("parity" keys).
+
+Beside this build's numbers the line carries, at N=1: the reference's own kernels rebuilt for
+sm_100a on the same workloads (`reference_gpu`, from baseline/_ref, installed by
+baseline/build_ref.py), the reference's PyTorch CPU path on the host cores
+(`cpu_baseline_torch`) and the C port of it (`cpu_baseline`); at every N the strong-scaling
+records of the two sharded workloads (`strong_scaling`).
+
 Launch: python bench.py [--gpus N --steps K --warmup W]; for N > 1 under torchrun, one rank per
 GPU, each owning its own batch shard and caches (weak scaling, no collective on the data path;
 NCCL only for the barrier and the max-over-ranks time).
-`--impl reference` times the reference's CPU algorithm (the CPU oracle port, all host threads)
-on the same workload and prints the same JSON line with impl=reference.
+`--impl reference` times the reference's CPU implementation (its PyTorch oracle, all host
+threads; the C port when the reference is not installed) on the same workload and prints the
+same JSON line with impl=reference.
 """
 import argparse
 import json
@@ -26,6 +37,8 @@ import subprocess
 import sys
 import threading
 import time
+import types
+from dataclasses import replace
 
 import torch
 
@@ -60,6 +73,8 @@ def parse_args():
                    help="skip the per-call operator ladder at batch 8")
     p.add_argument("--no-attention", action="store_true",
                    help="skip the fused append + decode attention measurement")
+    p.add_argument("--no-reference-gpu", action="store_true",
+                   help="skip the reference's own kernels (baseline/_ref) on the GPU")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--mode", choices=["full", "bw", "attention"], default="full",
@@ -258,17 +273,99 @@ def time_graph_steps(captured, steps, stream):
     return start.elapsed_time(end)
 
 
-def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters=400):
-    """One fused launch per call of a single-layer workload (sharded for this rank), input sets
-    rotated so they exceed 3x L2, launches replayed from a CUDA graph with programmatic
-    dependent launch between them (no launch writes another's positions, indices or tables),
-    device time per launch from CUDA events, max over ranks. cache_len > 0 shrinks the caches
-    (same per-token work) for profiling runs."""
-    from dataclasses import replace
+# ------------------------------------------------------------------------- parity of timed runs
+
+def rope_torch(x, pos, cos, sin, rotary):
+    """RoPE of x [T, H, D] at positions pos [T], computed with PyTorch on x's device: fp32, each
+    multiply and each add a separate elementwise op (each rounded once, never a fused
+    multiply-add), one rounding to x's dtype; dims past `rotary` are copied. This is the
+    arithmetic the reference specifies, evaluated independently of the kernels."""
+    half = rotary // 2
+    xf = x[..., :rotary].float()
+    idx = pos.long()
+    c = cos[idx, :rotary].unsqueeze(1)
+    s = sin[idx, :rotary].unsqueeze(1)
+    turned = torch.cat((-xf[..., half:], xf[..., :half]), dim=-1)
+    y = (xf * c + turned * s).to(x.dtype)
+    return torch.cat((y, x[..., rotary:]), dim=-1) if rotary < x.shape[-1] else y
+
+
+def _bits(t):
+    return t.contiguous().view({1: torch.uint8, 2: torch.int16, 4: torch.int32,
+                                8: torch.int64}[t.element_size()])
+
+
+def differing(a, b):
+    """Elements whose bits differ (0 means bit-exact)."""
+    return int((_bits(a) != _bits(b)).sum().item())
+
+
+def check_call(q, k, v, pos, ri, cos, sin, q_out, k_cache, v_cache, rotary):
+    """One call's outputs against rope_torch: q_out, and the K and V slots [ri, pos] of the
+    caches (which must hold this call's writes). Returns mismatching element counts."""
+    idx_r, idx_p = ri.long(), pos.long()
+    return {"q": differing(q_out, rope_torch(q, pos, cos, sin, rotary)),
+            "k_slots": differing(k_cache[idx_r, idx_p], rope_torch(k, pos, cos, sin, rotary)),
+            "v_slots": differing(v_cache[idx_r, idx_p], v)}
+
+
+def parity_label(counts):
+    total = sum(counts.values())
+    return "bit-exact" if total == 0 else f"MISMATCH {counts}"
+
+
+PARITY_NOTE = ("after the timed region one sampled input set's call is issued again; its q_out "
+               "and its K/V cache slots are compared bit for bit with a PyTorch fp32 "
+               "restatement on the GPU (separately rounded multiplies and adds)")
+
+
+# ------------------------------------------------------------------------- the reference
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def load_reference():
+    """The reference project installed by baseline/build_ref.py: its ops over its own CUDA
+    extension rebuilt for sm_100a, and its PyTorch oracle. Raises RuntimeError(reason) when it
+    is not installed or does not load."""
+    if not os.path.isdir(os.path.join(REF_DIR, "decode_kernels")):
+        raise RuntimeError("the reference is not installed (python baseline/build_ref.py)")
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    from decode_kernels import cuda as ref_cuda
+    from decode_kernels.cuda import ops as ref_ops
+    from decode_kernels.reference import fused_rope_kv_append_ref
+    return types.SimpleNamespace(ops=ref_ops, oracle=fused_rope_kv_append_ref,
+                                 gpu_ok=ref_cuda.is_available(),
+                                 gpu_reason=ref_cuda.unavailable_reason(),
+                                 ext_path=ref_cuda.extension_path())
+
+
+def reference_or_reason():
+    try:
+        return load_reference(), None
+    except Exception as e:  # noqa: BLE001 -- reported in the line, never fatal
+        return None, f"{type(e).__name__}: {e}"
+
+
+# ------------------------------------------------------------------------- single-layer probes
+
+def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters=400,
+                       impl="ours", rung="fused", ref=None):
+    """One launch per call of a single-layer workload (sharded for this rank), input sets
+    rotated so they exceed 3x L2, calls replayed from a CUDA graph, device time per call from
+    CUDA events, max over ranks. impl "ours": the fused op with programmatic dependent launch
+    between calls (no call writes another's positions, indices or tables); impl "reference":
+    the reference's own fused (or separate) op over its sm_100a build, same inputs, same graph
+    replay. cache_len > 0 shrinks the caches (same per-token work) for profiling runs."""
     from decode_llm_kernel_b200.cuda import ops
     w = WORKLOADS[name].shard_for(rank, world)
     if cache_len:
         w = replace(w, cache_alloc_len=cache_len)
+    rot = w.rotary_dim if w.rotary_dim and w.rotary_dim != w.head_dim else 0
+    if impl == "reference" and rot:
+        return {"workload": name, "unsupported": "the reference has no partial rotary: its "
+                "tables must be [max_position, head_dim] (csrc/kernel_common.cuh:70-72)"}
     g = torch.Generator(device=device).manual_seed(seed + 17)
     shape = (w.batch, w.cache_alloc_len, w.num_kv_heads, w.head_dim)
     kc = normal_(torch.empty(shape, dtype=w.dtype, device=device), g)
@@ -288,14 +385,21 @@ def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters
                      torch.arange(w.batch, device=device, dtype=idx),
                      torch.empty(w.batch, w.num_q_heads, w.head_dim, dtype=w.dtype,
                                  device=device)))
-    rot = w.rotary_dim if w.rotary_dim and w.rotary_dim != w.head_dim else 0
 
-    def call(i):
-        q, k, v, p, ri, qo = sets[i % nsets]
-        ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo, pdl=True,
-                                    rotary_dim=rot)
+    if impl == "ours":
+        def call(i):
+            q, k, v, p, ri, qo = sets[i % nsets]
+            ops.fused_rope_kv_append_ex(q, k, v, p, cos, sin, kc, vc, ri, q_out=qo, pdl=True,
+                                        rotary_dim=rot)
+            return qo
+    else:
+        fn = ref.ops.fused_rope_kv_append if rung == "fused" else ref.ops.separate_rope_kv_append
 
-    # Launches are replayed from a CUDA graph so host call overhead cannot pace the GPU.
+        def call(i):
+            q, k, v, p, ri, _ = sets[i % nsets]
+            return fn(q, k, v, p, cos, sin, kc, vc, ri)
+
+    # Calls are replayed from a CUDA graph so host call overhead cannot pace the GPU.
     for i in range(nsets):
         call(i)
     torch.cuda.synchronize()
@@ -321,19 +425,27 @@ def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters
     iters = reps * per_graph
     per_launch_s = ms / 1e3 / iters
     del graph
+    # parity of the timed configuration: set 0 once more, then its outputs and slots
+    q0, k0, v0, p0, r0, _ = sets[0]
+    out0 = call(0)
+    torch.cuda.synchronize()
+    counts = check_call(q0, k0, v0, p0, r0, cos, sin, out0, kc, vc, w.rotary)
     gbs_rank = w.bytes_per_call() / per_launch_s / 1e9
-    staged = w.batch >= 512
-    out = {"workload": name, "shard": w.shard, "batch_per_gpu": w.batch,
+    if impl == "ours":
+        kernel = ("drk::rope_kv_staged_kernel (TMA bulk copies, 3-stage mbarrier pipeline)"
+                  if w.batch >= 512 else "drk::rope_kv_kernel (register kernel)")
+    else:
+        kernel = f"reference cuda_{rung} (its csrc kernels rebuilt for sm_100a)"
+    out = {"workload": name, "impl": impl, "shard": w.shard, "batch_per_gpu": w.batch,
            "q_heads_per_gpu": w.num_q_heads, "kv_heads_per_gpu": w.num_kv_heads,
-           "head_dim": w.head_dim, "rotary_dim": w.rotary_dim or w.head_dim,
-           "dtype": w.dtype_label, "cache_alloc_len": w.cache_alloc_len, "launches": iters,
-           "pdl": True,
-           "kernel": ("drk::rope_kv_staged_kernel (TMA bulk copies, 3-stage mbarrier pipeline)"
-                      if staged else "drk::rope_kv_kernel (register kernel)"),
+           "head_dim": w.head_dim, "rotary_dim": w.rotary, "dtype": w.dtype_label,
+           "cache_alloc_len": w.cache_alloc_len, "launches": iters,
+           "pdl": impl == "ours", "kernel": kernel,
            "bytes_per_launch": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
            "achieved_gbs_per_gpu": gbs_rank, "frac_of_peak": gbs_rank / peak,
-           "aggregate_gbs": gbs_rank * world, "input_sets": nsets}
-    if name == "mistral_b4096" and world == 1:
+           "aggregate_gbs": gbs_rank * world, "input_sets": nsets,
+           "parity": parity_label(counts)}
+    if name == "mistral_b4096" and world == 1 and impl == "ours":
         out["traffic"] = MISTRAL_NCU_DRAM_BYTES
         out["traffic_note"] = ("ncu, caches cut to 128 positions: reads 51.5 MB = the "
                                "algorithmic reads; 5.6 MB of the 51.4 MB of writes reach DRAM "
@@ -348,6 +460,74 @@ def bandwidth_probe(world, rank, device, seed, peak, cache_len=0, iters=400):
     return single_layer_probe("mistral_b4096", world, rank, device, seed, peak, cache_len, iters)
 
 
+def reference_gpu(device, seed, peak, ours):
+    """The reference's own kernels (cuda_fused and cuda_separate, its csrc rebuilt for sm_100a
+    by baseline/build_ref.py) on the single-layer workloads, with the inputs, graph replay and
+    timing of this build's arm; `ours` maps each workload to this build's probe result."""
+    ref, why = reference_or_reason()
+    if ref is None or not ref.gpu_ok:
+        return {"unavailable": why or ref.gpu_reason}
+    out = {"extension": os.path.relpath(ref.ext_path, ROOT)}
+    for name in ("llama3_8b_b8", "llama3_70b_tp", "mistral_b4096", "phi2_partial"):
+        row = {}
+        for rung in ("fused", "separate"):
+            r = single_layer_probe(name, 1, 0, device, seed, peak, impl="reference", rung=rung,
+                                   ref=ref)
+            if "unsupported" in r:
+                row = r
+                break
+            row[f"cuda_{rung}"] = {k: r[k] for k in ("us_per_launch", "achieved_gbs_per_gpu",
+                                                      "frac_of_peak", "parity")}
+        mine = ours.get(name)
+        if mine and "cuda_fused" in row:
+            row["ours_us"] = mine["us_per_launch"]
+            row["speedup_vs_reference_fused"] = row["cuda_fused"]["us_per_launch"] / mine["us_per_launch"]
+            row["speedup_vs_reference_separate"] = (row["cuda_separate"]["us_per_launch"]
+                                                    / mine["us_per_launch"])
+        out[name] = row
+    return out
+
+
+def reference_decode_step(ref, k_caches, v_caches, sets, cos, sin, steps, warmup, w):
+    """The reference's fused op as the 32-layer decode step (one graph of 32 launches per
+    input set, no programmatic dependent launch: the reference's kernel has none), over the
+    same caches and input sets as this build's step."""
+    fn = ref.ops.fused_rope_kv_append
+    graphs, outs = [], []
+    for s in sets:
+        for layer in range(w.layers):
+            fn(s.q[layer], s.k[layer], s.v[layer], s.positions, cos, sin, k_caches[layer],
+               v_caches[layer], s.request_indices)
+    torch.cuda.synchronize()
+    for s in sets:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            o = [fn(s.q[layer], s.k[layer], s.v[layer], s.positions, cos, sin, k_caches[layer],
+                    v_caches[layer], s.request_indices) for layer in range(w.layers)]
+        graphs.append(g)
+        outs.append(o)
+    for i in range(warmup):
+        graphs[i % len(graphs)].replay()
+    stream = torch.cuda.current_stream()
+    ms = time_graph_steps(graphs, steps, stream)
+    graphs[0].replay()
+    torch.cuda.synchronize()
+    s0 = sets[0]
+    bad = 0
+    for layer in range(w.layers):
+        counts = check_call(s0.q[layer], s0.k[layer], s0.v[layer], s0.positions,
+                            s0.request_indices, cos, sin, outs[0][layer], k_caches[layer],
+                            v_caches[layer], w.rotary)
+        bad += sum(counts.values())
+    del graphs, outs
+    per_step_us = ms * 1e3 / steps
+    return {"us_per_step": per_step_us, "us_per_layer": per_step_us / w.layers,
+            "achieved_gbs": w.bytes_per_step() / (per_step_us * 1e-6) / 1e9,
+            "parity": "bit-exact" if bad == 0 else f"MISMATCH {bad} elements",
+            "kernel": "reference cuda_fused (its csrc kernel rebuilt for sm_100a), 32 launches "
+                      "per graph"}
+
+
 def run_ours(args, world, rank, local):
     from decode_llm_kernel_b200 import cuda
     from decode_llm_kernel_b200.harness.decode_loop import DecodeStep, StepInputs, pinned_like
@@ -357,7 +537,6 @@ def run_ours(args, world, rank, local):
     w = WORKLOADS[args.workload].shard_for(rank, world)
     if args.cache_len:
         # profiling runs only: smaller caches, same per-token work (one slot per token)
-        from dataclasses import replace
         w = replace(w, cache_alloc_len=args.cache_len)
     peak, peak_src = measured_hbm_peak()
     cos, sin = build_tables(w, device)
@@ -384,6 +563,18 @@ def run_ours(args, world, rank, local):
     clocks = sampler.summary(t_load0, t_timed1)
     cuda.check_status(local)
 
+    # parity of the timed step: input set 0 replayed once more, every layer checked
+    captured[0].replay()
+    torch.cuda.synchronize()
+    s0, bad = sets[0], {"q": 0, "k_slots": 0, "v_slots": 0}
+    for layer in range(w.layers):
+        counts = check_call(s0.q[layer], s0.k[layer], s0.v[layer], s0.positions,
+                            s0.request_indices, cos, sin, captured[0].q_out[layer],
+                            k_caches[layer], v_caches[layer], w.rotary)
+        for key in bad:
+            bad[key] += counts[key]
+    parity = {"result": parity_label(bad), "layers_checked": w.layers, "how": PARITY_NOTE}
+
     per_step_s = ms_max / 1e3 / args.steps
     bytes_step = w.bytes_per_step()
     value = world * bytes_step / per_step_s / 1e9
@@ -396,8 +587,9 @@ def run_ours(args, world, rank, local):
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                 "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per launch "
-                                "(878,848 + 0): the reads of q/k/v plus table and slot lines; "
-                                "the launch's 0.8 MB of writes stay in L2 until later",
+                                "(878,848 + 0) from profiles/rope_kv_kernel_decode32_bf16.md: "
+                                "the reads of q/k/v plus table and slot lines; the launch's "
+                                "0.8 MB of writes stay in L2 until later",
                 "kernel": "drk::rope_kv_kernel<BF16, int, 16, kFused, kStrided, 1 row/thread>",
                 "per_launch_bytes": w.bytes_per_call(), "us_per_launch": per_launch_s * 1e6,
                 "note": "average launch = graph step time / layers, so it includes the gaps "
@@ -435,6 +627,10 @@ def run_ours(args, world, rank, local):
         e2e_s = max_over_ranks(time.perf_counter() - t0, world)
         barrier(world)
         e2e_steps = replays * depth
+        # the end-to-end results on the host: step 0's q_out against the PyTorch restatement
+        h0 = hosts[0]
+        e2e_q_bad = differing(pipe.host_q_outs[0][0],
+                              rope_torch(h0.q[0], h0.positions, cos.cpu(), sin.cpu(), w.rotary))
         # the same copies without the decode work: the step's PCIe bound on this box
         cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
         hq, dq = pipe.host_q_outs[0], pipe.q_outs[0]
@@ -458,6 +654,7 @@ def run_ours(args, world, rank, local):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "us_per_step": e2e_s / e2e_steps * 1e6, "steps": e2e_steps,
                "copies_alone_us_per_step": copy_us,
+               "parity_layer0_q": "bit-exact" if e2e_q_bad == 0 else f"MISMATCH {e2e_q_bad}",
                "path": f"DecodeStep.capture_host_pipeline: {depth} steps per graph, each "
                        "copying q/k/v/positions in from pinned host memory, running the 32 "
                        "fused launches and copying q_out back; copies on their own streams; "
@@ -474,23 +671,44 @@ def run_ours(args, world, rank, local):
         floor["layer_us"] = us_launch
         floor["layer_vs_graph_node"] = us_launch / floor["graph_us_per_node"]
         floor["layer_vs_graph_node_pdl"] = us_launch / floor["graph_us_per_node_pdl"]
-    ladder = None if (args.no_ladder or rank != 0) else operator_ladder(device, args.seed)
+
+    ref, ref_why = (None, "skipped")
+    if world == 1 and not args.no_reference_gpu:
+        ref, ref_why = reference_or_reason()
+    ref_step = None
+    if ref is not None and ref.gpu_ok:
+        ref_step = reference_decode_step(ref, k_caches, v_caches, sets, cos, sin, args.steps,
+                                         args.warmup, w)
+        ref_step["speedup_of_ours"] = ref_step["us_per_step"] / (per_step_s * 1e6)
+    ladder = None if (args.no_ladder or rank != 0) else operator_ladder(device, args.seed, ref)
     del captured, sets, k_caches, v_caches, step
     torch.cuda.empty_cache()
     bw = None if args.no_bw_probe else bandwidth_probe(world, rank, device, args.seed, peak)
     tp = None if args.no_bw_probe else single_layer_probe("llama3_70b_tp", world, rank, device,
                                                           args.seed, peak)
-    partial = None
+    partial, cfg1 = None, None
     if not args.no_bw_probe and world == 1:
         partial = single_layer_probe("phi2_partial", world, rank, device, args.seed, peak)
+        cfg1 = single_layer_probe("llama3_8b_b8", world, rank, device, args.seed, peak)
+    ref_gpu = None
+    if world == 1 and rank == 0 and not args.no_reference_gpu and not args.no_bw_probe:
+        ref_gpu = reference_gpu(device, args.seed, peak,
+                                {"llama3_8b_b8": cfg1, "llama3_70b_tp": tp,
+                                 "mistral_b4096": bw, "phi2_partial": partial})
+        ref_gpu["llama3_8b_decode32"] = ref_step if ref_step is not None else {
+            "unavailable": ref_why}
     attention = None
     if not args.no_attention and rank == 0:
         torch.cuda.empty_cache()
         attention = attention_probe(device, args.seed, peak)
 
-    cpu = None
+    cpu, cpu_torch = None, None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, args.seed, args.cpu_seconds)
+        if ref is not None:
+            cpu_torch = cpu_baseline_torch(w, args.seed, args.cpu_seconds, ref)
+        else:
+            cpu_torch = {"unavailable": ref_why}
 
     if rank == 0:
         line = {
@@ -502,17 +720,19 @@ def run_ours(args, world, rank, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": w.dtype_label,
             "data": "synthetic (seeded N(0,1) q/k/v and caches, int32 positions)",
-            "config": dict(w.describe(), **{
-                "parallelism": f"batch shard x{world} (64 sequences and own caches per GPU)",
-                "global_batch": w.batch * world, "seq_len": w.cache_alloc_len,
-                "l2": f"inputs rotate over {nsets} distinct sets "
-                      f"({nsets * input_set_bytes(w) / 2**20:.0f} MiB > 3x L2)",
-                "pdl": not args.no_pdl}),
-            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "config": workload_config(w, world),
+            "timing": {"l2": f"inputs rotate over {nsets} distinct sets "
+                             f"({nsets * input_set_bytes(w) / 2**20:.0f} MiB > 3x L2)",
+                       "pdl": not args.no_pdl, "clock": "CUDA events on the launching stream, "
+                       "max over ranks"},
+            "parity": parity,
+            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu,
+            "cpu_baseline_torch": cpu_torch, "clocks": clocks,
             "gpu_launches": args.steps * w.layers, "launch_floor": floor,
-            "operator_ladder": ladder,
+            "strong_scaling": strong_scaling_record(bw, tp, world),
+            "reference_gpu": ref_gpu, "operator_ladder": ladder,
             "bandwidth_config": bw, "tp_config": tp, "partial_rotary_config": partial,
-            "fused_attention": attention,
+            "single_layer_config": cfg1, "fused_attention": attention,
         }
         print(json.dumps(line), flush=True)
 
@@ -688,36 +908,145 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
     return out
 
 
-def operator_ladder(device, seed):
-    """The reference's operator benchmark at its headline shape, on this build: Llama-3-8B
-    heads (32 Q / 8 KV, head_dim 128), batch 8, bf16, cache [8, 4096, 8, 128], eight rotating
-    device position sets, every rung through the drop-in ops and the reference's runners, with
-    the reference's three timers (benchmarks/benchmark_utils.py:80-126 of the reference). The
-    inputs are 200 KB, so like the reference's own rows these are launch-latency numbers."""
-    from decode_llm_kernel_b200.harness import impls, timing
+def operator_ladder(device, seed, ref):
+    """The reference's operator benchmark at its headline shape, for this build and for the
+    reference's own kernels: Llama-3-8B heads (32 Q / 8 KV, head_dim 128), batch 8, bf16,
+    theta 5e5, cache [8, 4096, 8, 128], eight rotating device position sets; each rung is
+    driven eagerly through the op's Python binding or by replaying one graph per position set
+    (harness/runners.py), and timed three ways (harness/timing.time_call). Then the fused op's
+    amortised per-call cost at batch 1, 8, 32 and 128. The inputs are 200 KB, so like the
+    reference's own rows these are launch-latency numbers."""
+    from decode_llm_kernel_b200.cuda import ops
     from decode_llm_kernel_b200.harness import positions as pos
-    from decode_llm_kernel_b200.harness.workload import Config, build_op_args
-    cfg = Config("gqa", 32, 8, 128, 8, 4096, "bf16", pos.RAGGED, theta=500000.0,
-                 index_dtype="int32")
-    sets = pos.build_position_sets(8, 4096, pos.RAGGED, seed, 8, device, torch.int32)
-    args = build_op_args(cfg, device, seed, sets[0])
-    nbytes = timing.logical_bytes(args.q, args.k, args.v, args.cos, args.sin, args.k_cache,
-                                  args.v_cache)["total_bytes"]
-    rows = {}
-    for spec in impls.IMPL_SPECS:
-        runner = spec.build()
-        thunk = runner.make_thunk(args, sets)
-        amort = timing.time_amortized_call(thunk, 200, 3000)
-        events = timing.time_device_events(thunk, 50, 500)
-        synced = timing.time_synchronized_call(thunk, 50, 500)
-        med = sorted(events)[len(events) // 2]
-        rows[spec.label] = {"amortized_us": amort * 1e3, "event_median_us": med * 1e3,
-                            "synchronized_us": synced * 1e3,
-                            "logical_gbs_amortized": timing.logical_eff_gbps(nbytes, amort)}
-        if hasattr(runner, "release"):
-            runner.release()
-    return {"workload": "llama3_8b_b8 (batch 8, 32/8 heads, head_dim 128, bf16, theta 5e5)",
-            "logical_bytes_per_call": nbytes, "rungs": rows}
+    from decode_llm_kernel_b200.harness.inputs import make_inputs
+    from decode_llm_kernel_b200.harness.runners import RUNGS
+    from decode_llm_kernel_b200.harness.timing import logical_bytes, time_call
+    impls = {"ours": ops}
+    if ref is not None and ref.gpu_ok:
+        impls["reference"] = ref.ops
+    names = {"fused": "fused_rope_kv_append", "separate": "separate_rope_kv_append"}
+    base = WORKLOADS["llama3_8b_b8"]
+    out = {"workload": "llama3_8b_b8 (batch 8, 32/8 heads, head_dim 128, bf16, theta 5e5)",
+           "rungs": {}, "fused_amortized_us_by_batch": {}}
+    for batch in (8, 1, 32, 128):
+        w = replace(base, batch=batch, positions="ragged")
+        sets = pos.build_position_sets(batch, w.cache_alloc_len, pos.RAGGED, seed, 8, device,
+                                       torch.int32)
+        inputs = make_inputs(w, device, seed, sets[0], cache_fill="normal")
+        if batch == 8:
+            out["logical_bytes_per_call"] = logical_bytes(
+                inputs.q, inputs.k, inputs.v, inputs.cos, inputs.sin, inputs.k_cache,
+                inputs.v_cache)["total_bytes"]
+            for impl, mod in impls.items():
+                for label, op_name, kind in RUNGS:
+                    runner = kind(getattr(mod, names[op_name]), inputs, sets)
+                    out["rungs"][f"{impl}:{label}"] = time_call(runner, warmup=200, iters=1000)
+                    runner.release()
+        for impl, mod in impls.items():
+            runner = RUNGS[1][2](mod.fused_rope_kv_append, inputs, sets)
+            out["fused_amortized_us_by_batch"].setdefault(impl, {})[batch] = time_call(
+                runner, warmup=200, iters=1000)["amortized_us"]
+        del inputs
+    if "reference" not in impls:
+        out["reference"] = "unavailable: " + (ref.gpu_reason if ref else "not installed")
+    return out
+
+
+def cpu_inputs(w, seed, cache_len):
+    """Host tensors for whole steps of workload w with caches cut to cache_len positions per
+    request (the op touches one slot per token, so per-token work is unchanged)."""
+    g = torch.Generator().manual_seed(seed)
+    L, T = w.layers, w.batch
+    q = torch.randn(L, T, w.num_q_heads, w.head_dim, generator=g).to(w.dtype)
+    k = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+    v = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+    kcs = [torch.randn(T, cache_len, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+           for _ in range(L)]
+    vcs = [torch.randn(T, cache_len, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
+           for _ in range(L)]
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    cos, sin = build_rope_tables(cache_len, w.rotary, w.theta)
+    pos = torch.randint(0, cache_len, (T,), generator=g)
+    ri = torch.arange(T)
+    return q, k, v, kcs, vcs, cos, sin, pos, ri
+
+
+CPU_CACHE_LEN = 64
+
+
+def time_cpu_steps(one_step, seconds, max_steps=100000):
+    one_step()
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        one_step()
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds or steps >= max_steps:
+            return elapsed / steps, steps
+
+
+def cpu_baseline(w, seed, seconds):
+    """The CPU oracle (a C port of the reference's PyTorch algorithm, OpenMP) on a bounded
+    sample of the workload: whole steps (every layer, every token), caches cut to 64 positions
+    per request, all host threads."""
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    q, k, v, kcs, vcs, cos, sin, pos, ri = cpu_inputs(w, seed, CPU_CACHE_LEN)
+
+    def one_step():
+        for layer in range(w.layers):
+            oracle.fused_rope_kv_append(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer],
+                                        vcs[layer], ri, nthreads=threads)
+
+    per_step, steps = time_cpu_steps(one_step, seconds)
+    return {"value": w.bytes_per_step() / per_step / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port", "ms_per_step": per_step * 1e3, "steps": steps,
+            "sample": f"{steps} whole {w.layers}-layer steps of {w.batch} tokens through the CPU "
+                      f"oracle (C, OpenMP, {threads} threads); caches cut to {CPU_CACHE_LEN} "
+                      f"positions per request and positions drawn in [0, {CPU_CACHE_LEN}), "
+                      "which leaves per-token work unchanged"}
+
+
+def cpu_baseline_torch(w, seed, seconds, ref, max_steps=100000):
+    """The reference's own PyTorch path (decode_kernels.reference.fused_rope_kv_append_ref) on
+    CPU tensors, all host threads, under torch.inference_mode(): whole steps with caches cut to
+    64 positions per request."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v, kcs, vcs, cos, sin, pos, ri = cpu_inputs(w, seed, CPU_CACHE_LEN)
+
+    def one_step():
+        for layer in range(w.layers):
+            ref.oracle(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer], vcs[layer], ri)
+
+    with torch.inference_mode():
+        per_step, steps = time_cpu_steps(one_step, seconds, max_steps)
+    return {"value": w.bytes_per_step() / per_step / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "reference", "ms_per_step": per_step * 1e3, "steps": steps,
+            "sample": f"{steps} whole {w.layers}-layer steps of {w.batch} tokens through the "
+                      "reference's PyTorch oracle fused_rope_kv_append_ref on CPU tensors "
+                      f"({threads} torch threads, inference_mode); caches cut to {CPU_CACHE_LEN} "
+                      "positions per request, which leaves per-token work unchanged"}
+
+
+def workload_config(w, world):
+    """The `config` both arms print, so the driver compares like with like."""
+    return dict(w.describe(), **{
+        "parallelism": f"batch shard x{world} ({w.batch} sequences and their own caches per GPU)",
+        "global_batch": w.batch * world, "seq_len": w.cache_alloc_len})
+
+
+def strong_scaling_record(bw, tp, world):
+    """Per-N records of the two sharded workloads (mistral_b4096 split by batch, llama3_70b_tp
+    split by KV head): total work fixed, so per-GPU work shrinks as N grows."""
+    out = {}
+    for key, r in (("mistral_b4096", bw), ("llama3_70b_tp", tp)):
+        if r:
+            out[key] = {"n_gpus": world, "us": r["us_per_launch"],
+                        "gbs_per_gpu": r["achieved_gbs_per_gpu"], "frac": r["frac_of_peak"],
+                        "aggregate_gbs": r["aggregate_gbs"], "shard": r["shard"],
+                        "parity": r["parity"]}
+    return out
 
 
 def launch_floor(stream, layers):
@@ -755,110 +1084,70 @@ def launch_floor(stream, layers):
     return out
 
 
-def cpu_baseline(w, seed, seconds):
-    """The CPU oracle (a port of the reference's PyTorch algorithm) on a bounded sample of the
-    workload: whole steps (every layer, every token) with caches cut to 64 positions per request
-    -- the op touches one slot per token, so per-token work is unchanged -- on all host
-    threads."""
-    from oracle import oracle
-    from decode_llm_kernel_b200.rope_tables import build_rope_tables
-    threads = os.cpu_count() or 1
-    S = 64
-    g = torch.Generator().manual_seed(seed)
-    L, T = w.layers, w.batch
-    q = torch.randn(L, T, w.num_q_heads, w.head_dim, generator=g).to(w.dtype)
-    k = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-    v = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-    kcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-           for _ in range(L)]
-    vcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-           for _ in range(L)]
-    cos, sin = build_rope_tables(S, w.rotary_dim or w.head_dim, w.theta)
-    pos = torch.randint(0, S, (T,), generator=g)
-    ri = torch.arange(T)
-
-    def one_step():
-        for layer in range(L):
-            oracle.fused_rope_kv_append(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer],
-                                        vcs[layer], ri, nthreads=threads)
-
-    one_step()
-    steps, t0 = 0, time.perf_counter()
-    while True:
-        one_step()
-        steps += 1
-        elapsed = time.perf_counter() - t0
-        if elapsed >= seconds or steps >= 100000:
-            break
-    per_step = elapsed / steps
-    return {"value": w.bytes_per_step() / per_step / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "port", "ms_per_step": per_step * 1e3, "steps": steps,
-            "sample": f"{steps} whole {L}-layer steps of {T} tokens through the CPU oracle "
-                      f"(C, OpenMP, {threads} threads); caches cut to {S} positions per request "
-                      f"and positions drawn in [0, {S}), which leaves per-token work unchanged"}
-
-
 def run_reference(args, world, rank):
-    """The reference's algorithm on the host CPU (the oracle port, all threads), same workload,
-    metric and unit; rank 0 only."""
+    """The reference's CPU implementation of the path on the host cores, rank 0 only: its
+    PyTorch oracle (decode_kernels.reference.fused_rope_kv_append_ref, installed by
+    baseline/build_ref.py) with all host threads under inference_mode; when that is not
+    installed, the C/OpenMP port of the same algorithm in oracle/. Same workload, metric, unit
+    and config dict as this build's arm; caches cut to 64 positions per request (per-token work
+    is unchanged), and each timed step sized so the whole run stays within about two
+    minutes."""
     if rank != 0:
         return
     w = WORKLOADS[args.workload]
-    # size each timed step so K + W steps stay within about two minutes
-    probe = cpu_baseline(w, args.seed, 0.5)
-    per_step_s = probe["ms_per_step"] / 1e3
-    total = (args.steps + args.warmup) * per_step_s
-    if total > 120.0:
-        note = (f"; {args.steps} steps would take {total:.0f} s, so each timed step is "
-                f"{args.steps} x a 2-minute budget")
-    else:
-        note = ""
-    from oracle import oracle
-    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    ref, why = reference_or_reason()
     threads = os.cpu_count() or 1
-    S = 64
-    g = torch.Generator().manual_seed(args.seed)
-    L, T = w.layers, w.batch
-    q = torch.randn(L, T, w.num_q_heads, w.head_dim, generator=g).to(w.dtype)
-    k = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-    v = torch.randn(L, T, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-    kcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-           for _ in range(L)]
-    vcs = [torch.randn(T, S, w.num_kv_heads, w.head_dim, generator=g).to(w.dtype)
-           for _ in range(L)]
-    cos, sin = build_rope_tables(S, w.rotary_dim or w.head_dim, w.theta)
-    pos = torch.randint(0, S, (T,), generator=g)
-    ri = torch.arange(T)
-    layers_per_step = L
-    if total > 120.0:
-        layers_per_step = max(1, int(L * 120.0 / total))
+    q, k, v, kcs, vcs, cos, sin, pos, ri = cpu_inputs(w, args.seed, CPU_CACHE_LEN)
+    if ref is not None:
+        torch.set_num_threads(threads)
+        kind = "reference"
+        what = (f"the reference's PyTorch oracle fused_rope_kv_append_ref on CPU tensors "
+                f"({threads} torch threads, inference_mode)")
 
-    def one_step():
-        for layer in range(layers_per_step):
-            oracle.fused_rope_kv_append(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer],
-                                        vcs[layer], ri, nthreads=threads)
+        def layer_call(layer):
+            ref.oracle(q[layer], k[layer], v[layer], pos, cos, sin, kcs[layer], vcs[layer], ri)
+    else:
+        from oracle import oracle
+        kind = "port"
+        what = (f"the C/OpenMP port of the reference's algorithm ({threads} threads; the "
+                f"reference itself is not installed: {why})")
 
-    for _ in range(args.warmup):
-        one_step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        one_step()
-    elapsed = time.perf_counter() - t0
-    per = elapsed / args.steps
-    bytes_step = w.bytes_per_call() * layers_per_step
-    value = bytes_step / per / 1e9
-    sample = (f"{layers_per_step} of {L} layers x {T} tokens per step through the CPU oracle "
-              f"(C port of the reference's PyTorch algorithm, OpenMP, {threads} threads); "
-              f"caches cut to {S} positions per request{note}")
+        def layer_call(layer):
+            oracle.fused_rope_kv_append(q[layer], k[layer], v[layer], pos, cos, sin,
+                                        kcs[layer], vcs[layer], ri, nthreads=threads)
+
+    with torch.inference_mode():
+        layer_call(0)
+        t0 = time.perf_counter()
+        for layer in range(w.layers):
+            layer_call(layer)
+        probe_step = time.perf_counter() - t0
+        layers_per_step = w.layers
+        total = (args.steps + args.warmup) * probe_step
+        if total > 120.0:
+            layers_per_step = max(1, int(w.layers * 120.0 / total))
+
+        def one_step():
+            for layer in range(layers_per_step):
+                layer_call(layer)
+
+        for _ in range(args.warmup):
+            one_step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            one_step()
+        per = (time.perf_counter() - t0) / args.steps
+    value = w.bytes_per_call() * layers_per_step / per / 1e9
+    sample = (f"{layers_per_step} of {w.layers} layers x {w.batch} tokens per step through "
+              f"{what}; caches cut to {CPU_CACHE_LEN} positions per request")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per * 1e3 * (L / layers_per_step), "higher_is_better": True,
+        "ms_per_step": per * 1e3 * (w.layers / layers_per_step), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": w.dtype_label,
-        "data": "synthetic (seeded N(0,1) q/k/v and caches)",
-        "config": dict(w.describe(), **{"parallelism": "host CPU, rank 0 only",
-                                        "global_batch": w.batch, "seq_len": w.cache_alloc_len}),
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+        "data": "synthetic (seeded N(0,1) q/k/v and caches, int positions)",
+        "config": workload_config(w, max(1, world)),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

@@ -101,6 +101,8 @@ bool is_contiguous(const drk_tensor* t) {
 void require(const drk_tensor* t, const char* name) {
   if (t == nullptr) invalid(name, " is NULL");
   if (t->ndim < 0 || t->ndim > 4) invalid(name, " has an unsupported number of dims ", t->ndim);
+  for (int i = 0; i < t->ndim; ++i)
+    if (t->sizes[i] < 0) invalid(name, " has a negative size ", t->sizes[i], " in dim ", i);
 }
 
 void check_device(const drk_tensor* t, const char* name, int32_t device) {
@@ -828,9 +830,147 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
   check_launch(drk::launch_rope_kv_attention(p, a, elem_code(q->dtype), index_bits, shape, s));
 }
 
+void rope_forward_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* positions,
+                       const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* q_out,
+                       const drk_tensor* k_out, const drk_options* opts, uint32_t* status,
+                       drk_stream_t stream, bool launch) {
+  const drk_options o = options_or_default(opts);
+  require(q, "q");
+  if (q->ndim != 3) invalid("q must be [num_tokens, num_q_heads, head_dim]");
+  const int64_t T = q->sizes[0], Hq = q->sizes[1], D = q->sizes[2];
+  if (D % 2) invalid("head_dim must be even for split-half RoPE, got ", D);
+  const int32_t device = q->device;
+  check_qkv(q, "q", T, D, device);
+  check_qkv(k, "k", T, D, device);
+  if (q->dtype != k->dtype)
+    invalid("q and k must share a dtype, got ", dtype_name(q->dtype), "/",
+            dtype_name(k->dtype));
+  check_index_tensor(positions, "positions", T, device);
+  const int32_t rot = resolve_rotary(o, D);
+  check_rope_tables(cos, sin, D, rot, device);
+  const int64_t Hkv = k->sizes[1];
+  check_output(q_out, "q_out", q->dtype, T, Hq, D, device);
+  check_output(k_out, "k_out", k->dtype, T, Hkv, D, device);
+  check_float_dtype(q->dtype, "rope_forward");
+  if (T == 0 || !launch) return;
+
+  const int64_t R = rot ? rot : D;
+  drk::KernelParams p{};
+  p.q = static_cast<const char*>(q->data);
+  p.k = static_cast<const char*>(k->data);
+  p.q_out = static_cast<char*>(q_out->data);
+  p.k_dst = static_cast<char*>(k_out->data);
+  p.positions = positions->data;
+  p.status = status;
+  p.T = T;
+  p.q_ts = q->strides[0]; p.q_hs = q->strides[1];
+  p.k_ts = k->strides[0]; p.k_hs = k->strides[1];
+  p.Hq = static_cast<int32_t>(Hq);
+  p.Hkv = static_cast<int32_t>(Hkv);
+  p.D = static_cast<int32_t>(D);
+  p.R = static_cast<int32_t>(R);
+  fill_table(p, cos, sin, o, R);
+  Aligner al{elem_size(q->dtype), R, D};
+  for (const drk_tensor* t : {q, k, q_out, k_out}) al.ptr(t->data);
+  al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
+  al.stride(T, k->strides[0]); al.stride(Hkv, k->strides[1]);
+  const Shape s = plan(al, static_cast<int>(Hq + Hkv), true, T, o.row_splits);
+  p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
+  p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
+  DeviceGuard guard(device);
+  const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
+  const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+  check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeRope,
+                                   drk::kCacheStrided, shape,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
+void kv_append_impl(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor* positions,
+                    const drk_tensor* request_indices, const drk_tensor* k_cache,
+                    const drk_tensor* v_cache, const drk_options* opts, uint32_t* status,
+                    drk_stream_t stream, bool launch) {
+  const drk_options o = options_or_default(opts);
+  require(k_rot, "k_rot");
+  if (k_rot->ndim != 3) invalid("k_rot must be [num_tokens, num_kv_heads, head_dim]");
+  const int64_t T = k_rot->sizes[0], Hkv = k_rot->sizes[1], D = k_rot->sizes[2];
+  const int32_t device = k_rot->device;
+  check_qkv(k_rot, "k_rot", T, D, device);
+  check_qkv(v, "v", T, D, device);
+  if (v->sizes[1] != Hkv) invalid("v has ", v->sizes[1], " kv heads, expected ", Hkv);
+  if (k_rot->dtype != v->dtype)
+    invalid("k_rot and v must share a dtype, got ", dtype_name(k_rot->dtype), "/",
+            dtype_name(v->dtype));
+  check_index_tensor(positions, "positions", T, device);
+  check_index_tensor(request_indices, "request_indices", T, device);
+  if (positions->dtype != request_indices->dtype)
+    invalid("positions and request_indices must share a dtype, got ",
+            dtype_name(positions->dtype), "/", dtype_name(request_indices->dtype));
+  const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0;
+  check_cache(k_cache, "k_cache", k_rot->dtype, Hkv, D, device, strided_ok);
+  check_cache(v_cache, "v_cache", v->dtype, Hkv, D, device, strided_ok);
+  check_caches_are_distinct(k_cache, v_cache);
+  check_float_dtype(k_rot->dtype, "kv_append");
+  if (o.k_position_limit < 0)
+    invalid("k_position_limit must be >= 0, got ", o.k_position_limit);
+  if (T == 0 || !launch) return;
+  if (D % 2)
+    throw Unsupported(cat("kv_append needs an even head_dim, got ", D));
+
+  drk::KernelParams p{};
+  p.k = static_cast<const char*>(k_rot->data);
+  p.v = static_cast<const char*>(v->data);
+  p.k_dst = static_cast<char*>(k_cache->data);
+  p.v_dst = static_cast<char*>(v_cache->data);
+  p.positions = positions->data;
+  p.request_indices = request_indices->data;
+  p.status = status;
+  p.T = T;
+  p.k_ts = k_rot->strides[0]; p.k_hs = k_rot->strides[1];
+  p.v_ts = v->strides[0]; p.v_hs = v->strides[1];
+  p.c_bs = k_cache->strides[0]; p.c_ss = k_cache->strides[1]; p.c_hs = k_cache->strides[2];
+  p.B = k_cache->sizes[0];
+  p.S = k_cache->sizes[1];
+  p.Hkv = static_cast<int32_t>(Hkv);
+  p.D = static_cast<int32_t>(D);
+  p.R = 0;
+  p.table_rows = o.k_position_limit > 0 ? o.k_position_limit : INT64_MAX;
+  Aligner al{elem_size(k_rot->dtype), 0, D};
+  for (const drk_tensor* t : {k_rot, v, k_cache, v_cache}) al.ptr(t->data);
+  al.stride(T, k_rot->strides[0]); al.stride(Hkv, k_rot->strides[1]);
+  al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
+  for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
+  const Shape s = plan(al, static_cast<int>(2 * Hkv), false, T, o.row_splits);
+  p.nslots = s.nslots; p.nrot = 0; p.G = s.G; p.rows_per_thread = s.rows;
+  p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
+  DeviceGuard guard(device);
+  const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
+  const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
+  check_launch(drk::launch_rope_kv(p, elem_code(k_rot->dtype), index_bits, s.vb,
+                                   drk::kModeAppend, drk::kCacheStrided, shape,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+}
+
 }  // namespace
 
 namespace drk {
+// The host checks of drk_rope_forward and drk_kv_append without the launch: DRK_OK, or the
+// error code with the message drk_last_error() returns. (noalloc.cu validates a call before it
+// touches its scratch array.)
+int validate_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor* positions,
+                          const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* q_out,
+                          const drk_tensor* k_out) {
+  return guarded([&] {
+    rope_forward_impl(q, k, positions, cos, sin, q_out, k_out, nullptr, nullptr, nullptr, false);
+  });
+}
+int validate_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor* positions,
+                       const drk_tensor* request_indices, const drk_tensor* k_cache,
+                       const drk_tensor* v_cache, const drk_options* opts) {
+  return guarded([&] {
+    kv_append_impl(k_rot, v, positions, request_indices, k_cache, v_cache, opts, nullptr,
+                   nullptr, false);
+  });
+}
 // For entry points defined in other files of this library (noalloc.cu).
 void set_last_error(const std::string& message) { g_last_error = message; }
 }  // namespace drk
@@ -878,55 +1018,7 @@ int drk_rope_forward(const drk_tensor* q, const drk_tensor* k, const drk_tensor*
                      const drk_tensor* k_out, const drk_options* opts, uint32_t* status,
                      drk_stream_t stream) {
   return guarded([&] {
-    const drk_options o = options_or_default(opts);
-    require(q, "q");
-    if (q->ndim != 3) invalid("q must be [num_tokens, num_q_heads, head_dim]");
-    const int64_t T = q->sizes[0], Hq = q->sizes[1], D = q->sizes[2];
-    if (D % 2) invalid("head_dim must be even for split-half RoPE, got ", D);
-    const int32_t device = q->device;
-    check_qkv(q, "q", T, D, device);
-    check_qkv(k, "k", T, D, device);
-    if (q->dtype != k->dtype)
-      invalid("q and k must share a dtype, got ", dtype_name(q->dtype), "/",
-              dtype_name(k->dtype));
-    check_index_tensor(positions, "positions", T, device);
-    const int32_t rot = resolve_rotary(o, D);
-    check_rope_tables(cos, sin, D, rot, device);
-    const int64_t Hkv = k->sizes[1];
-    check_output(q_out, "q_out", q->dtype, T, Hq, D, device);
-    check_output(k_out, "k_out", k->dtype, T, Hkv, D, device);
-    check_float_dtype(q->dtype, "rope_forward");
-    if (T == 0) return;
-
-    const int64_t R = rot ? rot : D;
-    drk::KernelParams p{};
-    p.q = static_cast<const char*>(q->data);
-    p.k = static_cast<const char*>(k->data);
-    p.q_out = static_cast<char*>(q_out->data);
-    p.k_dst = static_cast<char*>(k_out->data);
-    p.positions = positions->data;
-    p.status = status;
-    p.T = T;
-    p.q_ts = q->strides[0]; p.q_hs = q->strides[1];
-    p.k_ts = k->strides[0]; p.k_hs = k->strides[1];
-    p.Hq = static_cast<int32_t>(Hq);
-    p.Hkv = static_cast<int32_t>(Hkv);
-    p.D = static_cast<int32_t>(D);
-    p.R = static_cast<int32_t>(R);
-    fill_table(p, cos, sin, o, R);
-    Aligner al{elem_size(q->dtype), R, D};
-    for (const drk_tensor* t : {q, k, q_out, k_out}) al.ptr(t->data);
-    al.stride(T, q->strides[0]); al.stride(Hq, q->strides[1]);
-    al.stride(T, k->strides[0]); al.stride(Hkv, k->strides[1]);
-    const Shape s = plan(al, static_cast<int>(Hq + Hkv), true, T, o.row_splits);
-    p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
-    p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
-    DeviceGuard guard(device);
-    const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
-    const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
-    check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeRope,
-                                     drk::kCacheStrided, shape,
-                                     reinterpret_cast<cudaStream_t>(stream)));
+    rope_forward_impl(q, k, positions, cos, sin, q_out, k_out, opts, status, stream, true);
   });
 }
 
@@ -935,63 +1027,8 @@ int drk_kv_append(const drk_tensor* k_rot, const drk_tensor* v, const drk_tensor
                   const drk_tensor* v_cache, const drk_options* opts, uint32_t* status,
                   drk_stream_t stream) {
   return guarded([&] {
-    const drk_options o = options_or_default(opts);
-    require(k_rot, "k_rot");
-    if (k_rot->ndim != 3) invalid("k_rot must be [num_tokens, num_kv_heads, head_dim]");
-    const int64_t T = k_rot->sizes[0], Hkv = k_rot->sizes[1], D = k_rot->sizes[2];
-    const int32_t device = k_rot->device;
-    check_qkv(k_rot, "k_rot", T, D, device);
-    check_qkv(v, "v", T, D, device);
-    if (v->sizes[1] != Hkv) invalid("v has ", v->sizes[1], " kv heads, expected ", Hkv);
-    if (k_rot->dtype != v->dtype)
-      invalid("k_rot and v must share a dtype, got ", dtype_name(k_rot->dtype), "/",
-              dtype_name(v->dtype));
-    check_index_tensor(positions, "positions", T, device);
-    check_index_tensor(request_indices, "request_indices", T, device);
-    if (positions->dtype != request_indices->dtype)
-      invalid("positions and request_indices must share a dtype, got ",
-              dtype_name(positions->dtype), "/", dtype_name(request_indices->dtype));
-    const bool strided_ok = (o.flags & DRK_FLAG_STRIDED_CACHE) != 0;
-    check_cache(k_cache, "k_cache", k_rot->dtype, Hkv, D, device, strided_ok);
-    check_cache(v_cache, "v_cache", v->dtype, Hkv, D, device, strided_ok);
-    check_caches_are_distinct(k_cache, v_cache);
-    check_float_dtype(k_rot->dtype, "kv_append");
-    if (T == 0) return;
-    if (D % 2)
-      throw Unsupported(cat("kv_append needs an even head_dim, got ", D));
-
-    drk::KernelParams p{};
-    p.k = static_cast<const char*>(k_rot->data);
-    p.v = static_cast<const char*>(v->data);
-    p.k_dst = static_cast<char*>(k_cache->data);
-    p.v_dst = static_cast<char*>(v_cache->data);
-    p.positions = positions->data;
-    p.request_indices = request_indices->data;
-    p.status = status;
-    p.T = T;
-    p.k_ts = k_rot->strides[0]; p.k_hs = k_rot->strides[1];
-    p.v_ts = v->strides[0]; p.v_hs = v->strides[1];
-    p.c_bs = k_cache->strides[0]; p.c_ss = k_cache->strides[1]; p.c_hs = k_cache->strides[2];
-    p.B = k_cache->sizes[0];
-    p.S = k_cache->sizes[1];
-    p.Hkv = static_cast<int32_t>(Hkv);
-    p.D = static_cast<int32_t>(D);
-    p.R = 0;
-    p.table_rows = INT64_MAX;
-    Aligner al{elem_size(k_rot->dtype), 0, D};
-    for (const drk_tensor* t : {k_rot, v, k_cache, v_cache}) al.ptr(t->data);
-    al.stride(T, k_rot->strides[0]); al.stride(Hkv, k_rot->strides[1]);
-    al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
-    for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
-    const Shape s = plan(al, static_cast<int>(2 * Hkv), false, T, o.row_splits);
-    p.nslots = s.nslots; p.nrot = 0; p.G = s.G; p.rows_per_thread = s.rows;
-    p.pdl = (o.flags & DRK_FLAG_PDL) ? 1 : 0;
-    DeviceGuard guard(device);
-    const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, (o.flags & DRK_FLAG_PDL) != 0};
-    const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
-    check_launch(drk::launch_rope_kv(p, elem_code(k_rot->dtype), index_bits, s.vb,
-                                     drk::kModeAppend, drk::kCacheStrided, shape,
-                                     reinterpret_cast<cudaStream_t>(stream)));
+    kv_append_impl(k_rot, v, positions, request_indices, k_cache, v_cache, opts, status, stream,
+                   true);
   });
 }
 

@@ -265,10 +265,11 @@ std::tuple<at::Tensor, at::Tensor> rope_forward_ex(at::Tensor q, at::Tensor k,
 
 void kv_append_ex(at::Tensor k_rot, at::Tensor v, at::Tensor positions,
                   at::Tensor request_indices, at::Tensor k_cache, at::Tensor v_cache, bool pdl,
-                  bool strided_cache) {
-  const drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
-                                         (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
-                                     0, c10::nullopt);
+                  bool strided_cache, int64_t k_position_limit) {
+  drk_options o = make_options((pdl ? DRK_FLAG_PDL : 0u) |
+                                   (strided_cache ? DRK_FLAG_STRIDED_CACHE : 0u),
+                               0, c10::nullopt);
+  o.k_position_limit = k_position_limit;
   const drk_tensor dk = describe(k_rot), dv = describe(v), dp = describe(positions),
                    dri = describe(request_indices), dkc = describe(k_cache),
                    dvc = describe(v_cache);
@@ -452,7 +453,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("cos"), py::arg("sin"), py::arg("rotary_dim") = 0, py::arg("pdl") = false);
   m.def("kv_append_ex", &kv_append_ex, py::arg("k_rot"), py::arg("v"), py::arg("positions"),
         py::arg("request_indices"), py::arg("k_cache"), py::arg("v_cache"),
-        py::arg("pdl") = false, py::arg("strided_cache") = false);
+        py::arg("pdl") = false, py::arg("strided_cache") = false,
+        py::arg("k_position_limit") = 0);
   m.def("fused_rope_kv_append_attention", &fused_rope_kv_append_attention, py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("request_indices"),

@@ -400,7 +400,10 @@ rope_kv_kernel(const __grid_constant__ KernelParams p) {
             store_keep<VB>(dst, x1[i].bits);
             store_keep<VB>(dst + gap[i], x2[i].bits);
           }
-        } else if (cache_ok && (kind[i] == kRowV || M == Mode::kAppend || table_ok)) {
+        } else if (cache_ok && (kind[i] == kRowV || table_ok)) {
+          // K rows need table_ok: in fused mode the row was rotated with this token's table
+          // row; in append mode table_rows is the caller's k_position_limit (INT64_MAX unless
+          // set), past which the rope step left the k_rot row unwritten.
           char* dst = (kind[i] == kRowK ? p.k_dst : p.v_dst) + slot * ES + dst_off[i];
           store_stream<VB>(dst, x1[i].bits);
           store_stream<VB>(dst + gap[i], x2[i].bits);

@@ -23,7 +23,12 @@ def separate_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, requ
     """RoPE kernel then append kernel, with `k_rot` materialised between them: two launches and
     one intermediate, the ablation the fused op is measured against."""
     q_rot, k_rot = rope_forward(q, k, positions, cos, sin)
-    kv_append(k_rot, v, positions, request_indices, k_cache, v_cache)
+    # A token past the cos/sin table gets no k_rot row from rope_forward (a status bit
+    # instead), so the append is told the table length and leaves that K slot untouched, as the
+    # fused op does; its V slot is still written.
+    limit = cos.shape[0] if cos.dim() == 2 and cos.shape[0] > 0 else 0
+    require().kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, False, False,
+                           limit)
     return q_rot
 
 
@@ -70,9 +75,12 @@ def rope_forward_ex(q, k, positions, cos, sin, *, rotary_dim=0, pdl=False):
 
 
 def kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, *, pdl=False,
-                 strided_cache=False):
+                 strided_cache=False, k_position_limit=0):
+    """kv_append with PDL, strided caches, and k_position_limit: when > 0, the K row of a token
+    whose position is >= it is not written (its V row still is) -- pass the cos/sin table's row
+    count when k_rot came from rope_forward, which leaves such rows unwritten."""
     require().kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, pdl,
-                           strided_cache)
+                           strided_cache, k_position_limit)
 
 
 def advance_positions(positions, delta=1, *, pdl=False):

@@ -1,18 +1,18 @@
-"""Byte accounting and the three timers of the reference's harness
-(benchmarks/benchmark_utils.py:35-126).
+"""Byte accounting (the roofline numerator) and the per-call timer.
 
-`logical_bytes` is the roofline numerator: reads of q, k, v and the rotary half-rows of cos and
-sin, writes of q_rot and of the K and V cache slots. Index reads are excluded, as in the
-reference. With partial rotary only rotary_dim/2 cos and sin values are read per token.
+`logical_bytes` follows the reference's formula (benchmarks/benchmark_utils.py:35-68): reads of
+q, k, v and of the rotary half-rows of cos and sin, writes of q_rot and of the K and V cache
+slots; index reads are excluded. With partial rotary only rotary_dim/2 cos and sin values are
+read per token.
+
+`time_call` reports a call's cost in the three views the reference's results use (an
+amortised loop, per-call device events, per-call synchronised wall clock), from one
+measurement routine of this package.
 """
 import statistics
 import time
 
 import torch
-
-
-def sync():
-    torch.cuda.synchronize()
 
 
 def bytes_per_token(num_q_heads, num_kv_heads, head_dim, elem_bytes, rotary_dim=None):
@@ -43,67 +43,43 @@ def logical_bytes(q, k, v, cos, sin, k_cache, v_cache):
             "write_bytes": write_bytes, "total_bytes": read_bytes + write_bytes}
 
 
-def logical_eff_gbps(total_bytes, latency_ms):
-    return total_bytes / (latency_ms / 1e3) / 1e9
+def time_call(fn, *, warmup=100, iters=1000, stream=None):
+    """Cost of `fn()` (which launches work on `stream`, default the current stream), in us:
 
+      amortized_us     wall clock of `iters` calls issued back to back, with one synchronise
+                       after the last, divided by `iters`: what a launch-bound caller pays
+                       per call in steady state (the reference's headline timer);
+      event_median_us  median over calls of the device interval between two events recorded
+                       around each call (includes the gaps launch latency leaves);
+      synchronized_us  median over calls of the wall clock of one call plus a synchronise.
 
-def time_device_events(fn, warmup, iters):
-    """Per-invocation device-timeline ms: CUDA events bracketing each call."""
+    Events and wall clocks come from a single pass of `3 * iters` calls after `warmup`."""
+    stream = stream or torch.cuda.current_stream()
     for _ in range(warmup):
         fn()
-    sync()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(iters)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(iters)]
-    for i in range(iters):
-        starts[i].record()
-        fn()
-        ends[i].record()
-    sync()
-    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    torch.cuda.synchronize()
 
-
-def time_amortized_call(fn, warmup, iters):
-    """Wall time of an unsynchronised loop / iters (ms): steady-state cost per call with
-    launches pipelined, not a per-call latency."""
-    for _ in range(warmup):
-        fn()
-    sync()
     t0 = time.perf_counter()
     for _ in range(iters):
         fn()
-    sync()
-    return (time.perf_counter() - t0) / iters * 1e3
+    torch.cuda.synchronize()
+    amortized = (time.perf_counter() - t0) / iters
 
-
-def time_synchronized_call(fn, warmup, iters):
-    """Median wall time of individually synchronised calls (ms)."""
-    for _ in range(warmup):
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(2 * iters)]
+    for i in range(iters):
+        marks[2 * i].record(stream)
         fn()
-    sync()
-    samples = []
+        marks[2 * i + 1].record(stream)
+    torch.cuda.synchronize()
+    events = [marks[2 * i].elapsed_time(marks[2 * i + 1]) / 1e3 for i in range(iters)]
+
+    walls = []
     for _ in range(iters):
-        t0 = time.perf_counter()
+        t = time.perf_counter()
         fn()
-        sync()
-        samples.append((time.perf_counter() - t0) * 1e3)
-    return statistics.median(samples)
-
-
-def time_region_events(fn, iters, stream=None):
-    """Device ms for `iters` back-to-back calls bracketed by one pair of events."""
-    stream = stream or torch.cuda.current_stream()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(iters):
-        fn()
-    end.record(stream)
-    end.synchronize()
-    return start.elapsed_time(end)
-
-
-def summarize(samples):
-    s = sorted(samples)
-    n = len(s)
-    return {"median": statistics.median(s), "min": s[0], "p95": s[min(n - 1, int(0.95 * n))],
-            "mean": sum(s) / n}
+        torch.cuda.synchronize()
+        walls.append(time.perf_counter() - t)
+    return {"amortized_us": amortized * 1e6,
+            "event_median_us": statistics.median(events) * 1e6,
+            "synchronized_us": statistics.median(walls) * 1e6,
+            "iters": iters}

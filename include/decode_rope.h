@@ -109,7 +109,13 @@ typedef struct drk_options {
   int32_t row_splits;     /* register kernel: CTAs sharing one token's head rows (0 = chosen
                              by the library from the token count and the SM count) */
   int32_t reserved0;
-  int64_t reserved[3];
+  int64_t k_position_limit; /* drk_kv_append only: when > 0, the K row of a token whose
+                               position is >= this is not written (its V row still is). A
+                               separate RoPE-then-append passes the cos/sin table's row count,
+                               because drk_rope_forward leaves k_rot rows of such tokens
+                               unwritten, so they hold no defined value. 0: every K row is
+                               written (the reference's kv_append). */
+  int64_t reserved[2];
 } drk_options;
 
 /*
@@ -171,20 +177,25 @@ DRK_API int drk_paged_rope_kv_append(const drk_tensor* q, const drk_tensor* k, c
 
 /*
  * The separate op (drk_rope_forward, then drk_kv_append) for callers that cannot allocate
- * device memory when they launch it. No counterpart in the reference: it is this library's
- * allocation-free form of separate_rope_kv_append (decode_kernels/cuda/ops.py:25-34 of the
- * reference), whose k_rot intermediate the reference allocates per call.
+ * device memory when they launch it. It has no counterpart in the reference: it is this
+ * library's allocation-free form of the separate RoPE-then-append op, whose k_rot intermediate
+ * is otherwise allocated per call.
  *
  * Callers it is for: code recorded under a global-mode stream capture (where cudaMalloc is not
  * allowed), serving runtimes that have given all free HBM to their KV-cache pool, and hosts
  * reaching the library through this C ABI without an allocator of their own. The caller still
  * provides every input and output (q_out included); the k_rot intermediate lives in an 8 MiB
  * static device array inside the library, which every GPU that loads the library holds until
- * the process exits. Calls whose k_rot ([T, Hkv, D] of k's dtype) exceeds 8 MiB are rejected
- * with DRK_ERR_INVALID. The first call on a device looks up the array's address with that
- * device current; make it before any stream capture. All calls share the array, so calls that
- * overlap on the GPU race. Nothing in the array needs to start zeroed. Results are bit-identical
- * to drk_rope_forward + drk_kv_append with a caller-allocated k_rot.
+ * the process exits. Arguments go through the checks of drk_rope_forward and drk_kv_append
+ * first; then calls whose k_rot ([T, Hkv, D] of k's dtype) exceeds 8 MiB are rejected with
+ * DRK_ERR_INVALID, before any launch. The first call on a device looks up the array's address
+ * with that device current and keeps it for the life of the process: make it before any stream
+ * capture, and do not use this entry point after cudaDeviceReset in the same process. All calls
+ * share the array, so calls that overlap on the GPU race. Nothing in the array needs to start
+ * zeroed: a K slot is written only from a k_rot row the same call wrote (a token past the
+ * cos/sin table sets DRK_STATUS_POSITION_OUT_OF_TABLE and keeps its K slot, as in the fused
+ * op). Results are bit-identical to drk_rope_forward + drk_kv_append with a caller-allocated
+ * k_rot and k_position_limit set to the table's row count.
  */
 DRK_API int drk_separate_rope_kv_append_noalloc(
     const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,

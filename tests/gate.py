@@ -13,8 +13,7 @@ from typing import NamedTuple
 import torch
 
 from decode_llm_kernel_b200.harness import positions as pos
-from decode_llm_kernel_b200.harness.workload import (CACHE_SENTINEL, IDENTITY, PACKED, PERMUTED,
-                                                     STRIDED, build_op_args)
+from decode_llm_kernel_b200.harness.inputs import SENTINEL, make_inputs
 from golden_io import bits_equal
 from oracle import oracle
 
@@ -39,8 +38,8 @@ class AddressingError(ValueError):
 class ValidationCase(NamedTuple):
     label: str
     positions: torch.Tensor
-    request_mapping: str
-    layout: str
+    request_order: str      # "identity" | "shuffled" token -> request rows
+    qkv_layout: str         # "packed" | "fused" (views of one QKV projection)
 
 
 def assert_valid_addressing(positions, request_indices, cache_alloc_len, batch_size):
@@ -73,10 +72,10 @@ def _host(t):
 
 def validate_once(candidate, cfg, device, seed, case):
     tol = TOLERANCES[cfg.dtype]
-    a = build_op_args(cfg, device, seed, case.positions, sentinel_cache=True,
-                      request_mapping=case.request_mapping, layout=case.layout)
+    a = make_inputs(cfg, device, seed, case.positions, cache_fill=SENTINEL,
+                    request_order=case.request_order, qkv_layout=case.qkv_layout)
     assert_valid_addressing(a.positions, a.request_indices, cfg.cache_alloc_len,
-                            cfg.num_requests)
+                            cfg.batch)
     ref = [_host(t).clone() if i in (6, 7) else _host(t) for i, t in enumerate(a)]
     q_ref = oracle.fused_rope_kv_append(*ref)
     q_cand = _host(candidate(*a))
@@ -85,7 +84,7 @@ def validate_once(candidate, cfg, device, seed, case):
     k_ref_slots, k_cand_slots = ref[6][ri, p], kc[ri, p]
     v_cand_slots = vc[ri, p]
     v_in = _host(a.v)
-    mask = torch.zeros(cfg.num_requests, cfg.cache_alloc_len, dtype=torch.bool)
+    mask = torch.zeros(cfg.batch, cfg.cache_alloc_len, dtype=torch.bool)
     mask[ri, p] = True
 
     atol, rtol = tol["atol"], tol["rtol"]
@@ -100,10 +99,10 @@ def validate_once(candidate, cfg, device, seed, case):
     if not v_exact:
         failures.append("v_cache written slots are not byte-exact raw v "
                         f"(max_abs={_max_abs_diff(v_cand_slots, v_in):.3e})")
-    intact = bool((kc[~mask] == CACHE_SENTINEL).all() and (vc[~mask] == CACHE_SENTINEL).all())
+    intact = bool((kc[~mask] == SENTINEL).all() and (vc[~mask] == SENTINEL).all())
     if not intact:
-        n_k = int((kc[~mask] != CACHE_SENTINEL).sum())
-        n_v = int((vc[~mask] != CACHE_SENTINEL).sum())
+        n_k = int((kc[~mask] != SENTINEL).sum())
+        n_v = int((vc[~mask] != SENTINEL).sum())
         failures.append(f"unaddressed cache slots modified (k:{n_k} v:{n_v} elements)")
     return {
         "ok": not failures,
@@ -120,16 +119,16 @@ def validate_once(candidate, cfg, device, seed, case):
 
 
 def validation_cases(cfg, device, seed):
-    timed = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, cfg.position_mode,
+    timed = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, cfg.positions,
                                     seed, 2, device)
-    cases = [ValidationCase(f"{cfg.position_mode}[{i}]", p, cfg.request_mapping, cfg.layout)
+    cases = [ValidationCase(f"{cfg.positions}[{i}]", p, cfg.request_order, cfg.qkv_layout)
              for i, p in enumerate(timed)]
-    if cfg.position_mode != pos.UNIFORM:
-        uniform = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, pos.UNIFORM,
+    if cfg.positions != pos.UNIFORM:
+        uniform = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, pos.UNIFORM,
                                           seed, 1, device)[0]
-        cases.append(ValidationCase("uniform", uniform, cfg.request_mapping, cfg.layout))
-    cases.append(ValidationCase("permuted-requests", timed[0], PERMUTED, PACKED))
-    cases.append(ValidationCase("strided-qkv", timed[0], IDENTITY, STRIDED))
+        cases.append(ValidationCase("uniform", uniform, cfg.request_order, cfg.qkv_layout))
+    cases.append(ValidationCase("permuted-requests", timed[0], "shuffled", "packed"))
+    cases.append(ValidationCase("strided-qkv", timed[0], "identity", "fused"))
     return cases
 
 

@@ -1,9 +1,8 @@
 """Generates the golden fixtures in this directory from the reference project's own oracle.
 
-Run in a container that has the reference checkout (default /root/reference, or the path in
-$DECODE_REFERENCE_ROOT):
+Run where the reference checkout is present, naming it in $DECODE_REFERENCE_ROOT:
 
-    python tests/golden/make_golden.py
+    DECODE_REFERENCE_ROOT=/path/to/reference python tests/golden/make_golden.py
 
 It imports `decode_kernels.reference` from the reference checkout (rope_cache.py:3-36),
 builds seeded inputs, runs `fused_rope_kv_append_ref` on CPU and stores inputs and outputs
@@ -25,7 +24,7 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("DECODE_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("DECODE_REFERENCE_ROOT")
 SENTINEL = 7.5
 SEED = 1234
 
@@ -59,6 +58,8 @@ CASES = [
 
 
 def _reference():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "decode_kernels")):
+        raise SystemExit("set DECODE_REFERENCE_ROOT to the reference checkout")
     sys.path.insert(0, REF_ROOT)
     from decode_kernels.reference import rope_cache  # noqa: E402
     return rope_cache

@@ -1,6 +1,8 @@
-"""bench.py on a machine without a GPU: the reference arm (the CPU oracle on host cores) runs
-and prints the contract's JSON line; the workload byte accounting matches the roofline
-numerator."""
+"""bench.py on a machine without a GPU: the reference arm (the reference's PyTorch CPU path on
+the host cores, or the C port of it when the reference is not installed) runs and prints the
+contract's JSON line with the same config dict as this build's arm; the workload byte
+accounting matches the roofline numerator; the parity restatement bench.py checks timed runs
+with agrees with the CPU oracle bit for bit."""
 import json
 import os
 import subprocess
@@ -19,9 +21,15 @@ def test_reference_arm_prints_the_contract_line():
                 "higher_is_better", "scaling", "dtype", "config", "cpu_baseline", "e2e"):
         assert key in line
     assert line["unit"] == "GB/s" and line["value"] > 0
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    ref_installed = os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "decode_kernels"))
+    assert line["cpu_baseline"]["kind"] == ("reference" if ref_installed else "port")
+    assert line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
-    assert line["config"]["workload"] == "llama3_8b_decode32"
+    # the same config dict this build's arm prints (bench.workload_config), key for key
+    sys.path.insert(0, ROOT)
+    import bench
+    from decode_llm_kernel_b200.harness.configs import WORKLOADS
+    assert line["config"] == bench.workload_config(WORKLOADS["llama3_8b_decode32"], 1)
 
 
 def test_reference_arm_non_zero_ranks_exit_quietly():
@@ -46,3 +54,24 @@ def test_bytes_per_token_matches_the_reference_formula():
     assert lb["total_bytes"] == w.bytes_per_call() == 200704
     assert WORKLOADS["phi2_partial"].bytes_per_token() == 30848
     assert WORKLOADS["llama3_70b_tp"].bytes_per_token() == 41472
+
+
+def test_the_bench_parity_restatement_matches_the_oracle():
+    """bench.rope_torch (run on the GPU after each timed region) is bit-identical to the CPU
+    oracle on every dtype, full and partial rotary."""
+    import torch
+    sys.path.insert(0, ROOT)
+    import bench
+    from decode_llm_kernel_b200.rope_tables import build_rope_tables
+    from oracle import oracle
+    g = torch.Generator().manual_seed(5)
+    for dt in (torch.bfloat16, torch.float16, torch.float32, torch.float64):
+        for D, R in ((128, 128), (80, 32), (96, 96)):
+            T, S = 37, 300
+            q = torch.randn(T, 6, D, generator=g).to(dt)
+            k = torch.randn(T, 2, D, generator=g).to(dt)
+            pos = torch.randint(0, S, (T,), generator=g)
+            cos, sin = build_rope_tables(S, R, 500000.0)
+            q_ref, k_ref = oracle.rope_forward(q, k, pos, cos, sin)
+            assert bench.differing(bench.rope_torch(q, pos, cos, sin, R), q_ref) == 0, (dt, D, R)
+            assert bench.differing(bench.rope_torch(k, pos, cos, sin, R), k_ref) == 0, (dt, D, R)

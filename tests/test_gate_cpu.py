@@ -5,14 +5,14 @@ import pytest
 import torch
 
 from decode_llm_kernel_b200.harness import positions as pos
-from decode_llm_kernel_b200.harness.workload import IDENTITY, PACKED, PERMUTED, STRIDED, Config
+from decode_llm_kernel_b200.harness.inputs import case
 from gate import (AddressingError, ValidationCase, ValidationError, assert_valid_addressing,
                   validate_candidate, validate_once, validate_or_raise, validation_cases)
 
 DEVICE = "cpu"
 SEED = 1234
-MHA_BF16 = Config("mha", 8, 8, 64, 4, 128, "bf16", pos.RAGGED)
-GQA_BF16 = Config("gqa", 8, 2, 64, 4, 128, "bf16", pos.RAGGED)
+MHA_BF16 = case("mha", 8, 8, 64, 4, 128, "bf16", pos.RAGGED)
+GQA_BF16 = case("gqa", 8, 2, 64, 4, 128, "bf16", pos.RAGGED)
 
 
 def _rope(x, cos, sin, positions):
@@ -84,8 +84,8 @@ def clobbers_unrelated_slot(q, k, v, positions, cos, sin, k_cache, v_cache, requ
 @pytest.mark.parametrize("dtype_label", ["fp32", "fp16", "bf16"])
 @pytest.mark.parametrize("mode", [pos.UNIFORM, pos.RAGGED])
 def test_independent_correct_implementation_passes_bit_exactly(dtype_label, mode):
-    for cfg in (Config("mha", 8, 8, 64, 4, 128, dtype_label, mode),
-                Config("gqa", 8, 2, 64, 4, 128, dtype_label, mode)):
+    for cfg in (case("mha", 8, 8, 64, 4, 128, dtype_label, mode),
+                case("gqa", 8, 2, 64, 4, 128, dtype_label, mode)):
         report = validate_candidate(correct_alternate, cfg, DEVICE, SEED)
         assert report["ok"], report["failures"]
         assert report["q_bit_exact"] and report["k_bit_exact"]
@@ -108,9 +108,9 @@ def test_broken_implementations_are_caught(broken, expect):
 
 
 def _identity_packed_case(cfg):
-    p = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, cfg.position_mode,
+    p = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, cfg.positions,
                                 SEED, 1, DEVICE)[0]
-    return ValidationCase("identity-packed", p, IDENTITY, PACKED)
+    return ValidationCase("identity-packed", p, "identity", "packed")
 
 
 @pytest.mark.parametrize("broken,case_label", [
@@ -134,14 +134,15 @@ def test_flags_on_the_report():
 
 def test_case_lists():
     ragged = validate_candidate(correct_alternate, MHA_BF16, DEVICE, SEED)
-    uniform_cfg = Config("mha", 8, 8, 64, 4, 128, "bf16", pos.UNIFORM)
+    uniform_cfg = case("mha", 8, 8, 64, 4, 128, "bf16", pos.UNIFORM)
     uniform = validate_candidate(correct_alternate, uniform_cfg, DEVICE, SEED)
     assert ragged["cases"] == ["ragged[0]", "ragged[1]", "uniform", "permuted-requests",
                                "strided-qkv"]
     assert uniform["cases"] == ["uniform[0]", "uniform[1]", "permuted-requests", "strided-qkv"]
-    cfg = Config("mha", 8, 8, 64, 4, 128, "bf16", pos.RAGGED, STRIDED, PERMUTED)
+    cfg = case("mha", 8, 8, 64, 4, 128, "bf16", pos.RAGGED, qkv_layout="fused",
+               request_order="shuffled")
     cases = validation_cases(cfg, DEVICE, SEED)
-    assert cases[0].layout == STRIDED and cases[0].request_mapping == PERMUTED
+    assert cases[0].qkv_layout == "fused" and cases[0].request_order == "shuffled"
 
 
 def test_addressing_contract():

@@ -5,8 +5,8 @@ import pytest
 import torch
 
 from decode_llm_kernel_b200.harness import positions as pos
-from decode_llm_kernel_b200.harness.workload import (HEAD_CONFIGS, PACKED, STRIDED, Config,
-                                                     build_op_args)
+from decode_llm_kernel_b200.harness.configs import HEAD_SHAPES
+from decode_llm_kernel_b200.harness.inputs import SENTINEL, case, make_inputs
 from gate import TOLERANCES, validate_candidate
 from golden_io import Golden, bits_equal, names
 from oracle import oracle
@@ -37,7 +37,7 @@ def kernel(name):
 
 def cfg_for(head_cfg, dtype_label, batch=8, alloc=128, mode=pos.RAGGED, **kw):
     label, hq, hkv, d = head_cfg
-    return Config(label, hq, hkv, d, batch, alloc, dtype_label, mode, **kw)
+    return case(label, hq, hkv, d, batch, alloc, dtype_label, mode, **kw)
 
 
 def _oracle_args(args):
@@ -88,7 +88,7 @@ def test_golden_fixture_bit_exact(name, impl):
 # ---------------------------------------------------------------- the gate over the registry
 
 @pytest.mark.parametrize("name", NAMES)
-@pytest.mark.parametrize("head_cfg", HEAD_CONFIGS, ids=[h[0] for h in HEAD_CONFIGS])
+@pytest.mark.parametrize("head_cfg", HEAD_SHAPES, ids=[h[0] for h in HEAD_SHAPES])
 @pytest.mark.parametrize("dtype_label", ["fp32", "bf16", "fp16", "fp64"])
 def test_the_gate_clears_every_registry_shape_bit_exactly(name, head_cfg, dtype_label):
     report = validate_candidate(kernel(name), cfg_for(head_cfg, dtype_label), "cuda", SEED)
@@ -100,7 +100,7 @@ def test_the_gate_clears_every_registry_shape_bit_exactly(name, head_cfg, dtype_
 
 @pytest.mark.parametrize("name", NAMES)
 def test_head_dim_96_non_power_of_two_half(name):
-    head_cfg = next(h for h in HEAD_CONFIGS if h[3] == 96)
+    head_cfg = next(h for h in HEAD_SHAPES if h[3] == 96)
     report = validate_candidate(kernel(name), cfg_for(head_cfg, "bf16", batch=33), "cuda", SEED)
     assert report["ok"] and report["q_bit_exact"] and report["k_bit_exact"]
 
@@ -116,11 +116,11 @@ def test_llama3_shape_int32_and_theta(index_dtype, theta):
 
 def test_the_two_rungs_agree_with_each_other():
     cfg = cfg_for(("mha", 32, 32, 128), "bf16")
-    p = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, cfg.position_mode, SEED,
+    p = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, cfg.positions, SEED,
                                 1, "cuda")[0]
     outs, caches = [], []
     for impl in NAMES:
-        args = build_op_args(cfg, "cuda", SEED, p)
+        args = make_inputs(cfg, "cuda", SEED, p)
         outs.append(kernel(impl)(*args))
         caches.append((args.k_cache, args.v_cache))
     assert bits_equal(outs[0], outs[1])
@@ -131,10 +131,10 @@ def test_the_two_rungs_agree_with_each_other():
 @pytest.mark.parametrize("name", NAMES)
 def test_int32_positions_match_int64(name):
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16")
-    p = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, cfg.position_mode, SEED,
+    p = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, cfg.positions, SEED,
                                 1, "cuda")[0]
-    wide = build_op_args(cfg, "cuda", SEED, p)
-    narrow = build_op_args(cfg, "cuda", SEED, p.to(torch.int32))
+    wide = make_inputs(cfg, "cuda", SEED, p)
+    narrow = make_inputs(cfg, "cuda", SEED, p.to(torch.int32))
     narrow = narrow._replace(positions=narrow.positions.to(torch.int32),
                              request_indices=narrow.request_indices.to(torch.int32))
     assert bits_equal(kernel(name)(*wide), kernel(name)(*narrow))
@@ -152,7 +152,7 @@ def test_small_token_counts(name, batch):
 @pytest.mark.parametrize("name", NAMES)
 def test_zero_tokens_is_a_no_op_not_a_crash(name):
     cfg = cfg_for(("mha", 32, 32, 128), "bf16", batch=0)
-    args = build_op_args(cfg, "cuda", SEED, torch.zeros(0, dtype=torch.long, device="cuda"))
+    args = make_inputs(cfg, "cuda", SEED, torch.zeros(0, dtype=torch.long, device="cuda"))
     q_rot = kernel(name)(*args)
     torch.cuda.synchronize()
     assert q_rot.shape == (0, 32, 128)
@@ -161,7 +161,7 @@ def test_zero_tokens_is_a_no_op_not_a_crash(name):
 @pytest.mark.parametrize("name", NAMES)
 def test_zero_token_caches_are_not_mistaken_for_aliases(name):
     cfg = cfg_for(("mha", 32, 32, 128), "bf16", batch=0)
-    args = build_op_args(cfg, "cuda", SEED, torch.zeros(0, dtype=torch.long, device="cuda"))
+    args = make_inputs(cfg, "cuda", SEED, torch.zeros(0, dtype=torch.long, device="cuda"))
     assert args.k_cache.data_ptr() == args.v_cache.data_ptr() == 0
     kernel(name)(*args)
     torch.cuda.synchronize()
@@ -183,7 +183,7 @@ def _misaligned(t, shift):
 def test_narrow_vector_paths_stay_bit_exact(dtype_label, shift):
     cfg = cfg_for(("gqa", 8, 2, 64), dtype_label, batch=5, alloc=32)
     p = pos.build_position_sets(5, 32, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     a = a._replace(q=_misaligned(a.q, shift), k=_misaligned(a.k, shift), v=_misaligned(a.v, shift))
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
@@ -196,22 +196,22 @@ def test_narrow_vector_paths_stay_bit_exact(dtype_label, shift):
 @pytest.mark.parametrize("name", NAMES)
 def test_a_strided_qkv_view_is_not_copied_first(name):
     cfg = cfg_for(("mha96", 32, 32, 96), "bf16")
-    p = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, cfg.position_mode, SEED,
+    p = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, cfg.positions, SEED,
                                 1, "cuda")[0]
-    strided = build_op_args(cfg, "cuda", SEED, p, layout=STRIDED)
+    strided = make_inputs(cfg, "cuda", SEED, p, qkv_layout="fused")
     assert not strided.q.is_contiguous()
     ref = _oracle_args(strided)
     expected = oracle.fused_rope_kv_append(*ref)
     assert bits_equal(kernel(name)(*strided).cpu(), expected)
-    packed = build_op_args(cfg, "cuda", SEED, p, layout=PACKED)
+    packed = make_inputs(cfg, "cuda", SEED, p, qkv_layout="packed")
     assert packed.q.is_contiguous()
 
 
 @pytest.mark.parametrize("dtype_label", ["bf16", "fp16", "fp32"])
 def test_partial_rotary_phi2_shape(dtype_label):
-    cfg = Config("phi2", 32, 32, 80, 16, 64, dtype_label, pos.RAGGED, rotary_dim=32)
+    cfg = case("phi2", 32, 32, 80, 16, 64, dtype_label, pos.RAGGED, rotary_dim=32)
     p = pos.build_position_sets(16, 64, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     assert a.cos.shape == (64, 32)
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
@@ -225,9 +225,9 @@ def test_partial_rotary_phi2_shape(dtype_label):
 
 @pytest.mark.parametrize("dtype_label", ["bf16", "fp16"])
 def test_head_major_cache(dtype_label):
-    cfg = Config("gqa", 32, 8, 128, 8, 64, dtype_label, pos.RAGGED, cache_layout="head_major")
+    cfg = case("gqa", 32, 8, 128, 8, 64, dtype_label, pos.RAGGED, cache_layout="head_major")
     p = pos.build_position_sets(8, 64, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     assert not a.k_cache.is_contiguous()
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
@@ -243,9 +243,9 @@ def test_head_major_cache(dtype_label):
 @pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])
 def test_paged_cache_matches_the_contiguous_oracle(block_size, index_dtype):
     T, Hq, Hkv, D, S = 12, 32, 8, 128, 256
-    cfg = Config("gqa", Hq, Hkv, D, T, S, "bf16", pos.RAGGED)
+    cfg = case("gqa", Hq, Hkv, D, T, S, "bf16", pos.RAGGED)
     p = pos.build_position_sets(T, S, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     max_blocks = S // block_size
     num_blocks = T * max_blocks + 3
     g = torch.Generator().manual_seed(SEED)
@@ -274,7 +274,7 @@ def test_in_register_trig_within_the_reference_tolerance():
     from decode_llm_kernel_b200.rope_tables import inverse_frequencies
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=64, alloc=4096, theta=500000.0)
     p = pos.build_position_sets(64, 4096, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
     inv = inverse_frequencies(128, 500000.0).cuda()
@@ -298,9 +298,9 @@ def _assert_inreg_close(q, q_ref):
 @pytest.mark.parametrize("name", NAMES)
 def test_capturable_into_a_cuda_graph(name):
     cfg = cfg_for(("mha", 32, 32, 128), "bf16")
-    sets = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, cfg.position_mode,
+    sets = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, cfg.positions,
                                    SEED, 2, "cuda")
-    args = build_op_args(cfg, "cuda", SEED, sets[0])
+    args = make_inputs(cfg, "cuda", SEED, sets[0])
     static_positions = args.positions.clone()
     bound = args._replace(positions=static_positions)
     fn = kernel(name)
@@ -316,7 +316,7 @@ def test_capturable_into_a_cuda_graph(name):
     static_positions.copy_(sets[1])
     graph.replay()
     torch.cuda.synchronize()
-    expected_args = _oracle_args(build_op_args(cfg, "cuda", SEED, sets[1]))
+    expected_args = _oracle_args(make_inputs(cfg, "cuda", SEED, sets[1]))
     expected = oracle.fused_rope_kv_append(*expected_args)
     assert bits_equal(captured.cpu(), expected)
     ri, p1 = bound.request_indices.cpu(), sets[1].cpu()
@@ -386,7 +386,7 @@ def test_end_to_end_graph_copies_host_buffers():
 def test_runs_on_a_non_default_stream():
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16")
     p = pos.build_position_sets(8, 128, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p)
+    a = make_inputs(cfg, "cuda", SEED, p)
     ref = _oracle_args(a)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -402,8 +402,8 @@ def test_out_of_range_positions_set_status_and_skip_writes():
     from decode_llm_kernel_b200 import cuda
     cuda.read_status(clear=True)
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=4, alloc=16)
-    a = build_op_args(cfg, "cuda", SEED, torch.tensor([0, 3, 16, 5], device="cuda"),
-                      sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, torch.tensor([0, 3, 16, 5], device="cuda"),
+                      cache_fill=SENTINEL)
     ops().fused_rope_kv_append(*a)
     word = cuda.read_status(clear=False)
     assert word & 1 and word & 4          # outside the cache and outside the table
@@ -414,12 +414,40 @@ def test_out_of_range_positions_set_status_and_skip_writes():
     kc = a.k_cache.cpu()
     assert bool((kc[2] == 7.5).all())
     assert not bool((kc[0, 0] == 7.5).all())
-    a2 = build_op_args(cfg, "cuda", SEED, torch.tensor([0, 3, 15, 5], device="cuda"),
-                       sentinel_cache=True)
+    a2 = make_inputs(cfg, "cuda", SEED, torch.tensor([0, 3, 15, 5], device="cuda"),
+                       cache_fill=SENTINEL)
     ops().fused_rope_kv_append(*a2)
     a2r = a2._replace(request_indices=torch.tensor([0, 1, 9, 3], device="cuda"))
     ops().fused_rope_kv_append(*a2r)
     assert cuda.read_status() & 2
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_a_position_past_a_short_table_keeps_its_k_slot_in_both_ops(name):
+    """A cos/sin table shorter than the cache: the token whose position is inside the cache but
+    past the table sets the out-of-table bit and keeps its K slot (the separate op's append is
+    told the table length, so it never copies the k_rot row the rope step left unwritten); its
+    V slot is written, as in the fused op; every other token lands bit-exact."""
+    from decode_llm_kernel_b200 import cuda
+    cuda.read_status(clear=True)
+    cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=4, alloc=32)
+    a = make_inputs(cfg, "cuda", SEED, torch.tensor([0, 3, 20, 5], device="cuda"),
+                    cache_fill=SENTINEL)
+    a = a._replace(cos=a.cos[:16].contiguous(), sin=a.sin[:16].contiguous())
+    for _ in range(2):                    # twice: a stale k_rot row from call 1 stays unused
+        kernel(name)(*a)
+        torch.cuda.synchronize()
+        assert cuda.read_status() & 4     # DRK_STATUS_POSITION_OUT_OF_TABLE
+        kc, vc = a.k_cache.cpu(), a.v_cache.cpu()
+        assert bool((kc[2, 20] == SENTINEL).all()), "K slot past the table was written"
+        assert bits_equal(vc[2, 20], a.v[2].cpu())
+        ok = torch.tensor([0, 1, 3])
+        sub = a._replace(q=a.q[ok], k=a.k[ok], v=a.v[ok], positions=a.positions[ok],
+                         request_indices=a.request_indices[ok])
+        ref = _oracle_args(sub)
+        q_ref, k_ref = oracle.rope_forward(ref[0], ref[1], ref[3], ref[4], ref[5])
+        r, p = ref[8].long(), ref[3].long()
+        assert bits_equal(kc[r, p], k_ref)
 
 
 # ---------------------------------------------------------------- errors (reference messages)
@@ -427,7 +455,7 @@ def test_out_of_range_positions_set_status_and_skip_writes():
 def _small():
     cfg = cfg_for(("mha", 32, 32, 128), "bf16", batch=2)
     p = pos.build_position_sets(2, 128, pos.RAGGED, SEED, 1, "cuda")[0]
-    return build_op_args(cfg, "cuda", SEED, p)
+    return make_inputs(cfg, "cuda", SEED, p)
 
 
 def test_a_cache_dtype_mismatch_is_refused_rather_than_silently_cast():
@@ -469,7 +497,7 @@ def test_one_buffer_used_as_both_caches_is_refused(name):
 def test_rope_forward_returns_a_contiguous_tuple():
     cfg = cfg_for(("gqa", 32, 8, 128), "fp32", batch=2)
     p = pos.build_position_sets(2, 128, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p)
+    a = make_inputs(cfg, "cuda", SEED, p)
     from decode_llm_kernel_b200 import cuda
     out = cuda.require().rope_forward(a.q, a.k, a.positions, a.cos, a.sin)
     assert isinstance(out, tuple)
@@ -490,14 +518,14 @@ def test_fp32_margin_is_zero():
 # ---------------------------------------------------------------- the bulk-copy (staged) kernel
 
 @pytest.mark.parametrize("dtype_label", ["bf16", "fp16", "fp32", "fp64"])
-@pytest.mark.parametrize("head_cfg", HEAD_CONFIGS, ids=[h[0] for h in HEAD_CONFIGS])
-@pytest.mark.parametrize("layout", [PACKED, STRIDED])
+@pytest.mark.parametrize("head_cfg", HEAD_SHAPES, ids=[h[0] for h in HEAD_SHAPES])
+@pytest.mark.parametrize("layout", ["packed", "fused"])
 def test_staged_kernel_bit_exact(dtype_label, head_cfg, layout):
     """Large token counts take the staged kernel by default; force it and compare."""
-    cfg = cfg_for(head_cfg, dtype_label, batch=1100, alloc=64, layout=layout,
-                  request_mapping="permuted")
+    cfg = cfg_for(head_cfg, dtype_label, batch=1100, alloc=64, qkv_layout=layout,
+                  request_order="shuffled")
     p = pos.build_position_sets(1100, 64, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
     for path in ("staged", "auto"):
@@ -510,9 +538,9 @@ def test_staged_kernel_bit_exact(dtype_label, head_cfg, layout):
 
 @pytest.mark.parametrize("T", [1, 7, 148, 1000])
 def test_staged_kernel_token_counts_and_partial_rotary(T):
-    cfg = Config("phi2", 32, 32, 80, T, 128, "fp16", pos.RAGGED, rotary_dim=32)
+    cfg = case("phi2", 32, 32, 80, T, 128, "fp16", pos.RAGGED, rotary_dim=32)
     p = pos.build_position_sets(T, 128, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
     q = ops().fused_rope_kv_append_ex(*a, rotary_dim=32, path="staged")
@@ -523,9 +551,9 @@ def test_staged_kernel_token_counts_and_partial_rotary(T):
 
 def test_staged_kernel_paged_cache():
     T, Hq, Hkv, D, S, bs = 400, 32, 8, 128, 256, 16
-    cfg = Config("gqa", Hq, Hkv, D, T, S, "bf16", pos.RAGGED, request_mapping="permuted")
+    cfg = case("gqa", Hq, Hkv, D, T, S, "bf16", pos.RAGGED, request_order="shuffled")
     p = pos.build_position_sets(T, S, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     max_blocks = S // bs
     num_blocks = T * max_blocks + 5
     perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(3))[
@@ -549,7 +577,7 @@ def test_staged_kernel_out_of_range_and_pdl():
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=300, alloc=32)
     p = torch.randint(0, 32, (300,), generator=torch.Generator().manual_seed(1))
     p[5] = 32        # outside the cache and the table
-    a = build_op_args(cfg, "cuda", SEED, p.cuda(), sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p.cuda(), cache_fill=SENTINEL)
     q = ops().fused_rope_kv_append_ex(*a, path="staged", pdl=True)
     assert cuda.read_status() & 5
     kc = a.k_cache.cpu()
@@ -558,7 +586,7 @@ def test_staged_kernel_out_of_range_and_pdl():
     good[5] = False
     pv = p.clone()
     pv[5] = 0
-    a2 = build_op_args(cfg, "cuda", SEED, pv.cuda(), sentinel_cache=True)
+    a2 = make_inputs(cfg, "cuda", SEED, pv.cuda(), cache_fill=SENTINEL)
     ref = _oracle_args(a2)
     q_ref = oracle.fused_rope_kv_append(*ref)
     assert bits_equal(q.cpu()[good], q_ref[good])
@@ -607,7 +635,7 @@ def test_staged_kernel_in_register_trig_within_the_reference_tolerance():
     from decode_llm_kernel_b200.rope_tables import inverse_frequencies
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=700, alloc=4096, theta=500000.0)
     p = pos.build_position_sets(700, 4096, pos.RAGGED, SEED, 1, "cuda")[0]
-    a = build_op_args(cfg, "cuda", SEED, p, sentinel_cache=True)
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
     ref = _oracle_args(a)
     q_ref = oracle.fused_rope_kv_append(*ref)
     inv = inverse_frequencies(128, 500000.0).cuda()
@@ -654,27 +682,25 @@ def test_decode_loop_advances_positions_on_the_device():
 
 @pytest.mark.parametrize("label", ["graph_cuda_fused", "graph_cuda_separate", "cuda_fused",
                                    "cuda_separate"])
-def test_harness_runners_drive_the_ops(label):
-    """The reference's runners (benchmarks/impls.py:81-167) over this build's ops: the graph
-    runner copies new positions into its static buffer before each replay and recaptures when
-    an input pointer changes; every call lands bit-exact."""
-    from decode_llm_kernel_b200.harness import impls
-    spec = impls.resolve_impls([label])[0]
-    runner = spec.build()
+def test_ladder_runners_drive_the_ops(label):
+    """The operator ladder's drivers (harness/runners.py) over this build's ops: the eager
+    runner calls through the binding, the graph runner replays one graph per device position
+    set; every call in a rotation over three sets lands bit-exact, twice round."""
+    from decode_llm_kernel_b200.harness import runners
+    _, op_name, kind = next(r for r in runners.RUNGS if r[0] == label)
+    op = kernel(op_name)
     cfg = cfg_for(("gqa", 32, 8, 128), "bf16", batch=8, alloc=64)
     sets = pos.build_position_sets(8, 64, pos.RAGGED, SEED, 3, "cuda")
-    args = build_op_args(cfg, "cuda", SEED, sets[0])
-    for p in sets:
-        call_args = args._replace(positions=p)
-        out = runner(*call_args)
+    args = make_inputs(cfg, "cuda", SEED, sets[0])
+    runner = kind(op, args, sets)
+    for i in range(6):
+        p = sets[i % 3]
+        expect_in = _oracle_args(args._replace(positions=p))
+        out = runner()
         torch.cuda.synchronize()
-        ref = _oracle_args(call_args)
-        assert bits_equal(out.cpu(), oracle.fused_rope_kv_append(*ref))
-    if spec.graph:
-        assert runner.capture_count == 1
-        other = build_op_args(cfg, "cuda", SEED + 1, sets[0])
-        out = runner(*other)
-        torch.cuda.synchronize()
-        assert runner.capture_count == 2
-        assert bits_equal(out.cpu(), oracle.fused_rope_kv_append(*_oracle_args(other)))
-        runner.release()
+        # the oracle sees the caches as they were before this call
+        q_ref = oracle.fused_rope_kv_append(*expect_in)
+        assert bits_equal(out.cpu(), q_ref), (label, i)
+        assert bits_equal(args.k_cache.cpu(), expect_in[6]), (label, i)
+        assert bits_equal(args.v_cache.cpu(), expect_in[7]), (label, i)
+    runner.release()

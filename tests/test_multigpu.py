@@ -27,7 +27,7 @@ def _worker(rank, world, port, result_path):
     from decode_llm_kernel_b200.cuda import ops
     from decode_llm_kernel_b200.harness import positions as pos
     from decode_llm_kernel_b200.harness import sharding
-    from decode_llm_kernel_b200.harness.workload import Config, build_op_args
+    from decode_llm_kernel_b200.harness.inputs import SENTINEL, case, make_inputs
     from oracle import oracle
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -37,13 +37,13 @@ def _worker(rank, world, port, result_path):
                             device_id=torch.device("cuda", rank))
     ok = True
     try:
-        for kind, cfg in (("batch", Config("gqa", 32, 8, 128, 1024, 64, "fp16", pos.RAGGED,
-                                           request_mapping="permuted")),
-                          ("kv_head", Config("gqa70b", 64, 8, 128, 64, 64, "bf16", pos.RAGGED,
+        for kind, cfg in (("batch", case("gqa", 32, 8, 128, 1024, 64, "fp16", pos.RAGGED,
+                                           request_order="shuffled")),
+                          ("kv_head", case("gqa70b", 64, 8, 128, 64, 64, "bf16", pos.RAGGED,
                                              theta=500000.0))):
-            p = pos.build_position_sets(cfg.num_requests, cfg.cache_alloc_len, pos.RAGGED, 1234,
+            p = pos.build_position_sets(cfg.batch, cfg.cache_alloc_len, pos.RAGGED, 1234,
                                         1, "cpu")[0]
-            full = build_op_args(cfg, "cpu", 1234, p, sentinel_cache=True)
+            full = make_inputs(cfg, "cpu", 1234, p, cache_fill=SENTINEL)
             if kind == "batch":
                 local, tokens = sharding.shard_batch(full, rank, world)
             else:
@@ -53,7 +53,7 @@ def _worker(rank, world, port, result_path):
             torch.cuda.synchronize()
             if kind == "batch":
                 q_all, k_all, v_all = sharding.gather_batch_shards(
-                    q, tokens.cuda(), dev.k_cache, dev.v_cache, cfg.num_requests)
+                    q, tokens.cuda(), dev.k_cache, dev.v_cache, cfg.batch)
             else:
                 q_all, k_all, v_all = sharding.gather_kv_head_shards(q, dev.k_cache, dev.v_cache)
             if rank == 0:

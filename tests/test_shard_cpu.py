@@ -10,7 +10,7 @@ import torch.multiprocessing as mp
 
 from decode_llm_kernel_b200.harness import positions as pos
 from decode_llm_kernel_b200.harness.configs import WORKLOADS
-from decode_llm_kernel_b200.harness.workload import Config, build_op_args
+from decode_llm_kernel_b200.harness.inputs import SENTINEL, case, make_inputs
 
 
 def _free_port():
@@ -37,7 +37,7 @@ def test_workload_shards():
 
 
 def _cfg(mapping):
-    return Config("gqa", 16, 4, 64, 8, 32, "bf16", pos.RAGGED, request_mapping=mapping,
+    return case("gqa", 16, 4, 64, 8, 32, "bf16", pos.RAGGED, request_order=mapping,
                   theta=500000.0)
 
 
@@ -50,7 +50,7 @@ def _worker(rank, world, port, kind, mapping, result_path):
     try:
         cfg = _cfg(mapping)
         p = pos.build_position_sets(8, 32, pos.RAGGED, 1234, 1, "cpu")[0]
-        args = build_op_args(cfg, "cpu", 1234, p, sentinel_cache=True)
+        args = make_inputs(cfg, "cpu", 1234, p, cache_fill=SENTINEL)
         if kind == "kv_head":
             local = sharding.shard_kv_heads(args, rank, world)
             q = oracle.fused_rope_kv_append(*local)
@@ -73,7 +73,7 @@ def _worker(rank, world, port, kind, mapping, result_path):
 
 
 @pytest.mark.parametrize("kind,mapping", [("kv_head", "identity"), ("batch", "identity"),
-                                          ("batch", "permuted")])
+                                          ("batch", "shuffled")])
 def test_two_gloo_ranks_reassemble_the_unsharded_result(tmp_path, kind, mapping):
     result = tmp_path / "result.txt"
     ctx = mp.get_context("spawn")

@@ -3,9 +3,11 @@
 It is for callers that cannot allocate device memory when they launch the op (global-mode
 stream capture, runtimes that gave all free HBM to their cache pool, hosts without a device
 allocator): its k_rot intermediate lives in an 8 MiB static device array inside the library.
-The test compares it with the existing separate op (ops.separate_rope_kv_append, which
+The tests compare it with the existing separate op (ops.separate_rope_kv_append, which
 allocates k_rot through PyTorch) on two calls in a row -- bit for bit, the tolerance every
-kernel test here uses -- and checks that an over-size call is refused before any launch.
+kernel test here uses -- and check that an over-size call is refused before any launch, that
+argument errors are reported before the size check, and that a token past a short cos/sin table
+keeps its K slot although the shared array holds an earlier call's rows.
 
 The file name sorts last so a run that stops at the first failure has run every other test.
 """
@@ -53,12 +55,13 @@ def lib():
     return handle
 
 
-def noalloc(lib, q, k, v, positions, cos, sin, k_cache, v_cache, request_indices):
+def noalloc(lib, q, k, v, positions, cos, sin, k_cache, v_cache, request_indices, status=None):
     q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     ds = [desc(t) for t in (q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
                             q_out)]
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = lib.drk_separate_rope_kv_append_noalloc(*[ctypes.byref(d) for d in ds], None, stream)
+    word = None if status is None else ctypes.c_void_p(status.data_ptr())
+    rc = lib.drk_separate_rope_kv_append_noalloc(*[ctypes.byref(d) for d in ds], word, stream)
     return rc, q_out
 
 
@@ -109,3 +112,43 @@ def test_an_oversize_intermediate_is_refused_before_any_launch(lib):
     torch.cuda.synchronize()
     assert torch.equal(_bits(args[6]), _bits(before[0]))
     assert torch.equal(_bits(args[7]), _bits(before[1]))
+
+
+def test_a_position_past_a_short_table_keeps_its_k_slot(lib):
+    """The scratch array keeps the previous call's k_rot rows. A token inside the cache but past
+    a short cos/sin table gets no k_rot row from the rope step, and the append step must not
+    copy the stale one: its K slot keeps its old contents, the out-of-table status bit is set,
+    its V slot is written, and every other token matches the allocating separate op."""
+    from decode_llm_kernel_b200 import cuda
+    from decode_llm_kernel_b200.cuda import ops
+    args = _args(99, T=8, S=64)
+    noalloc(lib, *_args(98, T=8, S=64))   # leave other values in the shared array first
+    args[3] = torch.tensor([0, 5, 40, 7, 1, 2, 3, 4], device="cuda")
+    args[4], args[5] = args[4][:32].contiguous(), args[5][:32].contiguous()
+    ref = list(args)
+    ref[6], ref[7] = args[6].clone(), args[7].clone()
+    before = args[6].clone()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc, q_out = noalloc(lib, *args, status=status)
+    assert rc == 0, lib.drk_last_error().decode()
+    cuda.read_status(clear=True)
+    q_ref = ops.separate_rope_kv_append(*ref)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 4            # DRK_STATUS_POSITION_OUT_OF_TABLE
+    r2 = int(args[8][2])
+    assert torch.equal(_bits(args[6][r2, 40]), _bits(before[r2, 40]))
+    assert torch.equal(_bits(args[7][r2, 40]), _bits(args[2][2]))
+    assert torch.equal(_bits(args[6]), _bits(ref[6]))
+    assert torch.equal(_bits(args[7]), _bits(ref[7]))
+    keep = torch.tensor([0, 1, 3, 4, 5, 6, 7], device="cuda")
+    assert torch.equal(_bits(q_out[keep]), _bits(q_ref[keep]))
+
+
+def test_argument_errors_come_before_the_size_check(lib):
+    """A malformed call is refused with the regular message even when its k_rot would not fit
+    the scratch array."""
+    args = _args(7, T=4097, Hq=1, Hkv=8, D=128, S=2)
+    args[3] = args[3].cpu()
+    rc, _ = noalloc(lib, *args)
+    assert rc == -1
+    assert "must be a CUDA tensor" in lib.drk_last_error().decode()
