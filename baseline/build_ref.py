@@ -9,9 +9,10 @@ the GPU machines with the working tree).
    it (its setup.py:11,45) -- builds its CUDA extension decode_kernels.cuda._ext for sm_100a.
    The reference's setup() declares no Python packages, so this installs the compiled module
    alone.
-2. The reference's Python sources beside it, as a package install would lay them out:
-   decode_kernels/ (its cuda wrapper and its PyTorch oracle, decode_kernels/reference), the
-   benchmarks/ harness, tests/, conftest.py and setup.py (its tests import setup.py).
+2. The reference's sources beside it, as its checkout lays them out: decode_kernels/ (its cuda
+   wrapper and its PyTorch oracle, decode_kernels/reference), the benchmarks/ harness, tests/,
+   conftest.py, and setup.py with csrc/ (its build-contract tests import setup.py and list
+   csrc/).
 
 What uses it: bench.py's reference_gpu measurement (the reference's kernels, rebuilt for
 sm_100a, on the same GPU) and cpu_baseline_torch (the reference's PyTorch oracle on the host
@@ -30,7 +31,7 @@ import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 TARGET = os.path.join(HERE, "_ref")
-PY_TREES = ("decode_kernels", "benchmarks", "tests")
+PY_TREES = ("decode_kernels", "benchmarks", "tests", "csrc")
 PY_FILES = ("conftest.py", "setup.py")
 
 

@@ -300,18 +300,40 @@ def differing(a, b):
     return int((_bits(a) != _bits(b)).sum().item())
 
 
+def _ordered(t):
+    """Integer keys of a float tensor whose differences count ulps (+0 and -0 coincide)."""
+    b = _bits(t).to(torch.int64)
+    magnitude = b & ((1 << (8 * t.element_size() - 1)) - 1)
+    return torch.where(b < 0, -magnitude, b)
+
+
+def max_ulp(a, b):
+    if a.numel() == 0:
+        return 0
+    return int((_ordered(a) - _ordered(b)).abs().max().item())
+
+
 def check_call(q, k, v, pos, ri, cos, sin, q_out, k_cache, v_cache, rotary):
     """One call's outputs against rope_torch: q_out, and the K and V slots [ri, pos] of the
-    caches (which must hold this call's writes). Returns mismatching element counts."""
+    caches (which must hold this call's writes). Returns mismatching element counts and the
+    largest distance in ulps of the storage type."""
     idx_r, idx_p = ri.long(), pos.long()
-    return {"q": differing(q_out, rope_torch(q, pos, cos, sin, rotary)),
-            "k_slots": differing(k_cache[idx_r, idx_p], rope_torch(k, pos, cos, sin, rotary)),
-            "v_slots": differing(v_cache[idx_r, idx_p], v)}
+    q_ref, k_ref = rope_torch(q, pos, cos, sin, rotary), rope_torch(k, pos, cos, sin, rotary)
+    k_got = k_cache[idx_r, idx_p]
+    return {"q": differing(q_out, q_ref), "k_slots": differing(k_got, k_ref),
+            "v_slots": differing(v_cache[idx_r, idx_p], v),
+            "max_ulp": max(max_ulp(q_out, q_ref), max_ulp(k_got, k_ref)),
+            "elements": q_ref.numel() + k_ref.numel()}
 
 
 def parity_label(counts):
-    total = sum(counts.values())
-    return "bit-exact" if total == 0 else f"MISMATCH {counts}"
+    bad = counts["q"] + counts["k_slots"] + counts["v_slots"]
+    if bad == 0:
+        return "bit-exact"
+    if counts["v_slots"] == 0 and counts["max_ulp"] <= 1:
+        return (f"within 1 ulp: {counts['q'] + counts['k_slots']} of {counts['elements']} "
+                "rotated elements differ by 1 ulp, V bit-exact")
+    return f"MISMATCH {counts}"
 
 
 PARITY_NOTE = ("after the timed region one sampled input set's call is issued again; its q_out "
@@ -513,17 +535,18 @@ def reference_decode_step(ref, k_caches, v_caches, sets, cos, sin, steps, warmup
     graphs[0].replay()
     torch.cuda.synchronize()
     s0 = sets[0]
-    bad = 0
+    bad = {"q": 0, "k_slots": 0, "v_slots": 0, "max_ulp": 0, "elements": 0}
     for layer in range(w.layers):
         counts = check_call(s0.q[layer], s0.k[layer], s0.v[layer], s0.positions,
                             s0.request_indices, cos, sin, outs[0][layer], k_caches[layer],
                             v_caches[layer], w.rotary)
-        bad += sum(counts.values())
+        for key in bad:
+            bad[key] = max(bad[key], counts[key]) if key == "max_ulp" else bad[key] + counts[key]
     del graphs, outs
     per_step_us = ms * 1e3 / steps
     return {"us_per_step": per_step_us, "us_per_layer": per_step_us / w.layers,
             "achieved_gbs": w.bytes_per_step() / (per_step_us * 1e-6) / 1e9,
-            "parity": "bit-exact" if bad == 0 else f"MISMATCH {bad} elements",
+            "parity": parity_label(bad),
             "kernel": "reference cuda_fused (its csrc kernel rebuilt for sm_100a), 32 launches "
                       "per graph"}
 
@@ -566,13 +589,14 @@ def run_ours(args, world, rank, local):
     # parity of the timed step: input set 0 replayed once more, every layer checked
     captured[0].replay()
     torch.cuda.synchronize()
-    s0, bad = sets[0], {"q": 0, "k_slots": 0, "v_slots": 0}
+    s0 = sets[0]
+    bad = {"q": 0, "k_slots": 0, "v_slots": 0, "max_ulp": 0, "elements": 0}
     for layer in range(w.layers):
         counts = check_call(s0.q[layer], s0.k[layer], s0.v[layer], s0.positions,
                             s0.request_indices, cos, sin, captured[0].q_out[layer],
                             k_caches[layer], v_caches[layer], w.rotary)
         for key in bad:
-            bad[key] += counts[key]
+            bad[key] = max(bad[key], counts[key]) if key == "max_ulp" else bad[key] + counts[key]
     parity = {"result": parity_label(bad), "layers_checked": w.layers, "how": PARITY_NOTE}
 
     per_step_s = ms_max / 1e3 / args.steps

@@ -10,7 +10,9 @@ import os
 
 import torch  # noqa: F401  -- loads libc10/libtorch, without which _ext's symbols do not resolve
 
-BUILD_COMMAND = "python -m decode_llm_kernel_b200._build"
+# The reference's build command, run in this project's checkout (setup.py there builds the
+# library and the binding in place; `python -m decode_llm_kernel_b200._build` does the same).
+BUILD_COMMAND = "python setup.py build_ext --inplace"
 
 _PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 _IMPORT_ERROR = None
@@ -36,7 +38,8 @@ def require():
     """The extension module, or a RuntimeError that says how to get one."""
     if _ext is None:
         raise RuntimeError(f"the CUDA extension is not importable -- build it with "
-                           f"'{BUILD_COMMAND}'. Underlying error: {_IMPORT_ERROR}")
+                           f"'{BUILD_COMMAND}' in {os.path.dirname(os.path.dirname(_PKG_DIR))}. "
+                           f"Underlying error: {_IMPORT_ERROR}")
     return _ext
 
 

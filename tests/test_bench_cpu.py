@@ -75,3 +75,22 @@ def test_the_bench_parity_restatement_matches_the_oracle():
             q_ref, k_ref = oracle.rope_forward(q, k, pos, cos, sin)
             assert bench.differing(bench.rope_torch(q, pos, cos, sin, R), q_ref) == 0, (dt, D, R)
             assert bench.differing(bench.rope_torch(k, pos, cos, sin, R), k_ref) == 0, (dt, D, R)
+
+
+def test_ulp_distance_of_the_parity_report():
+    import torch
+    sys.path.insert(0, ROOT)
+    import bench
+    one = torch.tensor([1.0], dtype=torch.bfloat16)
+    up = torch.nextafter(torch.tensor([1.0]), torch.tensor([2.0])).to(torch.bfloat16)
+    nxt = (one.view(torch.int16) + 1).view(torch.bfloat16)
+    assert bench.max_ulp(one, nxt) == 1 and bench.max_ulp(nxt, one) == 1
+    assert bench.max_ulp(torch.tensor([0.0]), torch.tensor([-0.0])) == 0
+    neg = -one
+    assert bench.max_ulp(neg, (neg.view(torch.int16) + 1).view(torch.bfloat16)) == 1
+    assert bench.max_ulp(torch.tensor([-1e-45]), torch.tensor([1e-45])) == 2   # across zero
+    assert bench.max_ulp(one, up) == 0                    # 1 + fp32 ulp rounds back to 1
+    counts = {"q": 3, "k_slots": 1, "v_slots": 0, "max_ulp": 1, "elements": 100}
+    assert bench.parity_label(counts).startswith("within 1 ulp")
+    assert bench.parity_label(dict(counts, max_ulp=2)).startswith("MISMATCH")
+    assert bench.parity_label(dict(counts, q=0, k_slots=0, max_ulp=0)) == "bit-exact"
