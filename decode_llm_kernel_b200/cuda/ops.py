@@ -42,7 +42,7 @@ def fused_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request
 
 def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
                             *, rotary_dim=0, pdl=False, strided_cache=False, inv_freq=None,
-                            q_out=None, path="auto"):
+                            q_out=None, path="auto", row_splits=0):
     """fused_rope_kv_append with:
     rotary_dim     rotate only the first rotary_dim dims (table [P, rotary_dim]), copy the rest;
     pdl            programmatic dependent launch (indices and table read before waiting on the
@@ -55,10 +55,12 @@ def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, requ
     path           "auto" (default), "register" (the register kernel) or "staged" (the
                    bulk-copy kernel that stages tokens through shared memory; refused with a
                    RuntimeError when the layout does not allow it). "auto" takes the staged
-                   kernel for large token counts when it can."""
+                   kernel for large token counts when it can;
+    row_splits     register kernel: CTAs that share one token's head rows (0 = chosen by the
+                   library from the token count)."""
     return require().fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache,
                                              request_indices, rotary_dim, pdl, strided_cache,
-                                             inv_freq, q_out, path)
+                                             inv_freq, q_out, path, row_splits)
 
 
 def paged_rope_kv_append(q, k, v, positions, cos, sin, k_pages, v_pages, block_table,
