@@ -686,15 +686,19 @@ def run_ours(args, world, rank, local):
         pipe.release()
         del hosts, dev_sets
 
-    floor = None if args.no_floor else launch_floor(stream, w.layers)
-    if floor is not None:
-        # The layer launch against the graph-node floor: without PDL (an empty kernel per graph
-        # node, the floor the reference measures with no PDL in its graphs) and with PDL (the
-        # chain this step runs).
+    floor = None
+    if not args.no_floor:
+        # one layer reads (and writes) half its algorithmic bytes; the fused kernel's 1-row
+        # launch shape for this batch is 192-thread CTAs
+        floor = launch_floor(stream, w.layers, copy_bytes=w.bytes_per_call() // 2 // 32 * 32)
+        # The layer launch against the floors: the graph node without PDL (an empty kernel per
+        # node, the floor the reference measures, with no PDL in its graphs), with PDL (the
+        # chain this step runs), and the dependent copy with the layer's memory pattern.
         us_launch = per_launch_s * 1e6
         floor["layer_us"] = us_launch
         floor["layer_vs_graph_node"] = us_launch / floor["graph_us_per_node"]
         floor["layer_vs_graph_node_pdl"] = us_launch / floor["graph_us_per_node_pdl"]
+        floor["layer_vs_dependent_copy"] = us_launch / floor["dependent_copy_us_per_node"]
 
     ref, ref_why = (None, "skipped")
     if world == 1 and not args.no_reference_gpu:
@@ -1073,9 +1077,17 @@ def strong_scaling_record(bw, tp, world):
     return out
 
 
-def launch_floor(stream, layers):
-    """Empty-kernel floor: direct launches (amortised) and a graph of `layers` chained empty
-    kernels, with and without programmatic dependent launch."""
+def launch_floor(stream, layers, copy_bytes=0, copy_threads=192, sets=10):
+    """Launch floors of a chain of `layers` launches in one CUDA graph, per node:
+      graph_us_per_node[_pdl]   empty kernels (the floor the reference measures), without and
+                                with programmatic dependent launch;
+      dependent_copy_us_per_node  a copy with one layer's memory pattern (copy_bytes read and
+                                written, two 16-byte vectors per thread, copy_threads per CTA,
+                                source lines pulled toward L2 during the wait, PDL), rotating
+                                over `sets` buffer sets larger than L2 like the decode step's
+                                inputs: the cost of a chained launch that reads after the
+                                previous launch and writes before the next;
+      direct_us[_pdl]           empty kernels launched one by one from the host (amortised)."""
     from decode_llm_kernel_b200 import cuda
     ext = cuda.require()
     out = {}
@@ -1105,7 +1117,32 @@ def launch_floor(stream, layers):
         end.record(stream)
         torch.cuda.synchronize()
         out[f"graph_us_per_node{'_pdl' if pdl else ''}"] = start.elapsed_time(end) * 1e3 / (500 * layers)
+    if copy_bytes:
+        out.update(copy_floor(ext, stream, layers, copy_bytes, copy_threads, sets))
     return out
+
+
+def copy_floor(ext, stream, layers, copy_bytes, threads, sets, replays=200):
+    span = layers * copy_bytes
+    src = torch.empty(sets * span, dtype=torch.uint8, device="cuda")
+    dst = torch.empty_like(src)
+    src.random_(0, 255)
+    graphs = []
+    for s in range(sets):
+        chunk_s, chunk_d = src[s * span:(s + 1) * span], dst[s * span:(s + 1) * span]
+        ext.launch_copy_probe(chunk_s, chunk_d, copy_bytes, copy_bytes, layers, threads)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ext.launch_copy_probe(chunk_s, chunk_d, copy_bytes, copy_bytes, layers, threads)
+        graphs.append(g)
+    for i in range(3 * sets):
+        graphs[i % sets].replay()
+    ms = time_graph_steps(graphs, replays, stream)
+    ok = torch.equal(src[:span], dst[:span])
+    del graphs, src, dst
+    return {"dependent_copy_us_per_node": ms * 1e3 / (replays * layers),
+            "dependent_copy": {"bytes_read_per_node": copy_bytes, "threads_per_cta": threads,
+                               "prefetch": True, "pdl": True, "copied_correctly": ok}}
 
 
 def run_reference(args, world, rank):

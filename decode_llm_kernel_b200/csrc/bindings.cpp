@@ -424,6 +424,22 @@ void launch_empty(int64_t count, bool pdl) {
                                   at::cuda::getCurrentCUDAStream(device).stream()));
 }
 
+// The dependent-copy floor probe over two device tensors, whose sizes bound every launch.
+void launch_copy_probe(at::Tensor src, at::Tensor dst, int64_t bytes, int64_t stride_bytes,
+                       int64_t count, int64_t threads, bool pdl, bool prefetch) {
+  TORCH_CHECK(src.is_cuda() && dst.is_cuda() && src.get_device() == dst.get_device(),
+              "src and dst must be CUDA tensors on one device");
+  TORCH_CHECK(src.is_contiguous() && dst.is_contiguous(), "src and dst must be contiguous");
+  const int64_t need = count > 0 ? (count - 1) * stride_bytes + bytes : 0;
+  TORCH_CHECK(src.numel() * src.element_size() >= need &&
+                  dst.numel() * dst.element_size() >= need,
+              "src and dst must hold (count - 1) * stride_bytes + bytes = ", need, " bytes");
+  c10::cuda::CUDAGuard guard(src.device());
+  raise_on_error(drk_launch_copy_probe(src.data_ptr(), dst.data_ptr(), bytes, stride_bytes,
+                                       static_cast<int>(count), static_cast<int>(threads),
+                                       pdl ? 1 : 0, prefetch ? 1 : 0, stream_for(src)));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -482,6 +498,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_address", &status_address, py::arg("device"));
   m.def("status_string", &status_string, py::arg("status"));
   m.def("launch_empty", &launch_empty, py::arg("count"), py::arg("pdl") = false);
+  m.def("launch_copy_probe", &launch_copy_probe, py::arg("src"), py::arg("dst"),
+        py::arg("bytes"), py::arg("stride_bytes"), py::arg("count"), py::arg("threads"),
+        py::arg("pdl") = true, py::arg("prefetch") = true,
+        "Chained dependent copies with one decode layer's memory pattern (launch floor).");
   m.def("advance_positions", &advance_positions, py::arg("positions"), py::arg("delta") = 1,
         py::arg("pdl") = false, "positions += delta on the device (a decode loop's step).");
 }

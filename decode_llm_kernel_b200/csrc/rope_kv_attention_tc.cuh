@@ -56,9 +56,9 @@
 // reads it, so no unit depends on another's global write (the tile may have been fetched before
 // the slot was written).
 //
-// Waits are bounded (kWaitLimit polls); a wait that runs out -- no valid input causes one --
-// sets DRK_STATUS_TIMEOUT and ends the CTA's walk; the producer waits (bounded) for the copies it
-// issued, and the CTA frees its TMEM and returns. No thread-block clusters and no cross-CTA
+// Waits are bounded (one second of %globaltimer); a wait that runs out -- no valid input
+// causes one -- sets DRK_STATUS_TIMEOUT and ends the CTA's walk; the producer waits (bounded)
+// for the copies it issued, and the CTA frees its TMEM and returns. No thread-block clusters and no cross-CTA
 // waits.
 #pragma once
 

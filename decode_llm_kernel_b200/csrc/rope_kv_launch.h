@@ -123,5 +123,11 @@ cudaError_t launch_smoke_fill(void* data, int elem_code, int64_t numel, double v
                               cudaStream_t stream);
 cudaError_t run_arch_probe(int* arch_out, cudaStream_t stream);
 cudaError_t launch_empty(int count, bool pdl, cudaStream_t stream);
+// `count` chained copies of `vectors` 16-byte vectors (an even number), launch i from
+// src + i * stride_vectors to dst + i * stride_vectors, `threads` per CTA, two vectors a
+// thread (see copy_probe_kernel).
+cudaError_t launch_copy_probe(const void* src, void* dst, int64_t vectors, int64_t stride_vectors,
+                              int count, int threads, bool pdl, bool prefetch,
+                              cudaStream_t stream);
 
 }  // namespace drk

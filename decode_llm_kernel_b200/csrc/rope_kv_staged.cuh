@@ -6,7 +6,9 @@
 // contiguous, and a cache slot [Hkv, D] is contiguous (token-major or paged caches).
 //
 // Per CTA, a persistent loop over tokens t = blockIdx.x, blockIdx.x + gridDim.x, ... with a
-// kStages-deep pipeline in shared memory:
+// kStages-deep pipeline in shared memory. Before griddepcontrol.wait (programmatic dependent
+// launch) a CTA resolves its first token's indices, slot and table slice and pulls its first
+// tokens' row blocks toward L2 (cp.async.bulk.prefetch.L2); after it:
 //   1. one thread issues cp.async.bulk global->shared copies of the token's Q, K and V row
 //      blocks, completing on the stage's mbarrier (expect_tx bytes);
 //   2. every thread waits on the stage's mbarrier (bounded: see below); the position, request
@@ -23,9 +25,10 @@
 // No thread-block clusters: every copy moves data between global memory and this CTA's own
 // shared memory.
 //
-// Waits. Each mbarrier wait is bounded (kWaitLimit polls). If a wait runs out -- a copy that
-// never lands, which no valid input produces -- the CTA sets DRK_STATUS_TIMEOUT in the status
-// word, stops issuing work, waits (bounded) for its own copies in flight and returns.
+// Waits. Each mbarrier wait is bounded (one second of %globaltimer). If a wait runs out -- a
+// copy that never lands, which no valid input produces -- the CTA sets DRK_STATUS_TIMEOUT in
+// the status word, stops issuing work, waits (bounded) for its own copies in flight and
+// returns.
 #pragma once
 
 #include "rope_kv_kernels.cuh"
@@ -34,7 +37,17 @@ namespace drk {
 
 constexpr int kStagedThreads = kStagedThreadsPerBlock;
 constexpr uint32_t kStatusTimeout = 1u << 4;
-constexpr long long kWaitLimit = 1ll << 26;
+// A bounded wait gives up after this many nanoseconds of %globaltimer: a second, against the
+// microseconds any copy this library issues takes.
+#ifndef DRK_WAIT_LIMIT_NS
+#define DRK_WAIT_LIMIT_NS 1000000000ull
+#endif
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -51,10 +64,13 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
-// True once the barrier's phase with this parity has completed; false after kWaitLimit polls.
+// True once the barrier's phase with this parity has completed; false once DRK_WAIT_LIMIT_NS
+// have passed on %globaltimer since the wait started (read every 16 polls: try_wait itself
+// suspends the thread for a while between polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
-  for (long long i = 0; i < kWaitLimit; ++i) {
+  uint64_t deadline = 0;
+  for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -64,8 +80,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 15u) == 15u) {
+      const uint64_t now = global_ns();
+      if (deadline == 0) {
+        deadline = now + DRK_WAIT_LIMIT_NS;
+      } else if (now >= deadline) {
+        return false;
+      }
+    }
   }
-  return false;
 }
 
 // L2 eviction priority of the bulk copies: 0 none; bit 0: loads (q/k/v are read once) marked
@@ -109,6 +132,14 @@ __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src,
                "r"(smem_u32(smem_src)), "r"(bytes)
                : "memory");
 #endif
+}
+
+// Pulls `bytes` (a multiple of 16, 16-byte aligned) toward L2 without a destination: issued
+// before griddepcontrol.wait, so the copies after it hit L2. L2 is the point of coherence, so a
+// line the preceding kernel writes after the prefetch is still read fresh.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void bulk_commit() {
@@ -164,9 +195,15 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     for (int st = 0; st < sp.stages; ++st) mbar_init(&bars[st], 1);
     fence_mbar_init();
     s_abort = 0;
+    // The first tokens' Q/K/V row blocks toward L2 while the preceding kernel may still run
+    // (launched as a programmatic dependent; otherwise this is simply the first request).
+    for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) {
+      const int64_t t = blockIdx.x + j * gridDim.x;
+      bulk_prefetch_l2(p.q + t * p.q_ts * ES, sp.q_bytes);
+      bulk_prefetch_l2(p.k + t * p.k_ts * ES, sp.kv_bytes);
+      bulk_prefetch_l2(p.v + t * p.v_ts * ES, sp.kv_bytes);
+    }
   }
-  __syncthreads();
-  pdl_wait();   // q/k/v may be written by the preceding kernel
 
   int64_t issued = 0;   // tokens whose copies thread 0 has issued
   auto issue_load = [&](int64_t j) {
@@ -179,10 +216,6 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     bulk_load(stage + sp.q_bytes, p.k + t * p.k_ts * ES, sp.kv_bytes, &bars[st]);
     bulk_load(stage + sp.q_bytes + sp.kv_bytes, p.v + t * p.v_ts * ES, sp.kv_bytes, &bars[st]);
   };
-
-  if (tid == 0) {
-    for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) issue_load(j);
-  }
 
   const bool lane_rotates = lane < p.nrot;
   const int off1 = lane * VEC * static_cast<int>(ES);
@@ -256,6 +289,8 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     return m;
   };
 
+  // Indices, bounds, slot and table slice of the first tokens: they are never written by the
+  // preceding kernel, so they are resolved before waiting on it.
   float c_cur[VEC], s_cur[VEC];
   int64_t pos_next = 0, ri_next = 0;
   Meta cur{0, 0u, false, false};
@@ -264,6 +299,11 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     fetch_index(0, pos0, ri0);
     if (my_tokens > 1) fetch_index(1, pos_next, ri_next);
     cur = resolve(pos0, ri0, c_cur, s_cur);
+  }
+  __syncthreads();   // the barriers are initialised
+  pdl_wait();        // q/k/v may be written by the preceding kernel
+  if (tid == 0) {
+    for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) issue_load(j);
   }
 
   int64_t j = 0;

@@ -312,6 +312,19 @@ DRK_API int drk_build_info(char* buf, size_t len, drk_stream_t stream);
  * with programmatic dependent launch when pdl != 0. */
 DRK_API int drk_launch_empty(int count, int pdl, drk_stream_t stream);
 
+/* Dependent-copy floor probe: `count` launches chained like the layers of a decode step; launch
+ * i copies `bytes` (a multiple of 32) from src + i * stride_bytes to dst + i * stride_bytes,
+ * two 16-byte vectors per thread, threads_per_cta threads per CTA, with programmatic dependent
+ * launch when pdl != 0. Each launch loads only after griddepcontrol.wait; with prefetch != 0
+ * its threads first pull their source lines toward L2 while they wait. It is one layer of the
+ * fused op without its arithmetic and index work, so a layer's time against it shows what the
+ * op adds to the cost of a chained dependent read and write. The caller guarantees src and dst
+ * hold (count - 1) * stride_bytes + bytes bytes. No counterpart in the reference, whose floor
+ * probe (benchmarks/probe_graph_floor.py:36-112) launches empty kernels only. */
+DRK_API int drk_launch_copy_probe(const void* src, void* dst, int64_t bytes, int64_t stride_bytes,
+                                  int count, int threads_per_cta, int pdl, int prefetch,
+                                  drk_stream_t stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 DRK_API const char* drk_last_error(void);
 
