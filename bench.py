@@ -77,9 +77,12 @@ def parse_args():
                    help="skip the reference's own kernels (baseline/_ref) on the GPU")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=1234)
-    p.add_argument("--mode", choices=["full", "bw", "attention"], default="full",
+    p.add_argument("--mode", choices=["full", "bw", "single", "attention"], default="full",
                    help="bw: only the bandwidth-bound launch loop (for profiling small cases); "
+                        "single: only the single-layer loop of --probe; "
                         "attention: only the fused append + decode attention measurement")
+    p.add_argument("--probe", default="mistral_b4096", choices=sorted(WORKLOADS),
+                   help="single mode: the workload of the single-layer loop")
     p.add_argument("--cache-len", type=int, default=0,
                    help="override cache_alloc_len (profiling runs only: keeps a case small)")
     p.add_argument("--launches", type=int, default=400, help="bw mode: timed launches")
@@ -1224,12 +1227,13 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
-        elif args.mode == "bw":
+        elif args.mode in ("bw", "single"):
             local_dev = torch.device("cuda", local)
             torch.cuda.set_device(local_dev)
             peak, _ = measured_hbm_peak()
-            out = bandwidth_probe(world, rank, local_dev, args.seed, peak, args.cache_len,
-                                  args.launches)
+            name = "mistral_b4096" if args.mode == "bw" else args.probe
+            out = single_layer_probe(name, world, rank, local_dev, args.seed, peak,
+                                     args.cache_len, args.launches)
             if rank == 0:
                 print(json.dumps(out), flush=True)
         elif args.mode == "attention":

@@ -257,7 +257,8 @@ struct Shape {
 #endif
 constexpr int kRowsPerSplitCta = 20;
 
-Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens, int32_t splits_hint) {
+Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens, int32_t splits_hint,
+           int32_t rows_hint = 0) {
   Shape s{};
   s.vb = al.pick();
   if (s.vb == 0) throw Unsupported("tensors are not aligned to their element size");
@@ -269,7 +270,10 @@ Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens, int32_t s
                           drk::kMaxThreadsPerBlock, " are supported"));
   s.nslots = static_cast<int>(nslots);
   s.nrot = rotates ? static_cast<int>(al.R / (2 * vec)) : 0;
-  s.rows = tokens <= DRK_SMALL_BATCH_TOKENS ? 1 : drk::kRowsPerThread;
+  if (rows_hint != 0 && rows_hint != 1 && rows_hint != drk::kRowsPerThread)
+    invalid("rows_per_thread must be 0 (chosen by the library), 1 or ", drk::kRowsPerThread,
+            ", got ", rows_hint);
+  s.rows = rows_hint ? rows_hint : (tokens <= DRK_SMALL_BATCH_TOKENS ? 1 : drk::kRowsPerThread);
   const int max_threads = s.rows == 1 ? 1024 : drk::kMaxThreadsPerBlock;
   // `rows` rows per thread; a block holds whole row groups.
   const int want_groups = std::max(1, (nrows + s.rows - 1) / s.rows);
@@ -454,7 +458,7 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
                 const drk_tensor* k_cache, const drk_tensor* v_cache,
                 const drk_tensor* block_table, const drk_tensor* request_indices,
                 const drk_tensor* q_out, const drk_options* opts, uint32_t* status,
-                drk_stream_t stream) {
+                drk_stream_t stream, int64_t test_skip_token = -1, int64_t wait_limit_ns = 0) {
   const drk_options o = options_or_default(opts);
   const bool paged = block_table != nullptr;
   require(q, "q");
@@ -529,6 +533,9 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   p.R = static_cast<int32_t>(R);
   fill_table(p, cos, sin, o, R);
 
+  p.test_skip_token = test_skip_token;
+  p.wait_limit_ns = wait_limit_ns;
+
   const int index_bits = positions->dtype == DRK_I32 ? 32 : 64;
   const bool pdl = (o.flags & DRK_FLAG_PDL) != 0;
   const bool force_staged = (o.flags & DRK_FLAG_FORCE_STAGED_PATH) != 0;
@@ -558,12 +565,13 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   al.stride(T, v->strides[0]); al.stride(Hkv, v->strides[1]);
   for (int i = 0; i < 3; ++i) al.stride(k_cache->sizes[i], k_cache->strides[i]);
   const int nrows = static_cast<int>(Hq + 2 * Hkv);
-  const Shape s = plan(al, nrows, true, T, o.row_splits);
+  const Shape s = plan(al, nrows, true, T, o.row_splits, o.rows_per_thread);
   p.nslots = s.nslots; p.nrot = s.nrot; p.G = s.G; p.rows_per_thread = s.rows;
   p.pdl = pdl ? 1 : 0;
 
   DeviceGuard guard(device);
-  const drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, pdl};
+  drk::LaunchShape shape{grid_for(T), s.splits, s.nslots, s.G, pdl};
+  shape.allow_lean = s.rows == 1;
   check_launch(drk::launch_rope_kv(p, elem_code(q->dtype), index_bits, s.vb, drk::kModeFused,
                                    paged ? drk::kCachePaged : drk::kCacheStrided, shape,
                                    reinterpret_cast<cudaStream_t>(stream)));
@@ -1140,6 +1148,26 @@ int drk_launch_empty(int count, int pdl, drk_stream_t stream) {
   return guarded([&] {
     if (count < 0) invalid("count must be >= 0");
     check_launch(drk::launch_empty(count, pdl != 0, reinterpret_cast<cudaStream_t>(stream)));
+  });
+}
+
+// Testing the bounded-wait timeout path of the bulk-copy kernel, without a GPU fault: the
+// fused op forced onto that kernel, with the loads of token `skip_token` not issued and every
+// wait limited to `wait_limit_ns`. The CTA that owns the token waits for copies that were never
+// issued; when the limit passes it sets DRK_STATUS_TIMEOUT, waits for its other copies in
+// flight and returns, and the other CTAs finish normally. Not declared in the public header.
+DRK_API int drk_testing_staged_timeout(
+    const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,
+    const drk_tensor* cos, const drk_tensor* sin, const drk_tensor* k_cache,
+    const drk_tensor* v_cache, const drk_tensor* request_indices, const drk_tensor* q_out,
+    int64_t skip_token, int64_t wait_limit_ns, uint32_t* status, drk_stream_t stream) {
+  return guarded([&] {
+    if (wait_limit_ns <= 0 || wait_limit_ns > 2000000000ll)
+      invalid("wait_limit_ns must be in (0, 2e9], got ", wait_limit_ns);
+    drk_options o{};
+    o.flags = DRK_FLAG_FORCE_STAGED_PATH;
+    fused_impl(q, k, v, positions, cos, sin, k_cache, v_cache, nullptr, request_indices, q_out,
+               &o, status, stream, skip_token, wait_limit_ns);
   });
 }
 

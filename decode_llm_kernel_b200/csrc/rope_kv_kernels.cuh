@@ -52,8 +52,8 @@ enum class Mode : int { kFused = 0, kRope = 1, kAppend = 2 };
 enum class Cache : int { kStrided = 0, kPaged = 1 };
 
 constexpr int kMinBlocksPerSM = DRK_MIN_BLOCKS_PER_SM;
-#ifndef DRK_ONE_ROW_MAX_REGS
-#define DRK_ONE_ROW_MAX_REGS 56
+#ifndef DRK_ONE_ROW_LEAN_REGS
+#define DRK_ONE_ROW_LEAN_REGS 56
 #endif
 
 enum : uint32_t {
@@ -217,22 +217,22 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
 }
 
 // Threads per block the kernel is compiled for: NR == 1 (one head row per thread, the small-batch
-// shape) runs up to 1024 threads, otherwise kMaxThreadsPerBlock.
-template <int NR>
+// shape) runs up to 1024 threads, otherwise kMaxThreadsPerBlock. Registers per thread: one row
+// per thread takes 64, or 56 in the Lean form (an 8-byte spill), which lets an SM hold 36 warps
+// instead of 32. The host takes the Lean form only when that turns a launch of more than one
+// wave into one (a 70B-shaped call: 256 tokens x 80 rows x 8 lanes = 164k threads fits 148 SMs
+// at 36 warps, not at 32); for launches that fit either way the spill costs latency.
+template <int NR, bool Lean>
 struct RegisterKernelBounds {
   static constexpr int kThreads = NR == 1 ? 1024 : kMaxThreadsPerBlock;
   static constexpr int kMinBlocks = NR == 1 ? 1 : kMinBlocksPerSM;
-  // Registers per thread. One row per thread is the latency-bound shape, where what counts is
-  // how many rows are in flight at once: 56 registers (an 8-byte spill; 64 without the cap)
-  // let an SM hold 36 warps instead of 32, which puts a 70B-shaped call (256 tokens x 80 rows
-  // x 8 lanes = 164k threads) in one wave of the 148 SMs instead of 1.1.
-  static constexpr int kMaxRegs = NR == 1 ? DRK_ONE_ROW_MAX_REGS : 255;
+  static constexpr int kMaxRegs = NR == 1 ? (Lean ? DRK_ONE_ROW_LEAN_REGS : 64) : 128;
 };
 
-template <typename E, typename Idx, int VB, Mode M, Cache C, int NR>
-__global__ void __launch_bounds__(RegisterKernelBounds<NR>::kThreads,
-                                  RegisterKernelBounds<NR>::kMinBlocks)
-__maxnreg__(RegisterKernelBounds<NR>::kMaxRegs)
+template <typename E, typename Idx, int VB, Mode M, Cache C, int NR, bool Lean = false>
+__global__ void __launch_bounds__(RegisterKernelBounds<NR, Lean>::kThreads,
+                                  RegisterKernelBounds<NR, Lean>::kMinBlocks)
+__maxnreg__((RegisterKernelBounds<NR, Lean>::kMaxRegs))
 rope_kv_kernel(const __grid_constant__ KernelParams p) {
   using raw = typename E::raw;
   constexpr int VEC = VB / static_cast<int>(sizeof(raw));

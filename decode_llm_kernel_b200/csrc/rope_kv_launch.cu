@@ -15,11 +15,47 @@
 namespace drk {
 namespace {
 
-template <typename E, typename Idx, int VB, Mode M, Cache C, int NR>
+int sm_count(int device);
+
+// CTAs of `kernel` with `threads` threads one SM holds (cached per kernel, block size, device).
+template <typename K>
+int resident_ctas(K kernel, int threads) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, std::pair<int, int>>, int> cache;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel),
+                                  std::make_pair(device, threads));
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess) n = 0;
+  cache[key] = n;
+  return n;
+}
+
+template <typename E, typename Idx, int VB, Mode M, Cache C, int NR, bool Lean = false>
 cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStream_t stream) {
+  if constexpr (NR == 1 && !Lean && M == Mode::kFused && C == Cache::kStrided) {
+    // Waves of the 64-register form against the 56-register (Lean) form: take Lean when it
+    // fits the grid in fewer waves (both resident counts come from the occupancy calculator).
+    const int64_t ctas = static_cast<int64_t>(shape.grid) * shape.splits;
+    int device = 0;
+    if (shape.allow_lean && cudaGetDevice(&device) == cudaSuccess) {
+      const int64_t sms = sm_count(device);
+      const int threads = shape.lanes * shape.groups;
+      if (ctas > sms) {
+        const int64_t full = sms * resident_ctas(rope_kv_kernel<E, Idx, VB, M, C, 1, false>, threads);
+        const int64_t lean = sms * resident_ctas(rope_kv_kernel<E, Idx, VB, M, C, 1, true>, threads);
+        if (full > 0 && lean > 0 && (ctas + lean - 1) / lean < (ctas + full - 1) / full)
+          return launch_one<E, Idx, VB, M, C, 1, true>(p, shape, stream);
+      }
+    }
+  }
   if (!shape.pdl) {
     // The plain launch path: no attributes to process on the host.
-    rope_kv_kernel<E, Idx, VB, M, C, NR>
+    rope_kv_kernel<E, Idx, VB, M, C, NR, Lean>
         <<<dim3(shape.grid, shape.splits, 1), dim3(shape.lanes, shape.groups, 1), 0, stream>>>(p);
     return cudaGetLastError();
   }
@@ -35,7 +71,7 @@ cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStre
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, rope_kv_kernel<E, Idx, VB, M, C, NR>, p);
+  return cudaLaunchKernelEx(&cfg, rope_kv_kernel<E, Idx, VB, M, C, NR, Lean>, p);
 }
 
 template <typename E, typename Idx, int VB, int NR>

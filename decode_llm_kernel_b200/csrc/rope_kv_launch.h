@@ -46,6 +46,11 @@ struct KernelParams {
   int32_t table_vec4;         // table base and row stride allow 16-byte loads
   int32_t pdl;                // launched with programmatic dependent launch
   int32_t rows_per_thread;    // register kernel: 1 (small batches) or kRowsPerThread
+  // Bulk-copy kernel, for testing its timeout path only (drk_testing_staged_timeout): the
+  // token whose Q/K/V loads are not issued (-1: none) and the wait limit in ns (0: the
+  // compiled default).
+  int64_t test_skip_token = -1;
+  int64_t wait_limit_ns = 0;
 };
 
 enum { kElemF32 = 0, kElemF16 = 1, kElemBF16 = 2, kElemF64 = 3 };
@@ -58,6 +63,9 @@ struct LaunchShape {
   int lanes;     // blockDim.x: lanes per head row (nslots)
   int groups;    // blockDim.y: row groups (G)
   bool pdl;
+  bool allow_lean = false;  // register kernel, one row per thread, fused into a strided cache:
+                            // the launcher may take the 56-register form when that puts the
+                            // grid in one wave where the 64-register form needs more
 };
 
 cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits, int vb,

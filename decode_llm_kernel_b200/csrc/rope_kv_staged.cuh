@@ -64,10 +64,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
-// True once the barrier's phase with this parity has completed; false once DRK_WAIT_LIMIT_NS
-// have passed on %globaltimer since the wait started (read every 16 polls: try_wait itself
-// suspends the thread for a while between polls).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// True once the barrier's phase with this parity has completed; false once limit_ns
+// (DRK_WAIT_LIMIT_NS unless given) have passed on %globaltimer since the wait started (read
+// every 16 polls: try_wait itself suspends the thread for a while between polls).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = DRK_WAIT_LIMIT_NS) {
   const uint32_t addr = smem_u32(bar);
   uint64_t deadline = 0;
   for (uint32_t i = 0;; ++i) {
@@ -83,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if ((i & 15u) == 15u) {
       const uint64_t now = global_ns();
       if (deadline == 0) {
-        deadline = now + DRK_WAIT_LIMIT_NS;
+        deadline = now + limit_ns;
       } else if (now >= deadline) {
         return false;
       }
@@ -205,10 +206,17 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     }
   }
 
+  const uint64_t wait_ns = p.wait_limit_ns > 0 ? static_cast<uint64_t>(p.wait_limit_ns)
+                                               : DRK_WAIT_LIMIT_NS;
   int64_t issued = 0;   // tokens whose copies thread 0 has issued
+  int64_t skipped = -1; // testing only: the token whose copies were not issued
   auto issue_load = [&](int64_t j) {
     issued = j + 1;
     const int64_t t = blockIdx.x + j * gridDim.x;
+    if (t == p.test_skip_token) {
+      skipped = j;        // nothing in flight for it: its stage's wait runs out
+      return;
+    }
     const int st = static_cast<int>(j % sp.stages);
     unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
     mbar_expect_tx(&bars[st], sp.q_bytes + 2 * sp.kv_bytes);
@@ -320,7 +328,7 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     Meta nxt{0, 0u, false, false};
     if (j + 1 < my_tokens) nxt = resolve(pos_next, ri_next, c_nxt, s_nxt);
 
-    if (!mbar_wait(&bars[st], parity)) {
+    if (!mbar_wait(&bars[st], parity, wait_ns)) {
       atomicOr(&s_abort, 1);
     }
     __syncthreads();
@@ -373,7 +381,8 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
       if (p.status != nullptr) atomicOr(p.status, kStatusTimeout);
       // Let copies still landing in this CTA's stages finish before the CTA exits.
       for (int64_t k = j; k < issued; ++k) {
-        mbar_wait(&bars[k % sp.stages], static_cast<uint32_t>((k / sp.stages) & 1));
+        if (k == skipped) continue;
+        mbar_wait(&bars[k % sp.stages], static_cast<uint32_t>((k / sp.stages) & 1), wait_ns);
       }
     }
   }

@@ -108,7 +108,8 @@ typedef struct drk_options {
   const float* inv_freq;  /* [rotary_dim/2] fp32 device array, only for DRK_FLAG_INREG_TRIG */
   int32_t row_splits;     /* register kernel: CTAs sharing one token's head rows (0 = chosen
                              by the library from the token count and the SM count) */
-  int32_t reserved0;
+  int32_t rows_per_thread; /* register kernel: head rows a thread holds, 1 or 3 (0 = chosen by
+                              the library: 1 up to 256 tokens, 3 above) */
   int64_t k_position_limit; /* drk_kv_append only: when > 0, the K row of a token whose
                                position is >= this is not written (its V row still is). A
                                separate RoPE-then-append passes the cos/sin table's row count,
