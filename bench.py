@@ -330,12 +330,15 @@ def check_call(q, k, v, pos, ri, cos, sin, q_out, k_cache, v_cache, rotary):
 
 
 def parity_label(counts):
+    """'bit-exact'; or, when only rotated elements differ, how many and by how many ulps of the
+    storage type at most; 'MISMATCH' when a V slot (a byte copy) differs."""
     bad = counts["q"] + counts["k_slots"] + counts["v_slots"]
     if bad == 0:
         return "bit-exact"
-    if counts["v_slots"] == 0 and counts["max_ulp"] <= 1:
-        return (f"within 1 ulp: {counts['q'] + counts['k_slots']} of {counts['elements']} "
-                "rotated elements differ by 1 ulp, V bit-exact")
+    if counts["v_slots"] == 0:
+        ulp = counts["max_ulp"]
+        return (f"within {ulp} ulp: {counts['q'] + counts['k_slots']} of {counts['elements']} "
+                f"rotated elements differ (by at most {ulp} ulp), V bit-exact")
     return f"MISMATCH {counts}"
 
 

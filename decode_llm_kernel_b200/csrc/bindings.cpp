@@ -173,6 +173,25 @@ void kv_append(at::Tensor k_rot, at::Tensor v, at::Tensor positions, at::Tensor 
                                stream_for(k_rot)));
 }
 
+// rope_forward then the append, in one call from Python: k_rot is materialised (the separate
+// op's defining intermediate) and the append is told the cos/sin row count, so a token past the
+// table keeps its K slot as in the fused op.
+at::Tensor separate_rope_kv_append(at::Tensor q, at::Tensor k, at::Tensor v,
+                                   at::Tensor positions, at::Tensor cos, at::Tensor sin,
+                                   at::Tensor k_cache, at::Tensor v_cache,
+                                   at::Tensor request_indices) {
+  auto rotated = rope_forward(q, k, positions, cos, sin);
+  const at::Tensor& k_rot = std::get<1>(rotated);
+  drk_options o{};
+  o.k_position_limit = cos.dim() == 2 ? cos.size(0) : 0;
+  const drk_tensor dk = describe(k_rot), dv = describe(v), dp = describe(positions),
+                   dri = describe(request_indices), dkc = describe(k_cache),
+                   dvc = describe(v_cache);
+  raise_on_error(drk_kv_append(&dk, &dv, &dp, &dri, &dkc, &dvc, &o, status_for(k_rot),
+                               stream_for(k_rot)));
+  return std::get<0>(rotated);
+}
+
 void smoke_fill(at::Tensor tensor, double value) {
   const drk_tensor d = describe(tensor);
   raise_on_error(drk_smoke_fill(&d, value, stream_for(tensor)));
@@ -453,6 +472,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_append", &kv_append, py::arg("k_rot"), py::arg("v"), py::arg("positions"),
         py::arg("request_indices"), py::arg("k_cache"), py::arg("v_cache"),
         "Scatter rotated K and raw V into a contiguous token-major cache, in place.");
+  m.def("separate_rope_kv_append", &separate_rope_kv_append, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("request_indices"),
+        "rope_forward then kv_append (k_rot materialised); returns q_rot.");
   m.def("fused_rope_kv_append", &fused_rope_kv_append, py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("request_indices"),

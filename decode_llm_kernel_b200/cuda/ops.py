@@ -22,14 +22,12 @@ def kv_append(k_rot, v, positions, request_indices, k_cache, v_cache):
 def separate_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices):
     """RoPE kernel then append kernel, with `k_rot` materialised between them: two launches and
     one intermediate, the ablation the fused op is measured against."""
-    q_rot, k_rot = rope_forward(q, k, positions, cos, sin)
-    # A token past the cos/sin table gets no k_rot row from rope_forward (a status bit
-    # instead), so the append is told the table length and leaves that K slot untouched, as the
-    # fused op does; its V slot is still written.
-    limit = cos.shape[0] if cos.dim() == 2 and cos.shape[0] > 0 else 0
-    require().kv_append_ex(k_rot, v, positions, request_indices, k_cache, v_cache, False, False,
-                           limit)
-    return q_rot
+    # One binding call: rope_forward into a fresh k_rot, then the append. A token past the
+    # cos/sin table gets no k_rot row from the rope step (a status bit instead), so the append
+    # is told the table length and leaves that K slot untouched, as the fused op does; its V
+    # slot is still written.
+    return require().separate_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache,
+                                             request_indices)
 
 
 def fused_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices):

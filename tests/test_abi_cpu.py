@@ -147,3 +147,36 @@ def test_torch_binding_raises_runtime_errors_on_cpu_tensors():
         ops.fused_rope_kv_append(torch.zeros(2, 2), *a[1:])
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         cuda.smoke_fill(torch.zeros(4), 1.0)
+
+
+def test_copy_probe_checks_its_arguments_before_any_launch(lib):
+    fn = lib.drk_launch_copy_probe
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                   ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    lib.drk_last_error.restype = ctypes.c_char_p
+    for call, msg in (((16, 32, 32, 1, 128, 1, 1), "multiple of 32"),
+                      ((64, 32, 32, 1, 128, 1, 1), "stride_bytes must be >= bytes"),
+                      ((64, 64, 32, 1, 100, 1, 1), "threads_per_cta"),
+                      ((64, 64, -1, 1, 128, 1, 1), "count must be >= 0")):
+        bytes_, stride, count, _, threads, pdl, prefetch = call
+        rc = fn(None, None, bytes_, stride, count, threads, pdl, prefetch, None)
+        assert rc == -1 and msg in lib.drk_last_error().decode(), call
+    assert fn(None, None, 64, 64, 1, 128, 1, 1, None) == -1
+    assert "16-byte aligned" in lib.drk_last_error().decode()
+
+
+def test_noalloc_rejects_a_malformed_call_with_the_regular_message_first(lib):
+    """Argument checks run before the size check: a CPU positions tensor is named even when
+    the intermediate would not fit the 8 MiB array."""
+    a = args(T=4200, Hq=1, Hkv=8, D=128)
+    fn = lib.drk_separate_rope_kv_append_noalloc
+    fn.restype = ctypes.c_int
+    lib.drk_last_error.restype = ctypes.c_char_p
+    ds = [desc(t, -1 if i == 3 else 0) for i, t in enumerate(a)]
+    rc = fn(*[ctypes.byref(d) for d in ds], None, None)
+    assert rc == -1 and "positions must be a CUDA tensor" in lib.drk_last_error().decode()
+    # a well-formed but over-size call names the limit
+    ds = [desc(t, 0) for t in a]
+    rc = fn(*[ctypes.byref(d) for d in ds], None, None)
+    assert rc == -1 and "8 MiB" in lib.drk_last_error().decode()

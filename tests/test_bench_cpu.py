@@ -92,5 +92,6 @@ def test_ulp_distance_of_the_parity_report():
     assert bench.max_ulp(one, up) == 0                    # 1 + fp32 ulp rounds back to 1
     counts = {"q": 3, "k_slots": 1, "v_slots": 0, "max_ulp": 1, "elements": 100}
     assert bench.parity_label(counts).startswith("within 1 ulp")
-    assert bench.parity_label(dict(counts, max_ulp=2)).startswith("MISMATCH")
+    assert bench.parity_label(dict(counts, max_ulp=3)).startswith("within 3 ulp")
+    assert bench.parity_label(dict(counts, v_slots=1)).startswith("MISMATCH")
     assert bench.parity_label(dict(counts, q=0, k_slots=0, max_ulp=0)) == "bit-exact"
