@@ -844,10 +844,15 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
         attended = sum(int(x["p"].sum().item()) + T for x in st) / sets
         bytes_call = (2 * Hkv * D * 2 * attended + 2 * T * Hq * D * 2 + 4 * T * Hkv * D * 2)
 
+        nbytes = ops.attention_workspace_bytes(T, Hq, Hkv, D, S, dt, device=device.index or 0)
+        for x in st:
+            x["ws"] = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
         def fused(x):
+            # a persistent workspace, zeroed once: every call leaves its counters at zero
             return lambda: ops.fused_rope_kv_append_attention(
                 x["q"], x["k"], x["v"], x["p"], cos, sin, x["kc"], x["vc"], x["ri"],
-                attn_out=x["out"])
+                attn_out=x["out"], workspace=x["ws"], workspace_zeroed=True)
 
         def append(x):
             return lambda: ops.fused_rope_kv_append_ex(x["q"], x["k"], x["v"], x["p"], cos, sin,
@@ -857,7 +862,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
                "positions": "all at S-1" if full else "U[0, S)",
                "bytes_per_call": bytes_call, "fused_us": us,
                "fused_gbs": bytes_call / us / 1e3, "frac_of_hbm_peak": bytes_call / us / 1e3 / peak,
-               "kernel": "drk::rope_kv_attention_tc_kernel (tcgen05 + TMA, warp-specialized)"}
+               "kernel": "drk::rope_kv_attention_tc_kernel (tcgen05 + TMA, warp-specialized)",
+               "workspace": "persistent per input set, zeroed once (workspace_zeroed=True)"}
         try:
             if full:
                 import torch.nn.functional as F
@@ -913,10 +919,15 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
         attended = sum(int(x["p"].sum().item()) + T for x in st) / sets
         bytes_call = (2 * Hkv * D * 2 * attended + 2 * T * Hq * D * 2 + 4 * T * Hkv * D * 2)
 
+        nbytes = ops.attention_workspace_bytes(T, Hq, Hkv, D, nblk * bs, dt,
+                                               device=device.index or 0, path="tensor_cores")
+        for x in st:
+            x["ws"] = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
         def fused_paged(x):
             return lambda: ops.paged_rope_kv_append_attention(
                 x["q"], x["k"], x["v"], x["p"], cos, sin, x["kp"], x["vp"], x["table"], x["ri"],
-                attn_out=x["out"])
+                attn_out=x["out"], workspace=x["ws"], workspace_zeroed=True)
         us = graph_us([fused_paged(x) for x in st])
         res = {"T": T, "block_size": bs, "positions": "U[0, S)", "bytes_per_call": bytes_call,
                "fused_us": us, "fused_gbs": bytes_call / us / 1e3,

@@ -649,8 +649,9 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
     }
     pl.chunk = (chunk + 127) / 128 * 128;
     pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);
-    // Arrival counters of the units, then the persistent grid's unit counter.
-    pl.counter_bytes = ((T * Hkv * pl.nhb + 1) * 4 + 255) / 256 * 256;
+    // Arrival counters of the units, then the persistent grid's unit counter and its count
+    // of CTAs that have finished (the last one resets both).
+    pl.counter_bytes = ((T * Hkv * pl.nhb + 2) * 4 + 255) / 256 * 256;
     pl.partial_bytes = T * Hq * pl.max_chunks * (D + 2) * 4;
     return pl;
   }
@@ -818,7 +819,10 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
 
   DeviceGuard guard(device);
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(workspace, 0, static_cast<size_t>(pl.counter_bytes), s) != cudaSuccess)
+  // Every call returns the counters to zero (unless a bounded wait ran out), so a caller that
+  // keeps its workspace and says it is zeroed saves this memset node.
+  if (!(ao.flags & DRK_ATTN_WORKSPACE_ZEROED) &&
+      cudaMemsetAsync(workspace, 0, static_cast<size_t>(pl.counter_bytes), s) != cudaSuccess)
     throw CudaFailure("cudaMemsetAsync of the attention counters failed");
   const int index_bits_tc = positions->dtype == DRK_I32 ? 32 : 64;
   if (pl.tc) {

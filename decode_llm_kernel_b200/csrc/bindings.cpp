@@ -308,7 +308,7 @@ at::Tensor fused_rope_kv_append_attention(
     at::Tensor sin, at::Tensor k_cache, at::Tensor v_cache, at::Tensor request_indices,
     double scale, c10::optional<at::Tensor> q_out_opt, c10::optional<at::Tensor> attn_out_opt,
     int64_t chunk, int64_t heads_per_cta, int64_t rotary_dim, bool pdl, bool strided_cache,
-    c10::optional<at::Tensor> workspace_opt, const std::string& path) {
+    c10::optional<at::Tensor> workspace_opt, const std::string& path, bool workspace_zeroed) {
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && k_cache.dim() == 4,
               "q must be [num_tokens, num_q_heads, head_dim], k [num_tokens, num_kv_heads, "
               "head_dim] and k_cache [batch, cache_alloc_len, num_kv_heads, head_dim]");
@@ -320,6 +320,9 @@ at::Tensor fused_rope_kv_append_attention(
   ao.chunk = static_cast<int32_t>(chunk);
   ao.heads_per_cta = static_cast<int32_t>(heads_per_cta);
   ao.path = attention_path(path);
+  const bool given = workspace_opt.has_value() && workspace_opt->defined();
+  TORCH_CHECK(!workspace_zeroed || given, "workspace_zeroed=True needs a workspace");
+  ao.flags = workspace_zeroed ? DRK_ATTN_WORKSPACE_ZEROED : 0;
   const int32_t device = q.is_cuda() ? q.get_device() : -1;
   const int64_t need = drk_attention_workspace_bytes(
       q.size(0), static_cast<int32_t>(q.size(1)), static_cast<int32_t>(k.size(1)),
@@ -354,7 +357,7 @@ at::Tensor paged_rope_kv_append_attention(
     at::Tensor sin, at::Tensor k_pages, at::Tensor v_pages, at::Tensor block_table,
     at::Tensor request_indices, double scale, c10::optional<at::Tensor> q_out_opt,
     c10::optional<at::Tensor> attn_out_opt, int64_t chunk, int64_t rotary_dim, bool pdl,
-    c10::optional<at::Tensor> workspace_opt) {
+    c10::optional<at::Tensor> workspace_opt, bool workspace_zeroed) {
   TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && k_pages.dim() == 4 && block_table.dim() == 2,
               "q must be [num_tokens, num_q_heads, head_dim], k [num_tokens, num_kv_heads, "
               "head_dim], k_pages [num_blocks, block_size, num_kv_heads, head_dim] and "
@@ -366,6 +369,9 @@ at::Tensor paged_rope_kv_append_attention(
   ao.scale = scale;
   ao.chunk = static_cast<int32_t>(chunk);
   ao.path = DRK_ATTN_PATH_TENSOR_CORES;
+  const bool given = workspace_opt.has_value() && workspace_opt->defined();
+  TORCH_CHECK(!workspace_zeroed || given, "workspace_zeroed=True needs a workspace");
+  ao.flags = workspace_zeroed ? DRK_ATTN_WORKSPACE_ZEROED : 0;
   const int32_t device = q.is_cuda() ? q.get_device() : -1;
   const int64_t need = drk_attention_workspace_bytes(
       q.size(0), static_cast<int32_t>(q.size(1)), static_cast<int32_t>(k.size(1)),
@@ -506,6 +512,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("chunk") = 0, py::arg("heads_per_cta") = 0, py::arg("rotary_dim") = 0,
         py::arg("pdl") = false, py::arg("strided_cache") = false,
         py::arg("workspace") = py::none(), py::arg("path") = "auto",
+        py::arg("workspace_zeroed") = false,
         "Fused RoPE + KV append + decode attention over positions [0, pos]; returns attn_out.");
   m.def("paged_rope_kv_append_attention", &paged_rope_kv_append_attention, py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"),
@@ -513,6 +520,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("request_indices"), py::arg("scale") = 0.0, py::arg("q_out") = py::none(),
         py::arg("attn_out") = py::none(), py::arg("chunk") = 0, py::arg("rotary_dim") = 0,
         py::arg("pdl") = false, py::arg("workspace") = py::none(),
+        py::arg("workspace_zeroed") = false,
         "Fused RoPE + append + decode attention over a paged (block-table) KV cache.");
   m.def("attention_workspace_bytes", &attention_workspace_bytes, py::arg("num_tokens"),
         py::arg("num_q_heads"), py::arg("num_kv_heads"), py::arg("head_dim"),

@@ -1114,6 +1114,17 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   }
   if (sh.fin_merge) merge_unit(tc_unit_at(p, a, sh.fin[0], sh.fin[1], sh.fin[2]), warp,
                                kTcBlock / 32);
+  // Leave the unit counter at zero for the next call on this workspace: every CTA has taken
+  // its last unit before the barrier above, so the last CTA to count its exit here resets the
+  // counter and the exit count (the arrival counters are reset by the CTAs that merge).
+  if (threadIdx.x == 0) {
+    int* unit_counter = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
+    __threadfence();
+    if (atomicAdd(unit_counter + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(unit_counter, 0);
+      atomicExch(unit_counter + 1, 0);
+    }
+  }
 }
 
 }  // namespace drk

@@ -94,7 +94,8 @@ def advance_positions(positions, delta=1, *, pdl=False):
 def fused_rope_kv_append_attention(q, k, v, positions, cos, sin, k_cache, v_cache,
                                    request_indices, *, scale=None, q_out=None, attn_out=None,
                                    chunk=0, heads_per_cta=0, rotary_dim=0, pdl=False,
-                                   strided_cache=False, workspace=None, path="auto"):
+                                   strided_cache=False, workspace=None, path="auto",
+                                   workspace_zeroed=False):
     """The fused append followed by the decode attention that reads the cache, one launch.
 
     Appends exactly as fused_rope_kv_append (K slot = RoPE(k), V slot = v), then returns
@@ -105,16 +106,20 @@ def fused_rope_kv_append_attention(q, k, v, positions, cos, sin, k_cache, v_cach
     heads_per_cta tune the grid (0 = chosen by the library); workspace, when given, is a
     contiguous uint8 device tensor of at least attention_workspace_bytes(...) bytes (same
     tuning and path). path: "auto" (tensor cores for fp16/bf16 with head_dim 128, CUDA cores
-    otherwise), "tensor_cores" or "cuda_cores"."""
+    otherwise), "tensor_cores" or "cuda_cores". workspace_zeroed=True says the given
+    workspace's counters are zero, which every call leaves them (unless a bounded wait ran
+    out), so a workspace zeroed once can be passed call after call without the per-call
+    zeroing."""
     return require().fused_rope_kv_append_attention(
         q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
         0.0 if scale is None else float(scale), q_out, attn_out, chunk, heads_per_cta,
-        rotary_dim, pdl, strided_cache, workspace, path)
+        rotary_dim, pdl, strided_cache, workspace, path, workspace_zeroed)
 
 
 def paged_rope_kv_append_attention(q, k, v, positions, cos, sin, k_pages, v_pages, block_table,
                                    request_indices, *, scale=None, q_out=None, attn_out=None,
-                                   chunk=0, rotary_dim=0, pdl=False, workspace=None):
+                                   chunk=0, rotary_dim=0, pdl=False, workspace=None,
+                                   workspace_zeroed=False):
     """fused_rope_kv_append_attention over a paged cache: k_pages/v_pages
     [num_blocks, block_size, Hkv, D], block_table [num_requests, max_blocks] (positions' dtype);
     position p of request r lives in block block_table[r, p // block_size], row
@@ -124,7 +129,7 @@ def paged_rope_kv_append_attention(q, k, v, positions, cos, sin, k_pages, v_page
     return require().paged_rope_kv_append_attention(
         q, k, v, positions, cos, sin, k_pages, v_pages, block_table, request_indices,
         0.0 if scale is None else float(scale), q_out, attn_out, chunk, rotary_dim, pdl,
-        workspace)
+        workspace, workspace_zeroed)
 
 
 def attention_workspace_bytes(num_tokens, num_q_heads, num_kv_heads, head_dim, cache_alloc_len,

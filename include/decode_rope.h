@@ -211,9 +211,16 @@ typedef struct drk_attention_options {
                              count (the tensor-core kernel rounds it up to a multiple of 128) */
   int32_t heads_per_cta;  /* CUDA-core kernel: query heads per CTA, 0 (chosen), 1, 2, 4 or 8 */
   int32_t path;           /* DRK_ATTN_PATH_* */
-  int32_t reserved0;
+  int32_t flags;          /* DRK_ATTN_WORKSPACE_ZEROED */
   int64_t reserved;
 } drk_attention_options;
+
+/* drk_attention_options.flags. The workspace's counters are already zero, so the call skips
+ * zeroing them (one memset node less per call, which a graph-captured decode loop notices).
+ * Every call leaves a workspace's counters at zero again, so a workspace zeroed once (e.g.
+ * cudaMemset to 0 at allocation) may be passed with this flag call after call -- except after
+ * a call that set DRK_STATUS_TIMEOUT: zero it again before the next. */
+enum { DRK_ATTN_WORKSPACE_ZEROED = 1u << 0 };
 
 /* Kernel choice of drk_fused_rope_kv_append_attention (drk_attention_options.path). AUTO takes
  * the tensor-core (tcgen05 + TMA) kernel for fp16/bf16 with head_dim 128 and the CUDA-core

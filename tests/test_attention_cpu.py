@@ -18,7 +18,7 @@ ERR_INVALID, ERR_UNSUPPORTED = -1, -3
 class AttnOptions(ctypes.Structure):
     _fields_ = [("scale", ctypes.c_double), ("chunk", ctypes.c_int32),
                 ("heads_per_cta", ctypes.c_int32), ("path", ctypes.c_int32),
-                ("reserved0", ctypes.c_int32), ("reserved", ctypes.c_int64)]
+                ("flags", ctypes.c_int32), ("reserved", ctypes.c_int64)]
 
 
 @pytest.fixture(scope="module")

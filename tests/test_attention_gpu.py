@@ -349,3 +349,41 @@ def test_paged_cache_rejects_unsupported_shapes():
     with pytest.raises(RuntimeError, match="block sizes"):
         ops().paged_rope_kv_append_attention(*[t.cuda() for t in case[:6]], kp.cuda(), vp.cuda(),
                                              table.cuda(), case[8].cuda())
+
+
+@pytest.mark.parametrize("path,chunk", [("tensor_cores", 256), ("tensor_cores", 0),
+                                        ("cuda_cores", 128)])
+def test_a_zeroed_workspace_stays_zeroed_and_can_skip_the_per_call_zeroing(path, chunk):
+    """Every call leaves the workspace's counters (arrival counters and the persistent grid's
+    unit counter) at zero, so a workspace zeroed once can be passed with workspace_zeroed=True
+    call after call: three such calls give the same bits as the default path (which zeroes the
+    counters itself), and the counters read zero after each."""
+    case = make_case(31, 40, 16, 4, 128, 1024, torch.bfloat16)
+    q, k, v, p, cos, sin, kc, vc, ri = [t.cuda() for t in case]
+    hpc = 4      # CUDA-core kernel: all 4 query heads of a KV head in one CTA (one head block)
+    nbytes = ops().attention_workspace_bytes(40, 16, 4, 128, 1024, torch.bfloat16, chunk=chunk,
+                                             heads_per_cta=hpc, path=path)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    # the counter region comes first: 40 tokens x 4 KV heads x 1 head block arrival counters
+    # (+ the unit counter and exit count of the tensor-core kernel), rounded up to 768 bytes
+    counters = ws[:768].view(torch.int32)
+    for step in range(3):
+        pos = (p + step).clamp(max=1023)
+        kc_a, vc_a, kc_b, vc_b = kc.clone(), vc.clone(), kc.clone(), vc.clone()
+        want = ops().fused_rope_kv_append_attention(q, k, v, pos, cos, sin, kc_a, vc_a, ri,
+                                                    chunk=chunk, heads_per_cta=hpc, path=path)
+        got = ops().fused_rope_kv_append_attention(q, k, v, pos, cos, sin, kc_b, vc_b, ri,
+                                                   chunk=chunk, heads_per_cta=hpc, path=path,
+                                                   workspace=ws, workspace_zeroed=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), step
+        assert torch.equal(kc_b.view(torch.int16), kc_a.view(torch.int16))
+        assert torch.equal(vc_b.view(torch.int16), vc_a.view(torch.int16))
+        assert int(counters.abs().sum()) == 0, step
+
+
+def test_workspace_zeroed_needs_a_workspace():
+    case = make_case(3, 2, 8, 2, 128, 64, torch.bfloat16)
+    args = [t.cuda() for t in case]
+    with pytest.raises(RuntimeError, match="needs a workspace"):
+        ops().fused_rope_kv_append_attention(*args, workspace_zeroed=True)
