@@ -934,23 +934,70 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
                "frac_of_hbm_peak": bytes_call / us / 1e3 / peak}
         try:
             from flash_attn import flash_attn_with_kvcache
+            if bs % 256:
+                raise ValueError(f"flash_attn takes pages of 256 positions and up, not {bs}")
 
             def both(x):
                 def run():
-                    ops.paged_rope_kv_append(x["q"], x["k"], x["v"], x["p"], cos, sin, x["kp"],
-                                             x["vp"], x["table"], x["ri"])
-                    flash_attn_with_kvcache(x["qo"].view(T, 1, Hq, D), x["kp"], x["vp"],
+                    q_rot = ops.paged_rope_kv_append(x["q"], x["k"], x["v"], x["p"], cos, sin,
+                                                     x["kp"], x["vp"], x["table"], x["ri"])
+                    flash_attn_with_kvcache(q_rot.view(T, 1, Hq, D), x["kp"], x["vp"],
                                             cache_seqlens=x["p"] + 1, block_table=x["table"])
                 return run
             res["separate_us"] = graph_us([both(x) for x in st])
             res["separate"] = "paged append, then flash_attn_with_kvcache with the block table"
             res["speedup_vs_separate"] = res["separate_us"] / us
         except Exception as e:  # noqa: BLE001 -- an unavailable baseline is reported, not fatal
-            res["separate"] = f"unavailable: {type(e).__name__}: {str(e)[:160]}"
+            why = f"{type(e).__name__}: {str(e)[:120]}"
+            try:
+                res.update(flashinfer_separate(st, T, Hq, Hkv, D, bs, cos, sin, device, graph_us))
+                res["speedup_vs_separate"] = res["separate_us"] / us
+            except Exception as e2:  # noqa: BLE001
+                res["separate"] = (f"unavailable: flash_attn {why}; flashinfer "
+                                   f"{type(e2).__name__}: {str(e2)[:120]}")
         out[f"ragged_b64_paged{bs}"] = res
         del st
         torch.cuda.empty_cache()
     return out
+
+
+def flashinfer_separate(st, T, Hq, Hkv, D, bs, cos, sin, device, graph_us):
+    """The separate baseline over a paged cache with any page size: this build's paged append,
+    then flashinfer's batch decode over the same pages (its [num_pages, page_size, Hkv, D]
+    "NHD" layout is this build's page layout), each input set planned once outside the graph;
+    the faster of its CUDA-core and tensor-core decode kernels is reported."""
+    import flashinfer
+    from decode_llm_kernel_b200.cuda import ops
+    best = None
+    for tensor_cores in (False, True):
+        runs = []
+        for x in st:
+            lens = x["p"].to(torch.int64) + 1
+            npages = (lens + bs - 1) // bs
+            indptr = torch.zeros(T + 1, dtype=torch.int32, device=device)
+            indptr[1:] = torch.cumsum(npages, 0)
+            used = torch.arange(x["table"].shape[1], device=device)[None, :] < npages[:, None]
+            indices = x["table"][used].to(torch.int32)
+            last = ((lens - 1) % bs + 1).to(torch.int32)
+            work = torch.empty(128 << 20, dtype=torch.uint8, device=device)
+            w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(
+                work, "NHD", use_cuda_graph=True, use_tensor_cores=tensor_cores,
+                paged_kv_indptr_buffer=indptr, paged_kv_indices_buffer=indices,
+                paged_kv_last_page_len_buffer=last)
+            w.plan(indptr, indices, last, Hq, Hkv, D, bs, q_data_type=x["q"].dtype,
+                   kv_data_type=x["kp"].dtype)
+
+            def run(x=x, w=w, keep=(work, indptr, indices, last)):
+                q_rot = ops.paged_rope_kv_append(x["q"], x["k"], x["v"], x["p"], cos, sin,
+                                                 x["kp"], x["vp"], x["table"], x["ri"])
+                w.run(q_rot, (x["kp"], x["vp"]))
+            runs.append(run)
+        t = graph_us(runs)
+        if best is None or t < best[0]:
+            best = (t, tensor_cores)
+    return {"separate_us": best[0],
+            "separate": (f"paged append, then flashinfer BatchDecodeWithPagedKVCacheWrapper "
+                         f"(pages of {bs}, use_tensor_cores={best[1]}, the faster of the two)")}
 
 
 def operator_ladder(device, seed, ref):

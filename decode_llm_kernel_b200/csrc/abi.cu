@@ -299,17 +299,14 @@ Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens, int32_t s
 // The bulk-copy kernel's plan: eligible only if every row block it copies is one contiguous,
 // 16-byte-aligned run. It takes calls of DRK_STAGED_MIN_TOKENS tokens and up; measured on B200
 // (Mistral-shaped rows, fp16, graph-replayed launches with programmatic dependent launch), the
-// register kernel is faster up to 512 tokens (3.02 against 3.70 us) and the bulk-copy kernel
-// from 1024 (5.83 against 6.00 us; 4096 tokens: 19.4 against 21.9 us).
+// register kernel is faster at 512 tokens (3.04 against 3.78 us) and the bulk-copy kernel from
+// 768 (4.51 against 4.93 us; 1024: 5.89 against 6.09; 4096: 18.9 against 22.1 us).
 #ifndef DRK_STAGED_MIN_TOKENS
-#define DRK_STAGED_MIN_TOKENS 1024
+#define DRK_STAGED_MIN_TOKENS 768
 #endif
 // Pipeline depth of the bulk-copy kernel and the shared memory one CTA may use for its stages.
 #ifndef DRK_STAGED_STAGES
 #define DRK_STAGED_STAGES 3
-#endif
-#ifndef DRK_STAGED_SMEM_BUDGET
-#define DRK_STAGED_SMEM_BUDGET (192 * 1024)
 #endif
 
 struct StagedPlan {
@@ -322,7 +319,7 @@ struct StagedPlan {
 StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
                        const drk_tensor* q_out, const drk_tensor* k_cache,
                        const drk_tensor* v_cache, int64_t T, int64_t Hq, int64_t Hkv,
-                       int64_t D, int64_t R, int64_t es) {
+                       int64_t D, int64_t R, int64_t es, int32_t stages_hint = 0) {
   StagedPlan pl;
   auto fail = [&](const char* why) {
     pl.why = why;
@@ -360,7 +357,10 @@ StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tenso
   pl.groups = static_cast<int>(std::max<int64_t>(
       1, std::min<int64_t>(rot_rows, drk::kStagedThreadsPerBlock / pl.nrot)));
   const int64_t stage = (q_bytes + 2 * kv_bytes + 127) / 128 * 128;
-  int stages = static_cast<int>(std::min<int64_t>(DRK_STAGED_STAGES, DRK_STAGED_SMEM_BUDGET / stage));
+  if (stages_hint < 0 || stages_hint == 1 || stages_hint > 8)
+    invalid("staged_stages must be 0 (chosen by the library) or in [2, 8], got ", stages_hint);
+  int stages = static_cast<int>(std::min<int64_t>(stages_hint ? stages_hint : DRK_STAGED_STAGES,
+                                                  DRK_STAGED_SMEM_BUDGET / stage));
   if (stages < 2) {
     if (2 * stage > 200 * 1024) return fail("one token's rows do not fit two shared-memory stages");
     stages = 2;
@@ -369,6 +369,7 @@ StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tenso
   pl.sp.kv_bytes = static_cast<uint32_t>(kv_bytes);
   pl.sp.stage_bytes = static_cast<uint32_t>(stage);
   pl.sp.stages = stages;
+  pl.sp.deepen = stages_hint == 0 ? 1 : 0;
   pl.ok = true;
   return pl;
 }
@@ -543,7 +544,8 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   if (force_staged && force_register)
     invalid("DRK_FLAG_FORCE_STAGED_PATH and DRK_FLAG_FORCE_REGISTER_PATH are exclusive");
   if (!force_register && (force_staged || T >= DRK_STAGED_MIN_TOKENS)) {
-    const StagedPlan pl = plan_staged(q, k, v, q_out, k_cache, v_cache, T, Hq, Hkv, D, R, es);
+    const StagedPlan pl = plan_staged(q, k, v, q_out, k_cache, v_cache, T, Hq, Hkv, D, R, es,
+                                      o.staged_stages);
     if (pl.ok) {
       p.nrot = pl.nrot;
       p.G = pl.groups;

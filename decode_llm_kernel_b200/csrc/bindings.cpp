@@ -223,7 +223,8 @@ at::Tensor fused_rope_kv_append_ex(at::Tensor q, at::Tensor k, at::Tensor v,
                                    at::Tensor request_indices, int64_t rotary_dim, bool pdl,
                                    bool strided_cache, c10::optional<at::Tensor> inv_freq,
                                    c10::optional<at::Tensor> q_out_opt, const std::string& path,
-                                   int64_t row_splits, int64_t rows_per_thread) {
+                                   int64_t row_splits, int64_t rows_per_thread,
+                                   int64_t staged_stages) {
   at::Tensor q_out;
   if (q_out_opt.has_value() && q_out_opt->defined()) q_out = *q_out_opt;
   else if (q.dim() == 3) q_out = empty_like_rows(q, q.size(1));
@@ -235,6 +236,7 @@ at::Tensor fused_rope_kv_append_ex(at::Tensor q, at::Tensor k, at::Tensor v,
               row_splits);
   o.row_splits = static_cast<int32_t>(row_splits);
   o.rows_per_thread = static_cast<int32_t>(rows_per_thread);
+  o.staged_stages = static_cast<int32_t>(staged_stages);
   const drk_tensor dq = describe(q), dk = describe(k), dv = describe(v),
                    dp = describe(positions), dc = describe(cos), ds = describe(sin),
                    dkc = describe(k_cache), dvc = describe(v_cache),
@@ -493,6 +495,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("pdl") = false, py::arg("strided_cache") = false,
         py::arg("inv_freq") = py::none(), py::arg("q_out") = py::none(),
         py::arg("path") = "auto", py::arg("row_splits") = 0, py::arg("rows_per_thread") = 0,
+        py::arg("staged_stages") = 0,
         "fused_rope_kv_append with partial rotary, PDL, strided caches, in-register trig.");
   m.def("paged_rope_kv_append", &paged_rope_kv_append, py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("positions"), py::arg("cos"), py::arg("sin"), py::arg("k_pages"),

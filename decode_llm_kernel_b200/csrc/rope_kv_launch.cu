@@ -140,10 +140,10 @@ int sm_count(int device) {
 }
 
 template <typename E, typename Idx, int VB, Cache C>
-cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp,
+cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp_in,
                               const LaunchShape& shape, cudaStream_t stream) {
   auto kernel = rope_kv_staged_kernel<E, Idx, VB, C>;
-  const size_t smem = static_cast<size_t>(sp.stages) * (sp.stage_bytes + sizeof(uint64_t));
+  StagedParams sp = sp_in;
   const int threads = shape.lanes * shape.groups;
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
@@ -155,6 +155,7 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp,
   static std::map<int, bool> opted_in;
   static std::map<std::pair<int, std::pair<size_t, int>>, int> occupancy;
   int per_sm = 0;
+  size_t smem = static_cast<size_t>(sp.stages) * (sp.stage_bytes + sizeof(uint64_t));
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!opted_in[device]) {
@@ -166,15 +167,35 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp,
       if (err != cudaSuccess) return err;
       opted_in[device] = true;
     }
-    const auto key = std::make_pair(device, std::make_pair(smem, threads));
-    auto it = occupancy.find(key);
-    if (it == occupancy.end()) {
-      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
-      if (err != cudaSuccess) return err;
-      if (per_sm < 1) return cudaErrorInvalidConfiguration;
-      occupancy[key] = per_sm;
-    } else {
-      per_sm = it->second;
+    auto resident = [&](size_t bytes, int* out) -> cudaError_t {
+      const auto key = std::make_pair(device, std::make_pair(bytes, threads));
+      auto it = occupancy.find(key);
+      if (it != occupancy.end()) {
+        *out = it->second;
+        return cudaSuccess;
+      }
+      cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(out, kernel, threads, bytes);
+      if (e != cudaSuccess) return e;
+      occupancy[key] = *out;
+      return cudaSuccess;
+    };
+    err = resident(smem, &per_sm);
+    if (err != cudaSuccess) return err;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    // A deeper pipeline when every CTA walks many tokens: measured on B200 with Mistral-shaped
+    // fp16 rows (12 KB a token, PDL chain), one more stage -- one CTA fewer per SM -- gains
+    // 2-3% from about 4.8 tokens a CTA up (4096 tokens: 19.4 -> 18.9 us), while below that
+    // the CTA it costs shows as a longer tail (2048 tokens: 10.4 -> 11.2 us).
+    if (sp.deepen) {
+      const double per_cta = static_cast<double>(p.T) / (static_cast<double>(sm_count(device)) * per_sm);
+      const size_t deeper = static_cast<size_t>(sp.stages + 1) * (sp.stage_bytes + sizeof(uint64_t));
+      int per_sm_deeper = 0;
+      if (per_cta >= 4.8 && deeper <= static_cast<size_t>(DRK_STAGED_SMEM_BUDGET) &&
+          resident(deeper, &per_sm_deeper) == cudaSuccess && per_sm_deeper >= 1) {
+        sp.stages += 1;
+        smem = deeper;
+        per_sm = per_sm_deeper;
+      }
     }
   }
   const int64_t slots = static_cast<int64_t>(sm_count(device)) * per_sm;

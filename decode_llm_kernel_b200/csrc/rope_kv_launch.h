@@ -71,12 +71,18 @@ struct LaunchShape {
 cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits, int vb,
                            int mode, int cache, const LaunchShape& shape, cudaStream_t stream);
 
+// Shared memory one CTA of the bulk-copy kernel may use for its stages.
+#ifndef DRK_STAGED_SMEM_BUDGET
+#define DRK_STAGED_SMEM_BUDGET (192 * 1024)
+#endif
+
 // Stage geometry of the bulk-copy kernel (rope_kv_staged.cuh), in bytes.
 struct StagedParams {
   uint32_t q_bytes;      // Hq * D * es: one token's Q rows
   uint32_t kv_bytes;     // Hkv * D * es: one token's K (or V) rows
   uint32_t stage_bytes;  // q_bytes + 2 * kv_bytes, rounded up to 128
   int32_t stages;        // pipeline depth
+  int32_t deepen;        // the launcher may add a stage when CTAs walk many tokens each
 };
 
 // Fused mode only. shape.grid is ignored: the launcher sizes a persistent grid of

@@ -40,7 +40,8 @@ def fused_rope_kv_append(q, k, v, positions, cos, sin, k_cache, v_cache, request
 
 def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, request_indices,
                             *, rotary_dim=0, pdl=False, strided_cache=False, inv_freq=None,
-                            q_out=None, path="auto", row_splits=0, rows_per_thread=0):
+                            q_out=None, path="auto", row_splits=0, rows_per_thread=0,
+                            staged_stages=0):
     """fused_rope_kv_append with:
     rotary_dim     rotate only the first rotary_dim dims (table [P, rotary_dim]), copy the rest;
     pdl            programmatic dependent launch (indices and table read before waiting on the
@@ -56,10 +57,12 @@ def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, requ
                    kernel for large token counts when it can;
     row_splits     register kernel: CTAs that share one token's head rows (0 = chosen by the
                    library from the token count);
-    rows_per_thread register kernel: head rows a thread holds, 1 or 3 (0 = chosen)."""
+    rows_per_thread register kernel: head rows a thread holds, 1 or 3 (0 = chosen);
+    staged_stages  bulk-copy kernel: tokens a CTA stages at once, 2..8 (0 = chosen)."""
     return require().fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache,
                                              request_indices, rotary_dim, pdl, strided_cache,
-                                             inv_freq, q_out, path, row_splits, rows_per_thread)
+                                             inv_freq, q_out, path, row_splits, rows_per_thread,
+                                             staged_stages)
 
 
 def paged_rope_kv_append(q, k, v, positions, cos, sin, k_pages, v_pages, block_table,

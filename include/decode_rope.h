@@ -116,7 +116,10 @@ typedef struct drk_options {
                                because drk_rope_forward leaves k_rot rows of such tokens
                                unwritten, so they hold no defined value. 0: every K row is
                                written (the reference's kv_append). */
-  int64_t reserved[2];
+  int32_t staged_stages;  /* bulk-copy kernel: tokens staged per CTA at once, 2..8 (0 = the
+                             library's choice, bounded by shared memory) */
+  int32_t reserved1;
+  int64_t reserved;
 } drk_options;
 
 /*

@@ -143,7 +143,7 @@ def _mistral_inputs(tokens, seed):
 def test_mistral_b4096_and_its_batch_shards_through_the_bulk_copy_kernel(tokens):
     a = _mistral_inputs(tokens, SEED + tokens)
     assert a.q.dtype == torch.float16
-    q_auto = call_and_check(a, pdl=True)                 # >= 512 tokens: staged by default
+    q_auto = call_and_check(a, pdl=True)        # the default kernel: register at 512 tokens
     q_staged = call_and_check(a, path="staged")
     assert bits_equal(q_auto.cpu(), q_staged.cpu())
 
