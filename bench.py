@@ -51,7 +51,7 @@ from decode_llm_kernel_b200.harness.configs import WORKLOADS, make_positions  # 
 FALLBACK_HBM_GBS = 6650.0
 # ncu captures (profiles/): DRAM bytes read + written per launch
 DECODE32_NCU_DRAM_BYTES = 878848 + 0
-MISTRAL_NCU_DRAM_BYTES = 51522560 + 5620480
+MISTRAL_NCU_DRAM_BYTES = 51449088 + 5161984
 E2E_STEPS_PER_GRAPH = 32
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "achieved HBM GB/s per decode step (algorithmic bytes / device time), with us/call"
@@ -475,9 +475,11 @@ def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters
            "parity": parity_label(counts)}
     if name == "mistral_b4096" and world == 1 and impl == "ours":
         out["traffic"] = MISTRAL_NCU_DRAM_BYTES
-        out["traffic_note"] = ("ncu, caches cut to 128 positions: reads 51.5 MB = the "
-                               "algorithmic reads; 5.6 MB of the 51.4 MB of writes reach DRAM "
-                               "within the launch, the rest drains from L2 afterwards")
+        out["traffic_note"] = ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                               "profiles/rope_kv_staged_kernel_mistral_b4096_fp16.md (caches cut "
+                               "to 128 positions): reads 51.4 MB = the algorithmic reads; 5.2 MB "
+                               "of the 51.4 MB of writes reach DRAM within the launch, the rest "
+                               "drains from L2 afterwards")
     del kc, vc, sets
     torch.cuda.empty_cache()
     return out
