@@ -46,8 +46,10 @@ cudaError_t launch_one(const KernelParams& p, const LaunchShape& shape, cudaStre
       const int64_t sms = sm_count(device);
       const int threads = shape.lanes * shape.groups;
       if (ctas > sms) {
-        const int64_t full = sms * resident_ctas(rope_kv_kernel<E, Idx, VB, M, C, 1, false>, threads);
-        const int64_t lean = sms * resident_ctas(rope_kv_kernel<E, Idx, VB, M, C, 1, true>, threads);
+        const int64_t full =
+            sms * resident_ctas(rope_kv_kernel<E, Idx, VB, M, C, 1, false>, threads);
+        const int64_t lean =
+            sms * resident_ctas(rope_kv_kernel<E, Idx, VB, M, C, 1, true>, threads);
         if (full > 0 && lean > 0 && (ctas + lean - 1) / lean < (ctas + full - 1) / full)
           return launch_one<E, Idx, VB, M, C, 1, true>(p, shape, stream);
       }
@@ -187,8 +189,10 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp_in,
     // 2-3% from about 4.8 tokens a CTA up (4096 tokens: 19.4 -> 18.9 us), while below that
     // the CTA it costs shows as a longer tail (2048 tokens: 10.4 -> 11.2 us).
     if (sp.deepen) {
-      const double per_cta = static_cast<double>(p.T) / (static_cast<double>(sm_count(device)) * per_sm);
-      const size_t deeper = static_cast<size_t>(sp.stages + 1) * (sp.stage_bytes + sizeof(uint64_t));
+      const double per_cta =
+          static_cast<double>(p.T) / (static_cast<double>(sm_count(device)) * per_sm);
+      const size_t deeper =
+          static_cast<size_t>(sp.stages + 1) * (sp.stage_bytes + sizeof(uint64_t));
       int per_sm_deeper = 0;
       if (per_cta >= 4.8 && deeper <= static_cast<size_t>(DRK_STAGED_SMEM_BUDGET) &&
           resident(deeper, &per_sm_deeper) == cudaSuccess && per_sm_deeper >= 1) {
