@@ -773,7 +773,8 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-ATTENTION_CASES = ("full_cache_b32", "ragged_b64", "ragged_b64_paged16", "ragged_b64_paged256")
+ATTENTION_CASES = ("full_cache_b32", "ragged_b64", "full_cache_b32_d64", "ragged_b64_d64",
+                   "ragged_b64_paged16", "ragged_b64_paged256")
 
 
 def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
@@ -787,6 +788,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
       ragged_b64:      the decode loop's layer, positions U[0, 8192) (the baseline is our fused
                        append, then flash_attn's kv-cache decode with per-sequence lengths, when
                        flash_attn runs on this GPU);
+      full_cache_b32_d64, ragged_b64_d64: the same two with head_dim 64 (Llama-3.2-1B heads,
+                       32:8:64);
       ragged_b64_paged{16,256}: the same over a paged cache (pages shuffled through the block
                        table; the baseline is our paged append, then flash_attn's kv-cache
                        decode with the block table, which takes pages of 256 positions).
@@ -796,7 +799,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
     from decode_llm_kernel_b200.cuda import ops
     from decode_llm_kernel_b200.rope_tables import build_rope_tables
     Hq, Hkv, D, S, dt = 32, 8, 128, 8192, torch.bfloat16
-    cos, sin = build_rope_tables(S, D, 500000.0, device=device)
+    tables = {d: build_rope_tables(S, d, 500000.0, device=device) for d in (64, 128)}
+    cos, sin = tables[D]
     out = {}
 
     def graph_us(fns):
@@ -825,9 +829,12 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
         del g
         return s0.elapsed_time(s1) * 1e3 / (reps * len(fns))
 
-    for label, T, full in (("full_cache_b32", 32, True), ("ragged_b64", 64, False)):
+    for label, T, full, D in (("full_cache_b32", 32, True, 128), ("ragged_b64", 64, False, 128),
+                              ("full_cache_b32_d64", 32, True, 64),
+                              ("ragged_b64_d64", 64, False, 64)):
         if only is not None and label != only:
             continue
+        cos, sin = tables[D]
         gen = torch.Generator(device=device).manual_seed(seed)
         st = []
         for _ in range(sets):
@@ -898,6 +905,8 @@ def attention_probe(device, seed, peak, sets=2, reps=12, only=None):
         torch.cuda.empty_cache()
 
     # the decode layer over a paged cache: pages shuffled through the block table
+    D = 128
+    cos, sin = tables[D]
     for bs in (16, 256):
         if only is not None and only != f"ragged_b64_paged{bs}":
             continue

@@ -613,9 +613,10 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
   AttentionPlan pl;
   if (ao.path < DRK_ATTN_PATH_AUTO || ao.path > DRK_ATTN_PATH_TENSOR_CORES)
     invalid("path must be DRK_ATTN_PATH_AUTO, _CUDA_CORES or _TENSOR_CORES, got ", ao.path);
-  const bool tc_shape = es == 2 && D == 128;
+  const bool tc_shape = es == 2 && (D == 128 || D == 64);
   if (ao.path == DRK_ATTN_PATH_TENSOR_CORES && !tc_shape)
-    throw Unsupported("the tensor-core attention kernel takes fp16/bf16 with head_dim 128");
+    throw Unsupported(
+        "the tensor-core attention kernel takes fp16/bf16 with head_dim 64 or 128");
   if (tc_shape && ao.path != DRK_ATTN_PATH_CUDA_CORES) {
     pl.tc = true;
     pl.hpb = 16;
@@ -623,14 +624,15 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
     int64_t chunk = ao.chunk;
     if (chunk < 0) invalid("chunk must be >= 0, got ", chunk);
     if (chunk == 0) {
-      // Cost model of the persistent grid, fitted to B200 sweeps (batch 4..64, 2048..32768
+      // Cost model of the persistent grid, fitted to B200 sweeps (batch 1..64, 2048..32768
       // positions, GQA and MQA): units of one chunk run in rounds of one per SM; a full round
-      // streams at the HBM rate, a partial round of r units at min(HBM, r x one SM's TMA
-      // rate, ~90 GB/s with three 64 KB stages in flight); every round adds ~3 us of unit
-      // start and epilogue, and ~3 us more when chunks are merged. Positions live on the
-      // device, so every sequence is taken as S long. Candidates: 512 (four tiles) doubling
-      // up to S, then S itself (no merge).
-      constexpr double kHbm = 6.6e12, kPerSm = 90e9, kRound = 3e-6, kMerge = 3e-6;
+      // streams at the HBM rate, a partial round of r units at min(HBM, r x one SM's rate:
+      // ~90 GB/s with 128 dims, ~45 GB/s with 64, where a 64 KB tile takes 24 tensor-core
+      // products instead of 16); every round adds ~3 us of unit start and epilogue, and ~3 us
+      // more when chunks are merged. Positions live on the device, so every sequence is taken
+      // as S long. Candidates: 512 doubling up to S, then S itself (no merge).
+      constexpr double kHbm = 6.6e12, kRound = 3e-6, kMerge = 3e-6;
+      const double kPerSm = D == 64 ? 45e9 : 90e9;
       const int64_t heads = std::max<int64_t>(1, T * Hkv * pl.nhb);
       const int64_t sms = std::max(1, drk::device_sm_count(device));
       const double row_bytes = 2.0 * D * es;
@@ -649,7 +651,9 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
         if (cand >= whole) break;
       }
     }
-    pl.chunk = (chunk + 127) / 128 * 128;
+    // Whole tiles: 128 positions of 128 dims, or 256 of 64 dims (64 KB of K and V either way).
+    const int64_t tile = D == 64 ? 256 : 128;
+    pl.chunk = (chunk + tile - 1) / tile * tile;
     pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);
     // Arrival counters of the units, then the persistent grid's unit counter and its count
     // of CTAs that have finished (the last one resets both).
@@ -758,8 +762,8 @@ void attention_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* 
   const int64_t S = paged ? block_table->sizes[1] * block_size : k_cache->sizes[1];
   const AttentionPlan pl = plan_attention(T, Hq, Hkv, D, S, q->dtype, ao, device);
   if (paged && !pl.tc)
-    throw Unsupported("paged fused attention takes fp16/bf16 with head_dim 128 (the tensor-core "
-                      "kernel)");
+    throw Unsupported("paged fused attention takes fp16/bf16 with head_dim 64 or 128 (the "
+                      "tensor-core kernel)");
   if (T == 0) return;
   const int64_t es = elem_size(q->dtype);
   uintptr_t addr = reinterpret_cast<uintptr_t>(k_cache->data) |

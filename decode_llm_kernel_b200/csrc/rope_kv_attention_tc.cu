@@ -41,7 +41,21 @@ cudaError_t encode_cache_map(CUtensorMap* map, const void* base, bool bf16,
       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
   CUresult r;
-  if (p.block_table != nullptr) {
+  if (p.block_table != nullptr && p.D == 64) {
+    // Page pool [num_blocks, block_size, Hkv, 64] over its own strides as {64 dims, Hkv,
+    // block_size, pages}: a box holds a page slice's 128-byte rows of one head, which land as
+    // the tile's 1024-byte swizzle atoms [row group][8 rows][128 bytes].
+    const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(p.Hkv),
+                                static_cast<cuuint64_t>(p.block_size),
+                                static_cast<cuuint64_t>(p.num_blocks)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.c_hs) * 2,
+                                   static_cast<cuuint64_t>(p.c_ss) * 2,
+                                   static_cast<cuuint64_t>(p.c_bs) * 2};
+    const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
+    r = fn(map, type, 4, const_cast<void*>(base), dims, strides, box, estride,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (p.block_table != nullptr) {
     // Page pool [num_blocks, block_size, Hkv, 128], contiguous, as
     // {64 dims, 8 rows, 2 * Hkv half rows, block_size / 8 row groups, pages}: one box holds
     // a page slice's whole rows of one head (half rows 2g and 2g + 1) as 1024-byte swizzle
@@ -71,10 +85,12 @@ cudaError_t encode_cache_map(CUtensorMap* map, const void* base, bool bf16,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <typename E, typename Idx, int HR>
+template <typename E, typename Idx, int HR, int DIM>
 cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t units, bool pdl,
                       cudaStream_t stream) {
-  auto kernel = rope_kv_attention_tc_kernel<E, Idx, HR>;
+  auto kernel = rope_kv_attention_tc_kernel<E, Idx, HR, DIM>;
+  constexpr size_t smem = tc_smem_bytes<DIM>();
+  static_assert(smem <= 232448, "the kernel's shared memory exceeds a B200 CTA's 227 KB");
   int device = 0;
   cudaError_t err = cudaGetDevice(&device);
   if (err != cudaSuccess) return err;
@@ -84,7 +100,7 @@ cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t u
     std::lock_guard<std::mutex> lock(mu);
     if (!opted_in[device]) {
       err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kTcSmemBytes));
+                                 static_cast<int>(smem));
       if (err != cudaSuccess) return err;
       opted_in[device] = true;
     }
@@ -100,7 +116,7 @@ cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t u
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kTcBlock, 1, 1);
-  cfg.dynamicSmemBytes = kTcSmemBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   if (pdl) {
@@ -112,16 +128,16 @@ cudaError_t launch_tc(const KernelParams& p, const AttentionParams& a, int64_t u
   return cudaLaunchKernelEx(&cfg, kernel, p, a, kmap, vmap, units);
 }
 
-template <typename E, typename Idx>
+template <typename E, typename Idx, int DIM>
 cudaError_t launch_tc_hr(const KernelParams& p, const AttentionParams& a, int64_t units, bool pdl,
                          cudaStream_t stream) {
   // Real query heads per unit: the group size rounded up to a power of two, at most 16.
   const int g = a.group < kTcHeads ? a.group : kTcHeads;
-  if (g <= 1) return launch_tc<E, Idx, 1>(p, a, units, pdl, stream);
-  if (g <= 2) return launch_tc<E, Idx, 2>(p, a, units, pdl, stream);
-  if (g <= 4) return launch_tc<E, Idx, 4>(p, a, units, pdl, stream);
-  if (g <= 8) return launch_tc<E, Idx, 8>(p, a, units, pdl, stream);
-  return launch_tc<E, Idx, 16>(p, a, units, pdl, stream);
+  if (g <= 1) return launch_tc<E, Idx, 1, DIM>(p, a, units, pdl, stream);
+  if (g <= 2) return launch_tc<E, Idx, 2, DIM>(p, a, units, pdl, stream);
+  if (g <= 4) return launch_tc<E, Idx, 4, DIM>(p, a, units, pdl, stream);
+  if (g <= 8) return launch_tc<E, Idx, 8, DIM>(p, a, units, pdl, stream);
+  return launch_tc<E, Idx, 16, DIM>(p, a, units, pdl, stream);
 }
 
 }  // namespace
@@ -130,13 +146,21 @@ cudaError_t launch_rope_kv_attention_tc(const KernelParams& p, const AttentionPa
                                         int elem_code, int index_bits, int64_t units, bool pdl,
                                         cudaStream_t stream) {
   if (units <= 0) return cudaSuccess;
+  if (p.D != 64 && p.D != 128) return cudaErrorInvalidValue;
+  const bool d64 = p.D == 64;
   switch (elem_code) {
     case kElemF16:
-      return index_bits == 32 ? launch_tc_hr<F16, int>(p, a, units, pdl, stream)
-                              : launch_tc_hr<F16, long long>(p, a, units, pdl, stream);
+      if (index_bits == 32)
+        return d64 ? launch_tc_hr<F16, int, 64>(p, a, units, pdl, stream)
+                   : launch_tc_hr<F16, int, 128>(p, a, units, pdl, stream);
+      return d64 ? launch_tc_hr<F16, long long, 64>(p, a, units, pdl, stream)
+                 : launch_tc_hr<F16, long long, 128>(p, a, units, pdl, stream);
     case kElemBF16:
-      return index_bits == 32 ? launch_tc_hr<BF16, int>(p, a, units, pdl, stream)
-                              : launch_tc_hr<BF16, long long>(p, a, units, pdl, stream);
+      if (index_bits == 32)
+        return d64 ? launch_tc_hr<BF16, int, 64>(p, a, units, pdl, stream)
+                   : launch_tc_hr<BF16, int, 128>(p, a, units, pdl, stream);
+      return d64 ? launch_tc_hr<BF16, long long, 64>(p, a, units, pdl, stream)
+                 : launch_tc_hr<BF16, long long, 128>(p, a, units, pdl, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -1,12 +1,13 @@
 // Fused RoPE + KV append + decode attention on the 5th-generation tensor cores (tcgen05), for
-// 16-bit caches with head_dim 128: the bandwidth form of rope_kv_attention.cuh.
+// 16-bit caches with head_dim 128 or 64: the bandwidth form of rope_kv_attention.cuh.
 //
 // Work unit: (token t, KV head g, head block hb of up to 16 query heads, chunk of positions).
 // A persistent grid (one CTA per SM) takes units from a global atomic counter in the order they
 // are numbered (so the chunks and head blocks of one KV head run at about the same time) and
-// streams each unit's positions in tiles of 128 through a kTcStages-deep ring of shared-memory
-// stages. Taking units dynamically keeps the CTAs level even though the unit that holds the new
-// token, and whichever chunk arrives last and merges, do more work than the others.
+// streams each unit's positions in tiles of 128 through a ring of shared-memory stages (3 deep,
+// 6 with 64 dims). Taking units dynamically keeps the CTAs level even though the unit that
+// holds the new token, and whichever chunk arrives last and merges, do more work than the
+// others.
 // Five roles, synchronised by mbarriers only:
 //   - warp 4, the producer, takes the units, passes their indices to the other warps through a
 //     small queue in shared memory, and refills a stage as soon as the tensor core has finished
@@ -24,26 +25,30 @@
 //     output, or its partial, and merges a split KV head's chunks when it sees the last of
 //     them arrive.
 // So the softmax warps never wait on an MMA issue, a query rotation or a merge.
-// Per tile:
-//   1. TMA (cp.async.bulk.tensor, 128-byte swizzle) brings K[128 positions][128 dims] and V of
-//      the same rows, as two 64-dim boxes each (64 KB), completing on the stage's mbarrier;
-//   2. one thread issues S^T = K_tile . Q^T on the tensor cores (M = 128 positions, N = 16
-//      heads, K = 128 dims: 8 tcgen05.mma of K = 16; A = K tile, K-major; B = the unit's
-//      rotated queries, K-major) into a TMEM accumulator;
-//   3. each softmax thread reads its position's scores from TMEM (thread = TMEM lane = position),
-//      scales them, masks positions past the unit's end, takes the per-head tile maximum across
-//      the consumers, and writes p = 2^(s - m) to shared memory in the storage type (the B
-//      operand of the next product, K-major); per-thread partial row sums stay in registers;
-//   4. one thread issues O^T = V^T . P^T (M = 128 dims, N = 16 heads, K = 128 positions; A = the
-//      V tile read MN-major, B = P) into a second TMEM accumulator;
+// Per tile (64 KB: 128 positions of 128 dims, or 256 positions of 64 dims):
+//   1. TMA (cp.async.bulk.tensor, 128-byte swizzle) brings the tile's K rows and the V rows of
+//      the same positions as boxes of [128 positions][64 dims], completing on the stage's
+//      mbarrier;
+//   2. one thread issues S^T = K_tile . Q^T on the tensor cores, per 128-position row block
+//      (M = 128 positions, N = 16 heads, K = D dims: D / 16 tcgen05.mma of K = 16; A = K rows,
+//      K-major; B = the unit's rotated queries, K-major) into TMEM accumulators;
+//   3. each softmax thread reads its positions' scores from TMEM (thread = TMEM lane = position
+//      within a row block), scales them, masks positions past the unit's end, takes the
+//      per-head tile maximum across the consumers, and writes p = 2^(s - m) to shared memory
+//      in the storage type (the B operand of the next product, K-major); per-thread partial row
+//      sums stay in registers;
+//   4. one thread issues O^T = V^T . P^T (M = 128 dims, N = 16 heads, K = the tile's positions;
+//      A = the V rows read MN-major, dims past D read from a zero block, B = P) into a second
+//      TMEM accumulator;
 //   5. each thread (= one dim) reads its head values and folds them into its fp32 accumulator
 //      with the online-softmax correction.
 // S^T is triple-buffered and O^T and P double-buffered: QKs run up to two tiles ahead of the
-// softmax, and a tile's O^T is read after the next tile's softmax. Each tcgen05.mma of these shapes occupies
-// the tensor pipe for a fixed ~85 cycles whatever N is, so the pipe, not the math, sets the
-// floor of ~16 x 85 cycles per 128-position tile. Only the HR real heads of a unit (the group
-// size rounded up to a power of two, at most 16) go through the softmax; the MMA always runs
-// N = 16 with zero query rows.
+// softmax, and a tile's O^T is read after the next tile's softmax. Each tcgen05.mma of these
+// shapes holds its issuing thread for ~85-130 cycles whatever N is (the tensor pipe itself is
+// active for ~8 of them), so one SM streams ~90 GB/s with 128 dims (16 products per tile) and
+// ~45 GB/s with 64 dims (24). Only the HR real heads of a unit (the group size rounded up to a
+// power of two, at most 16) go through the softmax; the MMA always runs N = 16 with zero query
+// rows.
 // At a unit's end the partial (acc, m, l) per head goes to the workspace; the last chunk of a
 // (token, KV head, head block) to arrive merges them, exactly as in rope_kv_attention.cuh.
 //
@@ -58,8 +63,8 @@
 //
 // Waits are bounded (one second of %globaltimer); a wait that runs out -- no valid input
 // causes one -- sets DRK_STATUS_TIMEOUT and ends the CTA's walk; the producer waits (bounded)
-// for the copies it issued, and the CTA frees its TMEM and returns. No thread-block clusters and no cross-CTA
-// waits.
+// for the copies it issued, and the CTA frees its TMEM and returns. No thread-block clusters
+// and no cross-CTA waits.
 #pragma once
 
 #include <cuda.h>
@@ -79,14 +84,39 @@ constexpr int kTcPvWarp = 7;
 // Eight warps: each sub-partition's register file (16K) then holds two warps, so a thread may
 // use up to 255 registers.
 constexpr int kTcBlock = kTcThreads + 128;         // + producer, QK, aux and PV warps
-constexpr int kTcTile = 128;                       // positions per tile (MMA M of S^T)
+constexpr int kTcRows = 128;                       // MMA M: positions of S^T, dims of O^T
 constexpr int kTcHeads = 16;                       // query heads per unit (MMA N)
-constexpr int kTcDim = 128;                        // head_dim
+constexpr uint32_t kTcBoxBytes = kTcRows * 128;    // [128 rows][64 dims] of 2 bytes: 16 KB
 constexpr int kTcStages = 3;
-constexpr uint32_t kTcBoxBytes = kTcTile * 128;    // [128 rows][64 dims] of 2 bytes: 16 KB
-constexpr uint32_t kTcStageBytes = 4 * kTcBoxBytes;
-constexpr uint32_t kTcQBytes = 2 * kTcHeads * 128; // [2 dim halves][16 heads][128 B]
-constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 heads][128 B]
+constexpr int kTcSBufs = 3;                        // S^T accumulators in flight
+
+// Tile geometry per head_dim (64 or 128). A tile is 64 KB of K and V rows either way: 128
+// positions of 128 dims, or 256 positions of 64 dims, so the softmax, its barrier and the
+// output correction are paid once per 64 KB. A stage holds K then V, each as boxes of
+// [128 rows][64 dims] (row blocks, then dim halves); Q^T is [D / 64 dim halves][16 heads]
+// [128 B]; P is [tile / 64 position quarters][16 heads][128 B]. S^T takes tile / 128
+// accumulators of 16 columns (one per 128-position row block), O^T one: three S^T buffers and
+// two O^T buffers fill the 128 TMEM columns with 64 dims. O^T = V^T . P^T runs with M = 128
+// either way: with 64 dims each product's upper 64 rows are read from a 2 KB zero block after
+// the ring (the descriptor's leading-byte offset points there), so the accumulator keeps the
+// M = 128 TMEM layout (row i in lane i) and rows 64..127 come out zero.
+template <int DIM>
+struct TcGeom {
+  static_assert(DIM == 64 || DIM == 128, "the tensor-core path takes head_dim 64 or 128");
+  static constexpr int kTile = DIM == 64 ? 256 : 128;            // positions per tile
+  static constexpr int kRowBlocks = kTile / kTcRows;
+  static constexpr int kHalves = DIM / 64;
+  static constexpr uint32_t kVOff = kRowBlocks * kHalves * kTcBoxBytes;   // V's offset
+  static constexpr uint32_t kStageBytes = 2 * kVOff;
+  static constexpr uint32_t kZeroBytes = DIM == 64 ? 2048 : 0;   // two 8-row swizzle atoms
+  static constexpr uint32_t kRingBytes = kTcStages * kStageBytes + kZeroBytes;
+  static constexpr uint32_t kQBytes = kHalves * kTcHeads * 128;
+  static constexpr uint32_t kPBytes = (kTile / 64) * kTcHeads * 128;
+  static constexpr uint32_t kSCols = kRowBlocks * kTcHeads;      // columns of an S^T buffer
+  static constexpr uint32_t kOCol = kTcSBufs * kSCols;           // first O^T column
+  static constexpr uint32_t kTmemCols = 128;
+  static_assert(kOCol + 2 * kTcHeads <= kTmemCols, "S^T and O^T exceed the TMEM columns");
+};
 // Unit queue slots. The producer is at most kTcStages tiles ahead of the MMA warp, the prep
 // warp at most two units ahead of it (two Q buffers), the consumers at most two tiles behind it
 // and the epilogue warp at most one unit behind the consumers, so fewer than 8 queued units are
@@ -94,15 +124,14 @@ constexpr uint32_t kTcPBytes = 2 * kTcHeads * 128; // [2 position halves][16 hea
 constexpr int kTcQueue = 16;
 constexpr int kTcSortMax = 2048;                   // tokens ordered longest-first up to this
 constexpr int kTcSortBuckets = 256;                // length buckets of that order
-constexpr int kTcSBufs = 3;                        // S^T accumulators in flight
-constexpr uint32_t kTcOCol = kTcSBufs * 16;        // first O^T column
-constexpr uint32_t kTcTmemCols = 128;              // S^T at 0, 16, 32; O^T at 48, 64
 
+template <int DIM>
 struct TcShared {
-  uint8_t stage[kTcStages][kTcStageBytes];         // K lo, K hi, V lo, V hi boxes
-  uint8_t q[2][kTcQBytes];                         // Q^T operand, double-buffered across units
-  uint8_t pm[2][kTcPBytes];                        // P, double-buffered across tiles
-  float ep_acc[kTcHeads][kTcDim];                  // a unit's O accumulators for the epilogue
+  using G = TcGeom<DIM>;
+  uint8_t ring[G::kRingBytes];                     // stages (K boxes, V boxes), zero block
+  uint8_t q[2][G::kQBytes];                        // Q^T operand, double-buffered across units
+  uint8_t pm[2][G::kPBytes];                       // P, double-buffered across tiles
+  float ep_acc[kTcHeads][DIM];                     // a unit's O accumulators for the epilogue
   float ep_m[kTcHeads];
   float ep_l[kTcHeads];
   float red[2][kTcThreads / 32][kTcHeads];         // per-warp tile maxima, double-buffered
@@ -128,7 +157,10 @@ struct TcShared {
   int fin_merge;
   uint32_t tmem_base;
 };
-constexpr size_t kTcSmemBytes = sizeof(TcShared) + 1024;   // + alignment slack
+template <int DIM>
+constexpr size_t tc_smem_bytes() {
+  return sizeof(TcShared<DIM>) + 1024;   // + alignment slack
+}
 
 // Shared-memory matrix descriptor (tcgen05): start, leading and stride byte offsets (16-byte
 // units), descriptor version 1, swizzle layout in bits 61-63 (2 = 128-byte swizzle).
@@ -207,6 +239,25 @@ __device__ __forceinline__ bool consumer_any(bool v) {
   return r != 0;
 }
 
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 16 consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
@@ -256,7 +307,8 @@ struct TcUnit {
   bool bad;            // invalid position or request index
 };
 
-// A unit from its index and its token's position and request index.
+// A unit from its index and its token's position and request index (tiles of TILE positions).
+template <int TILE>
 __device__ __forceinline__ TcUnit tc_unit_at(const KernelParams& p, const AttentionParams& a,
                                              int64_t u, int64_t pos, int64_t ri) {
   TcUnit w;
@@ -272,33 +324,36 @@ __device__ __forceinline__ TcUnit tc_unit_at(const KernelParams& p, const Attent
   w.bad = w.pos < 0 || w.pos >= p.S || w.pos >= p.table_rows || w.ri < 0 || w.ri >= p.B;
   w.p0 = static_cast<int64_t>(w.chunk) * a.chunk;
   w.p1 = w.bad ? w.p0 : min(w.pos + 1, w.p0 + a.chunk);
-  w.ntiles = w.p1 > w.p0 ? static_cast<int>((w.p1 - w.p0 + kTcTile - 1) / kTcTile) : 0;
+  w.ntiles = w.p1 > w.p0 ? static_cast<int>((w.p1 - w.p0 + TILE - 1) / TILE) : 0;
   return w;
 }
 
-template <typename Idx>
+template <int TILE, typename Idx>
 __device__ __forceinline__ TcUnit tc_unit(const KernelParams& p, const AttentionParams& a,
                                           int64_t u) {
   const int64_t t = u / (static_cast<int64_t>(a.max_chunks) * a.nhb * p.Hkv);
-  return tc_unit_at(p, a, u, load_index<Idx>(p.positions, t),
-                    load_index<Idx>(p.request_indices, t));
+  return tc_unit_at<TILE>(p, a, u, load_index<Idx>(p.positions, t),
+                          load_index<Idx>(p.request_indices, t));
 }
 
-template <typename E, typename Idx, int HR>
+template <typename E, typename Idx, int HR, int DIM>
 __global__ void __launch_bounds__(kTcBlock, 1)
 rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
                             const __grid_constant__ AttentionParams a,
                             const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap, const int64_t units) {
   using raw = typename E::raw;
+  using G = TcGeom<DIM>;
+  constexpr int kStages = kTcStages;
+  constexpr int kTile = G::kTile;
   constexpr uint32_t kAB = std::is_same<E, BF16>::value ? 1u : 0u;
   static_assert(sizeof(raw) == 2, "the tensor-core path takes 16-bit caches");
   static_assert(HR >= 1 && HR <= kTcHeads, "HR real heads per unit, at most the MMA N");
-  constexpr uint32_t kIdescQK = tc_idesc(kAB, 0, 0, kTcTile, kTcHeads);
-  constexpr uint32_t kIdescPV = tc_idesc(kAB, 1, 0, kTcDim, kTcHeads);
+  constexpr uint32_t kIdescQK = tc_idesc(kAB, 0, 0, kTcRows, kTcHeads);
+  constexpr uint32_t kIdescPV = tc_idesc(kAB, 1, 0, kTcRows, kTcHeads);
 
   extern __shared__ uint8_t smem_raw[];
-  TcShared& sh = *reinterpret_cast<TcShared*>(
+  TcShared<DIM>& sh = *reinterpret_cast<TcShared<DIM>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = static_cast<int>(threadIdx.x);
   const int warp = tid >> 5, lane = tid & 31;
@@ -309,7 +364,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
   }
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
     }
@@ -329,12 +384,16 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     sh.fin_merge = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // P rows of heads past HR are never written per tile: zero both buffers once.
-  for (int i = tid; i < static_cast<int>(2 * kTcPBytes / 16); i += kTcBlock)
+  // P rows of heads past HR are never written per tile: zero both buffers once; so is the
+  // zero block that the upper rows of O^T read with 64 dims.
+  for (int i = tid; i < static_cast<int>(2 * G::kPBytes / 16); i += kTcBlock)
     reinterpret_cast<uint4*>(sh.pm)[i] = make_uint4(0u, 0u, 0u, 0u);
+  uint8_t* const zero_block = sh.ring + kStages * G::kStageBytes;
+  for (int i = tid; i < static_cast<int>(G::kZeroBytes / 16); i += kTcBlock)
+    reinterpret_cast<uint4*>(zero_block)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(&sh.tmem_base)), "r"(kTcTmemCols) : "memory");
+                 ::"r"(smem_u32(&sh.tmem_base)), "r"(G::kTmemCols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   proxy_fence_shared();
@@ -344,15 +403,18 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   const uint32_t tmem = sh.tmem_base;
   pdl_wait();
 
-  auto stage_of = [&](int64_t c) { return sh.stage[static_cast<int>(c % kTcStages)]; };
-  // Tile layout in a stage: K in the first 32 KB, V in the second, each as 128-byte swizzle
-  // atoms of 8 rows x 64 dims. Contiguous caches: [half][128 rows] (two 16 KB boxes); paged:
-  // [row group][half][8 rows] (one box per page slice). t_half is the offset of the upper 64
-  // dims, t_group the stride of 8-row groups.
+  auto stage_at = [&](int s) { return sh.ring + static_cast<uint32_t>(s) * G::kStageBytes; };
+  auto stage_of = [&](int64_t c) { return stage_at(static_cast<int>(c % kStages)); };
+  // Tile layout in a stage: K in the first half, V in the second, each as 128-byte swizzle
+  // atoms of 8 rows x 64 dims. 128 dims, contiguous caches: [half][128 rows] (two 16 KB
+  // boxes); paged: [row group][half][8 rows] (one box per page slice). 64 dims, both: [256
+  // rows] (two 16 KB boxes, or one per page slice). t_half is the offset of the upper 64 dims,
+  // t_group the stride of 8-row groups.
   const bool paged = p.block_table != nullptr;
-  const uint32_t t_half = paged ? 1024u : kTcBoxBytes;
-  const uint32_t t_group = paged ? 2048u : 1024u;
-  auto full_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kTcStages) & 1); };
+  const bool interleaved = DIM == 128 && paged;
+  const uint32_t t_half = interleaved ? 1024u : kTcBoxBytes;
+  const uint32_t t_group = interleaved ? 2048u : 1024u;
+  auto full_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kStages) & 1); };
   auto pair_parity = [&](int64_t c) { return static_cast<uint32_t>((c >> 1) & 1); };
   auto sbuf = [&](int64_t c) { return static_cast<int>(c % kTcSBufs); };
   auto s_parity = [&](int64_t c) { return static_cast<uint32_t>((c / kTcSBufs) & 1); };
@@ -373,15 +435,18 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
     const float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
     const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
-    raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+    raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{DIM};
+    constexpr int kPerLane = DIM / 32;   // dims lane + 32 i
     for (int h = h_first; h < nh; h += h_step) {
       const float* hw = ws + h * ws_head;
-      float M = -INFINITY, Ls = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+      float M = -INFINITY, Ls = 0.f, O[kPerLane];
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i) O[i] = 0.f;
       for (int cb = 0; cb < nchunks; cb += 32) {
         const int c = cb + lane;
-        const float mc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim)
+        const float mc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + DIM)
                                      : -INFINITY;
-        const float lc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + kTcDim + 1)
+        const float lc = c < nchunks ? __ldcg(hw + static_cast<int64_t>(c) * row + DIM + 1)
                                      : 0.f;
         float mg = fmaxf(M, mc);
 #pragma unroll
@@ -394,20 +459,20 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         for (int off = 16; off >= 1; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
         Ls = fmaf(Ls, rescale, lg);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) O[i] *= rescale;
+        for (int i = 0; i < kPerLane; ++i) O[i] *= rescale;
         const int nc = min(32, nchunks - cb);
 #pragma unroll 8
         for (int j = 0; j < nc; ++j) {
           const float wj = __shfl_sync(0xffffffffu, wc, j);
           const float* cp = hw + static_cast<int64_t>(cb + j) * row + lane;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) O[i] = fmaf(__ldcg(cp + 32 * i), wj, O[i]);
+          for (int i = 0; i < kPerLane; ++i) O[i] = fmaf(__ldcg(cp + 32 * i), wj, O[i]);
         }
         M = mg;
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(O[i] / Ls);
+      for (int i = 0; i < kPerLane; ++i)
+        out[h * int64_t{DIM} + lane + 32 * i] = E::from_f(O[i] / Ls);
     }
     if (lane == 0 && h_first == 0) a.counters[(w.t * p.Hkv + w.g) * a.nhb + w.hb] = 0;
   };
@@ -423,7 +488,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     const bool sorted = p.T > 1 && p.T <= kTcSortMax;
     if (sorted) {
       const int n = static_cast<int>(p.T);
-      int* cursor = reinterpret_cast<int*>(sh.stage[kTcStages - 1]);
+      int* cursor = reinterpret_cast<int*>(stage_at(kStages - 1));
       uint8_t* key = reinterpret_cast<uint8_t*>(cursor + kTcSortBuckets);
       for (int b = lane; b < kTcSortBuckets; b += 32) cursor[b] = 0;
       __syncwarp();
@@ -505,7 +570,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             const int64_t r = u / per_token;
             u = static_cast<int64_t>(sh.order[r]) * per_token + (u - r * per_token);
           }
-          const TcUnit w = tc_unit<Idx>(p, a, u);
+          const TcUnit w = tc_unit<kTile, Idx>(p, a, u);
           if (w.bad) {
             if (w.chunk == 0 && w.hb == 0 && w.g == 0 && p.status != nullptr) {
               uint32_t bad = 0;
@@ -529,7 +594,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       tri = __shfl_sync(0xffffffffu, tri, 0);
       index = tu;
       if (tu < 0) return TcUnit{-1, 0, 0, 0, 0, 0, 0, 0, 0, false};
-      return tc_unit_at(p, a, tu, tpos, tri);
+      return tc_unit_at<kTile>(p, a, tu, tpos, tri);
     };
     // Units are queued one ahead of the one being streamed, so the prep warp has a whole
     // unit's time to rotate the next unit's queries.
@@ -548,58 +613,82 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         need_next = false;
       };
       for (int tile = 0; tile < w.ntiles; ++tile) {
-        const int s = static_cast<int>(issued % kTcStages);
-        const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTcTile;
+        const int s = static_cast<int>(issued % kStages);
+        const int64_t z = w.p0 + static_cast<int64_t>(tile) * kTile;
         // Paged cache: box b of the tile holds the K (b even) or V rows of slice b / 2 of the
-        // tile's pages and is issued by lane b. A lane loads its page's block-table entry
-        // before the wait for a free stage, so the latency hides behind it. A tile starts on
-        // a multiple of 128 positions: with pages of at most 128 rows slice i is page
-        // first + i from row 0; a larger page holds the whole tile from row z - first * bs.
+        // tile, a.box_rows positions (the page size up to 128) that lie in one page, and is
+        // issued by lane b % 32 (64 dims: up to 64 boxes, two per lane). A lane loads its
+        // slices' block-table entries before the wait for a free stage, so the latency hides
+        // behind it. Slice i starts at position z + i * box_rows: page zs / bs, row zs % bs.
         constexpr int64_t kPastTable = INT64_MIN;   // a page past the request's table
-        int nbox = 0, row0 = 0;
-        int64_t blk = kPastTable;
-        if (p.block_table != nullptr) {
-          nbox = kTcTile / a.box_rows;
-          const int64_t first = z / p.block_size;
-          row0 = static_cast<int>(z - first * p.block_size);
-          const int64_t i = first + (lane >> 1);
-          if (lane < 2 * nbox && i < p.bt_stride)
-            blk = load_index<Idx>(p.block_table, w.ri * p.bt_stride + i);
+        constexpr int kSlots = DIM == 64 ? 2 : 1;   // boxes per lane
+        int nbox = 0;
+        int64_t blk[kSlots];
+        int brow[kSlots];
+#pragma unroll
+        for (int q = 0; q < kSlots; ++q) {
+          blk[q] = kPastTable;
+          brow[q] = 0;
+          const int b = lane + 32 * q;
+          if (p.block_table != nullptr) {
+            nbox = kTile / a.box_rows;
+            const int64_t zs = z + static_cast<int64_t>(b >> 1) * a.box_rows;
+            const int64_t pi = zs / p.block_size;
+            brow[q] = static_cast<int>(zs - pi * p.block_size);
+            if (b < 2 * nbox && pi < p.bt_stride)
+              blk[q] = load_index<Idx>(p.block_table, w.ri * p.bt_stride + pi);
+          }
         }
-        if (need_next && issued >= kTcStages) take_next();
-        if (issued >= kTcStages)
+        if (need_next && issued >= kStages) take_next();
+        if (issued >= kStages)
           ok = __all_sync(0xffffffffu,
                           tc_wait(&sh.empty[s],
-                                  static_cast<uint32_t>(((issued / kTcStages) + 1) & 1)));
+                                  static_cast<uint32_t>(((issued / kStages) + 1) & 1)));
         if (!ok) break;
-        uint8_t* st = sh.stage[s];
+        uint8_t* st = stage_at(s);
         if (p.block_table == nullptr) {
           if (lane == 0) {
-            mbar_expect_tx(&sh.full[s], kTcStageBytes);
-            const int zi = static_cast<int>(z), ri = static_cast<int>(w.ri);
-            tma_load_4d(st, &kmap, 0, w.g, zi, ri, &sh.full[s]);
-            tma_load_4d(st + kTcBoxBytes, &kmap, 64, w.g, zi, ri, &sh.full[s]);
-            tma_load_4d(st + 2 * kTcBoxBytes, &vmap, 0, w.g, zi, ri, &sh.full[s]);
-            tma_load_4d(st + 3 * kTcBoxBytes, &vmap, 64, w.g, zi, ri, &sh.full[s]);
+            // Boxes of 128 rows x 64 dims: row blocks, then dim halves.
+            mbar_expect_tx(&sh.full[s], G::kStageBytes);
+            const int ri = static_cast<int>(w.ri);
+#pragma unroll
+            for (int rb = 0; rb < G::kRowBlocks; ++rb) {
+              const int zi = static_cast<int>(z) + kTcRows * rb;
+#pragma unroll
+              for (int hf = 0; hf < G::kHalves; ++hf) {
+                const uint32_t off = (rb * G::kHalves + hf) * kTcBoxBytes;
+                tma_load_4d(st + off, &kmap, 64 * hf, w.g, zi, ri, &sh.full[s]);
+                tma_load_4d(st + G::kVOff + off, &vmap, 64 * hf, w.g, zi, ri, &sh.full[s]);
+              }
+            }
           }
         } else {
           // A slice's box holds its rows' 1024-byte swizzle atoms in the paged tile layout
-          // [row group][half][8 rows][128 bytes], K at 0 and V at 32 KB.
-          if (lane == 0) mbar_expect_tx(&sh.full[s], kTcStageBytes);
+          // (128 dims: [row group][half][8 rows][128 bytes]; 64 dims: [8 rows][128 bytes] per
+          // row group), K at 0 and V at kVOff.
+          if (lane == 0) mbar_expect_tx(&sh.full[s], G::kStageBytes);
           __syncwarp();
-          if (lane < 2 * nbox) {
-            const int i = lane >> 1, kind = lane & 1;
+#pragma unroll
+          for (int q = 0; q < kSlots; ++q) {
+            const int b = lane + 32 * q;
+            if (b >= 2 * nbox) continue;
+            const int i = b >> 1, kind = b & 1;
             const int r0 = i * a.box_rows;
-            if (blk < 0 || blk >= p.num_blocks) {
+            int64_t bk = blk[q];
+            if (bk < 0 || bk >= p.num_blocks) {
               // Outside the pool: TMA reads zeros there (coordinate past the last page).
-              if (kind == 0 && blk != kPastTable && z + r0 < w.p1 && p.status != nullptr)
+              if (kind == 0 && bk != kPastTable && z + r0 < w.p1 && p.status != nullptr)
                 atomicOr(p.status, kStatusBlock);
-              blk = p.num_blocks;
+              bk = p.num_blocks;
             }
-            const uint32_t off = static_cast<uint32_t>(kind) * (kTcStageBytes / 2) +
-                                 static_cast<uint32_t>(r0) * 256u;
-            tma_load_5d(st + off, kind ? &vmap : &kmap, 0, 0, 2 * w.g, row0 >> 3,
-                        static_cast<int>(blk), &sh.full[s]);
+            const uint32_t off = static_cast<uint32_t>(kind) * G::kVOff +
+                                 static_cast<uint32_t>(r0) * (128u * G::kHalves);
+            if constexpr (DIM == 128)
+              tma_load_5d(st + off, kind ? &vmap : &kmap, 0, 0, 2 * w.g, brow[q] >> 3,
+                          static_cast<int>(bk), &sh.full[s]);
+            else
+              tma_load_4d(st + off, kind ? &vmap : &kmap, 0, w.g, brow[q],
+                          static_cast<int>(bk), &sh.full[s]);
           }
         }
         ++issued;
@@ -611,8 +700,8 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       enqueue(-1, 0, 0);
       if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
       // Every copy this CTA issued lands before its shared memory goes away.
-      for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i)
-        (void)mbar_wait(&sh.full[i % kTcStages], static_cast<uint32_t>((i / kTcStages) & 1));
+      for (int64_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+        (void)mbar_wait(&sh.full[i % kStages], static_cast<uint32_t>((i / kStages) & 1));
     }
   } else if (warp == kTcAuxWarp) {
     // ---- aux warp, per queued unit k: prepare unit k, then finish unit k - 1 ----
@@ -632,29 +721,32 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         if (a.q_vec) {
           // Full rotary, 16-byte rows: item = (head, 8-dim chunk of the first half); both halves
           // of the rotate_half pair from one lane. A lane's items share their chunk c (and its
-          // cos/sin), for heads lane / 8 + 4 i; every load is issued before the first store.
-          const int c = lane & 7;
+          // cos/sin), for heads lane / kChunks + (32 / kChunks) i; every load is issued before
+          // the first store.
+          constexpr int kChunks = DIM / 16;                 // 8-dim chunks of a half row
+          constexpr int kPasses = kTcHeads * kChunks / 32;  // heads per lane
+          const int c = lane % kChunks;
           const float4 c0 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c));
           const float4 c1 = __ldg(reinterpret_cast<const float4*>(crow + 8 * c + 4));
           const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c));
           const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow + 8 * c + 4));
-          uint4 xs1[4], xs2[4];
+          uint4 xs1[kPasses], xs2[kPasses];
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int hh = (lane >> 3) + 4 * r;
+          for (int r = 0; r < kPasses; ++r) {
+            const int hh = lane / kChunks + (32 / kChunks) * r;
             xs1[r] = xs2[r] = make_uint4(0u, 0u, 0u, 0u);
             if (hh < nh) {
               const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
                                 static_cast<int64_t>(h0 + hh) * p.q_hs;
               xs1[r] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-              xs2[r] = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c);
+              xs2[r] = *reinterpret_cast<const uint4*>(qrow + DIM / 2 + 8 * c);
             }
           }
           const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
           const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int hh = (lane >> 3) + 4 * r;
+          for (int r = 0; r < kPasses; ++r) {
+            const int hh = lane / kChunks + (32 / kChunks) * r;
             uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
             if (hh < nh) {
               float f1[8], f2[8];
@@ -675,18 +767,21 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
               hi = make_uint4(wh[0], wh[1], wh[2], wh[3]);
               if (a.q_out != nullptr && w.chunk == 0) {
                 raw* qo =
-                    reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+                    reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{DIM};
                 *reinterpret_cast<uint4*>(qo + 8 * c) = lo;
-                *reinterpret_cast<uint4*>(qo + 64 + 8 * c) = hi;
+                *reinterpret_cast<uint4*>(qo + DIM / 2 + 8 * c) = hi;
               }
             }
+            // Dim d of head hh sits in box d / 64, chunk (d % 64) / 8 of row hh.
+            constexpr int kHi = DIM / 2;
             *reinterpret_cast<uint4*>(qs + sw128(hh, c)) = lo;
-            *reinterpret_cast<uint4*>(qs + kTcHeads * 128 + sw128(hh, c)) = hi;
+            *reinterpret_cast<uint4*>(qs + (kHi >> 6) * (kTcHeads * 128) +
+                                      sw128(hh, ((kHi & 63) >> 3) + c)) = hi;
           }
         } else {
-          for (int idx = lane; idx < kTcHeads * (kTcDim / 2); idx += 32) {
-            const int hh = idx / (kTcDim / 2);
-            const int d = 2 * (idx - hh * (kTcDim / 2));       // an even dim; pairs d, d + 1
+          for (int idx = lane; idx < kTcHeads * (DIM / 2); idx += 32) {
+            const int hh = idx / (DIM / 2);
+            const int d = 2 * (idx - hh * (DIM / 2));          // an even dim; pairs d, d + 1
             raw y0 = 0, y1 = 0;
             if (hh < nh) {
               const raw* qrow = reinterpret_cast<const raw*>(p.q) + w.t * p.q_ts +
@@ -707,7 +802,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
               y1 = ys[1];
               if (a.q_out != nullptr && w.chunk == 0) {
                 raw* qo =
-                    reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{kTcDim};
+                    reinterpret_cast<raw*>(a.q_out) + (w.t * p.Hq + h0 + hh) * int64_t{DIM};
                 qo[d] = y0;
                 qo[d + 1] = y1;
               }
@@ -738,10 +833,11 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           }
           // Dims lane + 32 j: every load is issued before the first store (the cache append
           // could alias the sources as far as the compiler knows).
-          raw kx[4], k1[4], k2[4], vx[4];
-          float cx[4], sx[4];
+          constexpr int kPerLane = DIM / 32;
+          raw kx[kPerLane], k1[kPerLane], k2[kPerLane], vx[kPerLane];
+          float cx[kPerLane], sx[kPerLane];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < kPerLane; ++j) {
             const int d = lane + 32 * j;
             const int i = d < half_r ? d : d - half_r;
             kx[j] = krow[d];
@@ -756,7 +852,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
             }
           }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < kPerLane; ++j) {
             const int d = lane + 32 * j;
             raw kr = kx[j];
             if (d < p.R)
@@ -784,24 +880,25 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         const int h0 = w.g * a.group + w.hb * kTcHeads;
         const int nh = min(HR, a.group - w.hb * kTcHeads);
         const int nchunks = static_cast<int>((w.pos + a.chunk) / a.chunk);
-        float acc[HR][4], mh[HR], lh[HR];
+        constexpr int kPerLane = DIM / 32;   // dims lane + 32 i
+        float acc[HR][kPerLane], mh[HR], lh[HR];
 #pragma unroll
         for (int h = 0; h < HR; ++h) {
           mh[h] = sh.ep_m[h];
           lh[h] = sh.ep_l[h];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[h][i] = sh.ep_acc[h][lane + 32 * i];
+          for (int i = 0; i < kPerLane; ++i) acc[h][i] = sh.ep_acc[h][lane + 32 * i];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.ep_empty);   // the softmax warps may refill the buffer
-        raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{kTcDim};
+        raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{DIM};
         if (nchunks == 1) {
 #pragma unroll
           for (int h = 0; h < HR; ++h)
             if (h < nh)
 #pragma unroll
-              for (int i = 0; i < 4; ++i)
-                out[h * int64_t{kTcDim} + lane + 32 * i] = E::from_f(acc[h][i] / lh[h]);
+              for (int i = 0; i < kPerLane; ++i)
+                out[h * int64_t{DIM} + lane + 32 * i] = E::from_f(acc[h][i] / lh[h]);
           return true;
         }
         float* ws = a.workspace + (w.t * p.Hq + h0) * static_cast<int64_t>(a.max_chunks) * row;
@@ -811,10 +908,10 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           if (h >= nh) continue;
           float* dst = ws + h * ws_head + static_cast<int64_t>(w.chunk) * row;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = acc[h][i];
+          for (int i = 0; i < kPerLane; ++i) dst[lane + 32 * i] = acc[h][i];
           if (lane == 0) {
-            dst[kTcDim] = mh[h];
-            dst[kTcDim + 1] = lh[h];
+            dst[DIM] = mh[h];
+            dst[DIM + 1] = lh[h];
           }
         }
         __syncwarp();
@@ -842,7 +939,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       const bool last_unit = msg[0] < 0;
       TcUnit w{};
       if (!last_unit) {
-        w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+        w = tc_unit_at<kTile>(p, a, msg[0], msg[1], msg[2]);
         ok = prep_unit(k, w);
         if (!ok) break;
       }
@@ -879,7 +976,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       if (!ok) break;
       const int64_t* msg = sh.uq[k % kTcQueue];
       if (msg[0] < 0) break;
-      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+      const TcUnit w = tc_unit_at<kTile>(p, a, msg[0], msg[1], msg[2]);
       const int qb = static_cast<int>(k & 1);
       ok = __all_sync(0xffffffffu, tc_wait(&sh.q_full[qb], static_cast<uint32_t>((k >> 1) & 1)));
       if (!ok) break;
@@ -887,24 +984,25 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       const uint32_t qaddr = smem_u32(sh.q[qb]);
       for (int j = 0; j < w.ntiles; ++j) {
         const int64_t c = cj + j;
-        const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
-        const bool patch_tile = holds_pos && w.pos >= tp0 && w.pos < tp0 + kTcTile;
+        const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTile;
+        const bool patch_tile = holds_pos && w.pos >= tp0 && w.pos < tp0 + kTile;
         // Lane 0 alone polls unless every lane is about to write into the tile.
         bool mine = true;
         if (lane == 0 && c >= kTcSBufs)
           mine = tc_wait(&sh.s_free[sbuf(c)], static_cast<uint32_t>(((c / kTcSBufs) - 1) & 1));
         if (mine && (patch_tile || lane == 0))
-          mine = tc_wait(&sh.full[c % kTcStages], full_parity(c));
+          mine = tc_wait(&sh.full[c % kStages], full_parity(c));
         ok = __all_sync(0xffffffffu, mine);
         if (!ok) break;
         if (patch_tile) {
-          // The new token's K and V row, 16 chunks each, into the staged tile.
+          // The new token's K and V row, D / 8 16-byte chunks each, into the staged tile.
           const uint32_t r = static_cast<uint32_t>(w.pos - tp0);
           const int ch = lane & 15;
           const bool is_v = lane >= 16;
-          uint8_t* base = stage_of(c) + (is_v ? 2 : 0) * kTcBoxBytes;
+          uint8_t* base = stage_of(c) + (is_v ? G::kVOff : 0u);
           const uint32_t at = (r >> 3) * t_group + (ch >> 3) * t_half + sw128(r & 7u, ch & 7);
-          *reinterpret_cast<uint4*>(base + at) = is_v ? sh.vn[qb][ch] : sh.kn[qb][ch];
+          if (ch < DIM / 8)
+            *reinterpret_cast<uint4*>(base + at) = is_v ? sh.vn[qb][ch] : sh.kn[qb][ch];
           proxy_fence_shared();
           __syncwarp();
         }
@@ -912,12 +1010,19 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           tc_fence_after();
           const int b = sbuf(c);
           const uint32_t kb = smem_u32(stage_of(c));
+          // One S^T accumulator of 16 columns per 128-position row block of the tile.
 #pragma unroll
-          for (int ks = 0; ks < kTcDim / 16; ++ks) {
-            const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
-            const uint64_t ad = tc_sdesc(kb + (ks >> 2) * t_half + off, 16, t_group);
-            const uint64_t bd = tc_sdesc(qaddr + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
-            tc_mma(tmem + b * kTcHeads, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+          for (int rb = 0; rb < G::kRowBlocks; ++rb) {
+            const uint32_t kr = kb + rb * (kTcRows / 8) * t_group;
+#pragma unroll
+            for (int ks = 0; ks < DIM / 16; ++ks) {
+              const uint32_t off = static_cast<uint32_t>((ks & 3) * 32);
+              const uint64_t ad = tc_sdesc(kr + (ks >> 2) * t_half + off, 16, t_group);
+              const uint64_t bd =
+                  tc_sdesc(qaddr + (ks >> 2) * (kTcHeads * 128) + off, 16, 1024);
+              tc_mma(tmem + b * G::kSCols + rb * kTcHeads, ad, bd, kIdescQK,
+                     ks > 0 ? 1u : 0u);
+            }
           }
           tc_commit(&sh.s_bar[b]);
           // After the unit's last QK, the prep warp may refill this Q buffer.
@@ -939,22 +1044,28 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         if (!ok) break;
         const int64_t* msg = sh.uq[k % kTcQueue];
         if (msg[0] < 0) break;
-        const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+        const TcUnit w = tc_unit_at<kTile>(p, a, msg[0], msg[1], msg[2]);
         for (int j = 0; j < w.ntiles; ++j, ++c) {
           ok = tc_wait(&sh.p_bar[c & 1], pair_parity(c));
           if (!ok) break;
           tc_fence_after();
           const int b = static_cast<int>(c & 1);
-          const uint32_t vb = smem_u32(stage_of(c) + 2 * kTcBoxBytes), pb = smem_u32(sh.pm[b]);
+          const uint32_t vb = smem_u32(stage_of(c) + G::kVOff), pb = smem_u32(sh.pm[b]);
+          const uint32_t zb = smem_u32(zero_block);
 #pragma unroll
-          for (int ks = 0; ks < kTcTile / 16; ++ks) {
-            const uint64_t ad = tc_sdesc(vb + ks * 2 * t_group, t_half, t_group);
+          for (int ks = 0; ks < kTile / 16; ++ks) {
+            // The second 64-row atom of V^T: the upper dims, or (64 dims) the zero block, the
+            // same 16 zero rows for every product: it sits past every stage, so the offset is
+            // positive and below 256 KB.
+            const uint32_t va = vb + ks * 2 * t_group;
+            const uint32_t upper = DIM == 128 ? t_half : zb - va;
+            const uint64_t ad = tc_sdesc(va, upper, t_group);
             const uint64_t bd =
                 tc_sdesc(pb + (ks >> 2) * (kTcHeads * 128) + (ks & 3) * 32, 16, 1024);
-            tc_mma(tmem + kTcOCol + b * kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
+            tc_mma(tmem + G::kOCol + b * kTcHeads, ad, bd, kIdescPV, ks > 0 ? 1u : 0u);
           }
           tc_commit(&sh.o_bar[b]);
-          tc_commit(&sh.empty[static_cast<int>(c % kTcStages)]);
+          tc_commit(&sh.empty[static_cast<int>(c % kStages)]);
         }
       }
       if (!ok && p.status != nullptr) atomicOr(p.status, kStatusTimeout);
@@ -974,12 +1085,16 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     bool pending = false;
     int64_t pend_k = 0, pend_c = 0;
     float pend_acc[HR];
+    // O^T buffer ob: this thread's dim for the 16 heads.
+    auto read_o = [&](int ob, float* o) {
+      tc_ld16(tmem + tmem_lane + G::kOCol + ob * kTcHeads, o);
+    };
     // Adds the pending unit's last O^T and hands the unit to the epilogue warp.
     auto hand_over = [&]() {
       ok = tc_wait(&sh.o_bar[pend_c & 1], pair_parity(pend_c)) && ok;
       tc_fence_after();
       float o[kTcHeads];
-      tc_ld16(tmem + tmem_lane + kTcOCol + static_cast<int>(pend_c & 1) * kTcHeads, o);
+      read_o(static_cast<int>(pend_c & 1), o);
 #pragma unroll
       for (int h = 0; h < HR; ++h) pend_acc[h] += o[h];
       tc_fence_before();
@@ -987,7 +1102,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       if (consumer_any(!ok)) return false;
 #pragma unroll
       for (int h = 0; h < HR; ++h) {
-        sh.ep_acc[h][tid] = pend_acc[h];
+        if (tid < DIM) sh.ep_acc[h][tid] = pend_acc[h];   // lanes past D hold zero rows
         if (tid == 0) {
           const int pb = static_cast<int>(pend_k & 1);
           sh.ep_m[h] = sh.pend_m[pb][h];
@@ -1007,7 +1122,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       }
       const int64_t* msg = sh.uq[k % kTcQueue];
       if (msg[0] < 0) break;
-      const TcUnit w = tc_unit_at(p, a, msg[0], msg[1], msg[2]);
+      const TcUnit w = tc_unit_at<kTile>(p, a, msg[0], msg[1], msg[2]);
       const int nh = min(HR, a.group - w.hb * kTcHeads);
 
       float m_run[HR], lp[HR], acc[HR], corr_prev[HR];
@@ -1023,17 +1138,24 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
         const int b = static_cast<int>(c & 1);
         ok = tc_wait(&sh.s_bar[sbuf(c)], s_parity(c)) && ok;
         tc_fence_after();
-        float sc[kTcHeads];
-        tc_ld16(tmem + tmem_lane + sbuf(c) * kTcHeads, sc);
+        // Position rb * 128 + tid of the tile, for each 128-position row block rb.
+        float sc[G::kRowBlocks][kTcHeads];
+        if constexpr (G::kRowBlocks == 2)
+          tc_ld32(tmem + tmem_lane + sbuf(c) * G::kSCols, &sc[0][0]);
+        else
+          tc_ld16(tmem + tmem_lane + sbuf(c) * G::kSCols, &sc[0][0]);
         tc_fence_before();
         mbar_arrive(&sh.s_free[sbuf(c)]);   // the QK issuer may reuse this S^T buffer
-        const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTcTile;
-        const bool live = tp0 + tid < w.p1;
+        const int64_t tp0 = w.p0 + static_cast<int64_t>(j) * kTile;
         float mx[HR];
 #pragma unroll
-        for (int h = 0; h < HR; ++h) {
-          sc[h] = h < nh ? (live ? sc[h] * scale : -INFINITY) : 0.f;
-          mx[h] = sc[h];
+        for (int rb = 0; rb < G::kRowBlocks; ++rb) {
+          const bool live = tp0 + rb * kTcRows + tid < w.p1;
+#pragma unroll
+          for (int h = 0; h < HR; ++h) {
+            sc[rb][h] = h < nh ? (live ? sc[rb][h] * scale : -INFINITY) : 0.f;
+            mx[h] = rb == 0 ? sc[rb][h] : fmaxf(mx[h], sc[rb][h]);
+          }
         }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1)
@@ -1049,21 +1171,25 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           break;
         }
         float corr_cur[HR];
-        {
-          const int half = tid >> 6, pc = tid & 63;
-          uint8_t* pb = sh.pm[b] + half * (kTcHeads * 128);
 #pragma unroll
-          for (int h = 0; h < HR; ++h) {
-            const float mt = fmaxf(fmaxf(sh.red[b][0][h], sh.red[b][1][h]),
-                                   fmaxf(sh.red[b][2][h], sh.red[b][3][h]));
-            const float m_new = fmaxf(m_run[h], mt);
-            corr_cur[h] = exp2f(m_run[h] - m_new);
-            const float e = exp2f(sc[h] - m_new);
-            lp[h] = fmaf(lp[h], corr_cur[h], e);
-            m_run[h] = m_new;
+        for (int h = 0; h < HR; ++h) {
+          const float mt = fmaxf(fmaxf(sh.red[b][0][h], sh.red[b][1][h]),
+                                 fmaxf(sh.red[b][2][h], sh.red[b][3][h]));
+          const float m_new = fmaxf(m_run[h], mt);
+          corr_cur[h] = exp2f(m_run[h] - m_new);
+          float es = 0.f;
+#pragma unroll
+          for (int rb = 0; rb < G::kRowBlocks; ++rb) {
+            // P is [position quarter][head][64 positions], K-major for the PV product.
+            const int pp = rb * kTcRows + tid, pc = pp & 63;
+            uint8_t* pb = sh.pm[b] + (pp >> 6) * (kTcHeads * 128);
+            const float e = exp2f(sc[rb][h] - m_new);
+            es = rb == 0 ? e : es + e;
             *reinterpret_cast<raw*>(pb + sw128(h, (pc * 2) >> 4) + ((pc * 2) & 15)) =
                 E::from_f(e);
           }
+          lp[h] = fmaf(lp[h], corr_cur[h], es);
+          m_run[h] = m_new;
         }
         // P(c) is ready, and this thread is done with O^T(c - 2).
         proxy_fence_shared();
@@ -1074,7 +1200,7 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
           ok = tc_wait(&sh.o_bar[b ^ 1], pair_parity(c - 1)) && ok;
           tc_fence_after();
           float o[kTcHeads];
-          tc_ld16(tmem + tmem_lane + kTcOCol + (b ^ 1) * kTcHeads, o);
+          read_o(b ^ 1, o);
 #pragma unroll
           for (int h = 0; h < HR; ++h) acc[h] = fmaf(acc[h], corr_prev[h], o[h]);
         } else if (pending && !hand_over()) {
@@ -1110,9 +1236,9 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTcTmemCols) : "memory");
+                 "r"(G::kTmemCols) : "memory");
   }
-  if (sh.fin_merge) merge_unit(tc_unit_at(p, a, sh.fin[0], sh.fin[1], sh.fin[2]), warp,
+  if (sh.fin_merge) merge_unit(tc_unit_at<kTile>(p, a, sh.fin[0], sh.fin[1], sh.fin[2]), warp,
                                kTcBlock / 32);
   // Leave the unit counter at zero for the next call on this workspace: every CTA has taken
   // its last unit before the barrier above, so the last CTA to count its exit here resets the

@@ -122,7 +122,7 @@ cudaError_t launch_rope_kv_attention(const KernelParams& p, const AttentionParam
                                      int elem_code, int index_bits, const AttentionShape& s,
                                      cudaStream_t stream);
 
-// rope_kv_attention_tc.cu: the tcgen05 form (16-bit, head_dim 128), a persistent grid over
+// rope_kv_attention_tc.cu: the tcgen05 form (16-bit, head_dim 64 or 128), a persistent grid over
 // `units` = T * Hkv * nhb * max_chunks work units of up to 16 query heads.
 cudaError_t launch_rope_kv_attention_tc(const KernelParams& p, const AttentionParams& a,
                                         int elem_code, int index_bits, int64_t units, bool pdl,

@@ -108,8 +108,8 @@ def fused_rope_kv_append_attention(q, k, v, positions, cos, sin, k_cache, v_cach
     appears at most once per call. q_out, when given, also receives q_rot. chunk and
     heads_per_cta tune the grid (0 = chosen by the library); workspace, when given, is a
     contiguous uint8 device tensor of at least attention_workspace_bytes(...) bytes (same
-    tuning and path). path: "auto" (tensor cores for fp16/bf16 with head_dim 128, CUDA cores
-    otherwise), "tensor_cores" or "cuda_cores". workspace_zeroed=True says the given
+    tuning and path). path: "auto" (tensor cores for fp16/bf16 with head_dim 64 or 128, CUDA
+    cores otherwise), "tensor_cores" or "cuda_cores". workspace_zeroed=True says the given
     workspace's counters are zero, which every call leaves them (unless a bounded wait ran
     out), so a workspace zeroed once can be passed call after call without the per-call
     zeroing."""
@@ -126,8 +126,8 @@ def paged_rope_kv_append_attention(q, k, v, positions, cos, sin, k_pages, v_page
     """fused_rope_kv_append_attention over a paged cache: k_pages/v_pages
     [num_blocks, block_size, Hkv, D], block_table [num_requests, max_blocks] (positions' dtype);
     position p of request r lives in block block_table[r, p // block_size], row
-    p % block_size. fp16/bf16 with head_dim 128; block_size a multiple of 8 dividing 128, or a
-    multiple of 128. A workspace, when given, holds at least attention_workspace_bytes(...,
+    p % block_size. fp16/bf16 with head_dim 64 or 128; block_size a multiple of 8 dividing 128,
+    or a multiple of 128. A workspace, when given, holds at least attention_workspace_bytes(...,
     cache_alloc_len=max_blocks * block_size, path="tensor_cores") bytes."""
     return require().paged_rope_kv_append_attention(
         q, k, v, positions, cos, sin, k_pages, v_pages, block_table, request_indices,

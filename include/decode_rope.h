@@ -226,8 +226,8 @@ typedef struct drk_attention_options {
 enum { DRK_ATTN_WORKSPACE_ZEROED = 1u << 0 };
 
 /* Kernel choice of drk_fused_rope_kv_append_attention (drk_attention_options.path). AUTO takes
- * the tensor-core (tcgen05 + TMA) kernel for fp16/bf16 with head_dim 128 and the CUDA-core
- * kernel otherwise; forcing the tensor-core kernel on another shape returns
+ * the tensor-core (tcgen05 + TMA) kernel for fp16/bf16 with head_dim 64 or 128 and the
+ * CUDA-core kernel otherwise; forcing the tensor-core kernel on another shape returns
  * DRK_ERR_UNSUPPORTED. */
 enum {
   DRK_ATTN_PATH_AUTO = 0,
@@ -280,10 +280,11 @@ DRK_API int drk_fused_rope_kv_append_attention(
  * contiguous of the index dtype; position p of request r lives in block block_table[r, p /
  * block_size], row p % block_size (the layout of drk_paged_rope_kv_append). No counterpart in
  * the reference, whose cache is one contiguous row per request and whose notes name the
- * block-table layout as the next step. fp16/bf16 with head_dim 128; block_size a multiple of 8
- * that divides 128, or a multiple of 128. Size the workspace with drk_attention_workspace_bytes
- * for cache_alloc_len = max_blocks_per_request * block_size. Block-table entries outside the
- * pool are read as zeros, skip the append, and set DRK_STATUS_BLOCK_OUT_OF_RANGE.
+ * block-table layout as the next step. fp16/bf16 with head_dim 64 or 128; block_size a
+ * multiple of 8 that divides 128, or a multiple of 128. Size the workspace with
+ * drk_attention_workspace_bytes for cache_alloc_len = max_blocks_per_request * block_size.
+ * Block-table entries outside the pool are read as zeros, skip the append, and set
+ * DRK_STATUS_BLOCK_OUT_OF_RANGE.
  */
 DRK_API int drk_paged_rope_kv_append_attention(
     const drk_tensor* q, const drk_tensor* k, const drk_tensor* v, const drk_tensor* positions,

@@ -50,9 +50,16 @@ def test_tensor_core_workspace_rounds_chunk_to_tiles(lib):
     # a chunk that is not a multiple of the 128-position tile is rounded up
     assert ws_bytes(lib, 4, 32, 8, 128, 1000, chunk=200, path=TENSOR_CORES) == \
         expected(4, 32, 8, 128, 1000, 256, 1, True)
-    # auto takes the tensor-core kernel for bf16 / head_dim 128
+    # auto takes the tensor-core kernel for bf16 / head_dim 128, and for head_dim 64
     assert ws_bytes(lib, 4, 32, 8, 128, 1000, chunk=256) == \
         expected(4, 32, 8, 128, 1000, 256, 1, True)
+    assert ws_bytes(lib, 4, 32, 8, 64, 1000, chunk=256) == \
+        expected(4, 32, 8, 64, 1000, 256, 1, True)
+    # with 64 dims a tile is 256 positions: chunks round up to a multiple of 256
+    assert ws_bytes(lib, 4, 32, 8, 64, 1000, chunk=200) == \
+        expected(4, 32, 8, 64, 1000, 256, 1, True)
+    assert ws_bytes(lib, 4, 32, 8, 64, 1000, chunk=384) == \
+        expected(4, 32, 8, 64, 1000, 512, 1, True)
 
 
 def test_tensor_core_splits_large_groups_into_blocks_of_16(lib):
@@ -73,7 +80,7 @@ def test_cuda_core_workspace(lib):
 @pytest.mark.parametrize("args, code, message", [
     (dict(Hq=6, Hkv=4, D=64), ERR_INVALID, "multiple of num_kv_heads"),
     (dict(Hq=4, Hkv=2, D=64, dtype=torch.float64), ERR_UNSUPPORTED, "fp32, fp16 and bf16"),
-    (dict(Hq=4, Hkv=2, D=96, path=TENSOR_CORES), ERR_UNSUPPORTED, "head_dim 128"),
+    (dict(Hq=4, Hkv=2, D=96, path=TENSOR_CORES), ERR_UNSUPPORTED, "head_dim 64 or 128"),
     (dict(Hq=4, Hkv=2, D=130), ERR_UNSUPPORTED, "multiple of 16 bytes"),
     (dict(Hq=4, Hkv=2, D=512), ERR_UNSUPPORTED, "head_dim <= 256"),
     (dict(Hq=4, Hkv=2, D=256, dtype=torch.float32), ERR_UNSUPPORTED, "head_dim <= 128"),

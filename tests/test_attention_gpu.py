@@ -112,36 +112,46 @@ def test_matches_oracle(head, dtype):
     check(case, run_gpu(case))
 
 
-TC_HEADS = [  # head_dim 128 shapes the tensor-core kernel takes
+TC_HEADS = [  # query / KV head shapes the tensor-core kernel takes (head_dim 64 or 128)
     ("gqa_llama3", 32, 8),
     ("mha_llama2", 8, 8),
     ("gqa8_70b", 16, 2),
     ("mqa_71", 71, 1),      # five blocks of up to 16 query heads per KV head
     ("gqa_20", 40, 2),      # a 16 + 4 split
 ]
+TC_DIMS = [128, 64]
 
 
+@pytest.mark.parametrize("D", TC_DIMS)
 @pytest.mark.parametrize("path", ["tensor_cores", "cuda_cores"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("head", TC_HEADS, ids=[h[0] for h in TC_HEADS])
-def test_both_kernels_match_oracle(head, dtype, path):
+def test_both_kernels_match_oracle(head, dtype, path, D):
     _, Hq, Hkv = head
-    case = make_case(31, 5, Hq, Hkv, 128, 700, dtype)
+    case = make_case(31, 5, Hq, Hkv, D, 700, dtype)
     check(case, run_gpu(case, path=path))
 
 
+@pytest.mark.parametrize("D", TC_DIMS)
 @pytest.mark.parametrize("chunk", [0, 128, 256, 1000, 4096])
-def test_tensor_core_chunks_and_tile_edges(chunk):
+def test_tensor_core_chunks_and_tile_edges(chunk, D):
     """Positions on both sides of tile (128) and chunk edges, and the last slot."""
     positions = [0, 1, 126, 127, 128, 129, 255, 256, 511, 999]
-    case = make_case(32, len(positions), 32, 8, 128, 1000, torch.bfloat16,
+    case = make_case(32, len(positions), 32, 8, D, 1000, torch.bfloat16,
                      positions=positions)
     check(case, run_gpu(case, chunk=chunk, path="tensor_cores"))
 
 
-def test_tensor_core_head_major_cache_int64_partial_rotary():
-    case = make_case(33, 6, 16, 4, 128, 600, torch.float16, R=64, index_dtype=torch.int64)
+@pytest.mark.parametrize("D", TC_DIMS)
+def test_tensor_core_head_major_cache_int64_partial_rotary(D):
+    case = make_case(33, 6, 16, 4, D, 600, torch.float16, R=D // 2, index_dtype=torch.int64)
     check(case, run_gpu(case, strided=True, path="tensor_cores"))
+
+
+def test_tensor_core_head_dim_64_long_cache():
+    """Falcon / Llama-3.2-1B-shaped heads over an 8192-position cache, many chunks per token."""
+    case = make_case(43, 12, 32, 8, 64, 8192, torch.bfloat16, theta=500000.0)
+    check(case, run_gpu(case, path="tensor_cores"))
 
 
 @pytest.mark.parametrize("chunk", [1, 7, 64, 4096])
@@ -151,11 +161,12 @@ def test_chunks_and_head_blocks(chunk, heads_per_cta):
     check(case, run_gpu(case, chunk=chunk, heads_per_cta=heads_per_cta))
 
 
+@pytest.mark.parametrize("D", TC_DIMS)
 @pytest.mark.parametrize("T", [300, 2100])
-def test_tensor_core_many_ragged_tokens(T):
+def test_tensor_core_many_ragged_tokens(T, D):
     """The grid hands out tokens longest first up to 2048 tokens (300: many equal positions,
     so the order's ties matter) and in index order beyond (2100)."""
-    case = make_case(41, T, 4, 1, 128, 200, torch.bfloat16)
+    case = make_case(41, T, 4, 1, D, 200, torch.bfloat16)
     check(case, run_gpu(case, path="tensor_cores"))
 
 
@@ -300,11 +311,12 @@ def gather(pages, table):
     return pages[table.long().flatten()].view(B, nblk * pages.shape[1], *pages.shape[2:])
 
 
+@pytest.mark.parametrize("D", TC_DIMS)
 @pytest.mark.parametrize("block_size", [8, 16, 32, 64, 128, 256])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_paged_cache_matches_oracle(block_size, dtype):
+def test_paged_cache_matches_oracle(block_size, dtype, D):
     from decode_llm_kernel_b200 import cuda
-    case = make_case(35, 5, 32, 8, 128, 512, dtype, B=7)
+    case = make_case(35, 5, 32, 8, D, 512, dtype, B=7)
     kp, vp, table = paged_from(case, block_size, 36)
     q, k, v, p, cos, sin, _, _, ri = [t.cuda() for t in case]
     kpd, vpd, tbl = kp.cuda(), vp.cuda(), table.cuda()
@@ -325,9 +337,10 @@ def test_paged_cache_matches_oracle(block_size, dtype):
     assert cuda.read_status() == 0
 
 
-def test_paged_cache_block_out_of_pool_sets_status():
+@pytest.mark.parametrize("D", TC_DIMS)
+def test_paged_cache_block_out_of_pool_sets_status(D):
     from decode_llm_kernel_b200 import cuda
-    case = make_case(37, 3, 16, 4, 128, 256, torch.bfloat16, positions=[10, 200, 255])
+    case = make_case(37, 3, 16, 4, D, 256, torch.bfloat16, positions=[10, 200, 255])
     kp, vp, table = paged_from(case, 64, 38)
     table[int(case[8][1]), 3] = kp.shape[0] + 5        # the page holding token 1's position 200
     q, k, v, p, cos, sin, _, _, ri = [t.cuda() for t in case]
@@ -339,9 +352,9 @@ def test_paged_cache_block_out_of_pool_sets_status():
 
 
 def test_paged_cache_rejects_unsupported_shapes():
-    case = make_case(39, 2, 8, 2, 64, 128, torch.bfloat16)
+    case = make_case(39, 2, 8, 2, 96, 128, torch.bfloat16)
     kp, vp, table = paged_from(case, 16, 40)
-    with pytest.raises(RuntimeError, match="head_dim 128"):
+    with pytest.raises(RuntimeError, match="head_dim 64 or 128"):
         ops().paged_rope_kv_append_attention(*[t.cuda() for t in case[:6]], kp.cuda(), vp.cuda(),
                                              table.cuda(), case[8].cuda())
     case = make_case(41, 2, 8, 2, 128, 120, torch.bfloat16)
