@@ -157,7 +157,8 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp_in,
   static std::map<int, bool> opted_in;
   static std::map<std::pair<int, std::pair<size_t, int>>, int> occupancy;
   int per_sm = 0;
-  size_t smem = static_cast<size_t>(sp.stages) * (sp.stage_bytes + sizeof(uint64_t));
+  size_t smem =
+      static_cast<size_t>(sp.stages) * (sp.stage_bytes + sizeof(uint64_t)) + kStagedMetaBytes;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!opted_in[device]) {
@@ -192,7 +193,8 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp_in,
       const double per_cta =
           static_cast<double>(p.T) / (static_cast<double>(sm_count(device)) * per_sm);
       const size_t deeper =
-          static_cast<size_t>(sp.stages + 1) * (sp.stage_bytes + sizeof(uint64_t));
+          static_cast<size_t>(sp.stages + 1) * (sp.stage_bytes + sizeof(uint64_t)) +
+          kStagedMetaBytes;
       int per_sm_deeper = 0;
       if (per_cta >= 4.8 && deeper <= static_cast<size_t>(DRK_STAGED_SMEM_BUDGET) &&
           resident(deeper, &per_sm_deeper) == cudaSuccess && per_sm_deeper >= 1) {

@@ -80,10 +80,16 @@ cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits,
 struct StagedParams {
   uint32_t q_bytes;      // Hq * D * es: one token's Q rows
   uint32_t kv_bytes;     // Hkv * D * es: one token's K (or V) rows
-  uint32_t stage_bytes;  // q_bytes + 2 * kv_bytes, rounded up to 128
+  uint32_t tab_bytes;    // R / 2 * 4: one cos (or sin) row copied into the stage; 0: loaded
+                         // by the lanes instead (in-register trig, unaligned tables)
+  uint32_t stage_bytes;  // q_bytes + 2 * kv_bytes + 2 * tab_bytes, rounded up to 128
   int32_t stages;        // pipeline depth
   int32_t deepen;        // the launcher may add a stage when CTAs walk many tokens each
 };
+// Token metadata a CTA of the bulk-copy kernel keeps in shared memory: two blocks of 32 tokens
+// of 24 bytes (position, cache slot, status bits, flags), after the stages and their barriers.
+constexpr int kStagedMetaBlock = 32;
+constexpr size_t kStagedMetaBytes = 2 * kStagedMetaBlock * 24;
 
 // Fused mode only. shape.grid is ignored: the launcher sizes a persistent grid of
 // min(T, SMs x resident CTAs per SM).

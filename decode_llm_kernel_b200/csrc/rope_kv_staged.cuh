@@ -7,13 +7,14 @@
 //
 // Per CTA, a persistent loop over tokens t = blockIdx.x, blockIdx.x + gridDim.x, ... with a
 // kStages-deep pipeline in shared memory. Before griddepcontrol.wait (programmatic dependent
-// launch) a CTA resolves its first token's indices, slot and table slice and pulls its first
-// tokens' row blocks toward L2 (cp.async.bulk.prefetch.L2); after it:
+// launch) a CTA resolves the indices, bounds and cache slots of its first 64 tokens into
+// shared memory, all threads at once (later blocks of 32 the same way, a block ahead), and
+// pulls its first tokens' row blocks toward L2 (cp.async.bulk.prefetch.L2); after it:
 //   1. one thread issues cp.async.bulk global->shared copies of the token's Q, K and V row
-//      blocks, completing on the stage's mbarrier (expect_tx bytes);
-//   2. every thread waits on the stage's mbarrier (bounded: see below); the position, request
-//      index, slot and cos/sin slice of a token were fetched while earlier tokens were being
-//      processed (two tokens ahead for the indices, one for the rest);
+//      blocks and, when the table rows are 16-byte aligned, its cos and sin rows, all
+//      completing on the stage's mbarrier (expect_tx bytes) -- so no token waits on a load of
+//      its own index or table row (otherwise a lane's table slice is loaded a token ahead);
+//   2. every thread waits on the stage's mbarrier (bounded: see below);
 //   3. threads rotate only the rotary dims of the Q and K rows, in place in shared memory
 //      (lane j: elements [j*VEC, +VEC) and [R/2 + j*VEC, +VEC), the rotate_half pair), with
 //      the same per-element roundings as the register kernel (bit-exact to the oracle);
@@ -123,6 +124,15 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
 #endif
 }
 
+// bulk_load without an L2 hint: for rows that many tokens read (the cos/sin tables).
+__device__ __forceinline__ void bulk_load_keep(void* smem_dst, const void* gmem_src,
+                                               uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
 #if DRK_STAGED_L2_HINT & 2
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;"
@@ -171,6 +181,17 @@ __device__ __forceinline__ void sts(unsigned char* p, typename VecBits<VB>::type
   *reinterpret_cast<typename VecBits<VB>::type*>(p) = x;
 }
 
+// One token's metadata, resolved once for the CTA's walk (shared memory).
+struct StagedTokenMeta {
+  int64_t pos;
+  int64_t slot;       // element offset of the token's cache slot (valid when cache_ok)
+  uint32_t bad;       // DRK_STATUS bits this token reports
+  uint32_t ok;        // bit 0: table row in range; bit 1: cache slot in range
+};
+static_assert(2 * kStagedMetaBlock * sizeof(StagedTokenMeta) == kStagedMetaBytes,
+              "the launcher's shared-memory size for the metadata array");
+constexpr uint32_t kMetaTableOk = 1u, kMetaCacheOk = 2u;
+
 template <typename E, typename Idx, int VB, Cache C>
 __global__ void __launch_bounds__(kStagedThreads)
 rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
@@ -181,16 +202,65 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(sp.stages) *
                                                sp.stage_bytes);
+  StagedTokenMeta* meta = reinterpret_cast<StagedTokenMeta*>(bars + sp.stages);
   __shared__ int s_abort;
 
   pdl_launch_dependents();
 
   const int tid = static_cast<int>(threadIdx.x + threadIdx.y * blockDim.x);
+  const int nthreads = static_cast<int>(blockDim.x * blockDim.y);
   const int lane = static_cast<int>(threadIdx.x);   // < nrot
   const int grp = static_cast<int>(threadIdx.y);
   const int rot_rows = p.Hq + p.Hkv;
   const int64_t my_tokens = p.T > blockIdx.x ? (p.T - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int row_bytes = p.D * static_cast<int>(ES);
+  const uint32_t qkv_bytes = sp.q_bytes + 2 * sp.kv_bytes;
+
+  // Token j's metadata lives in block (j / kStagedMetaBlock) % 2 of the shared array. Every
+  // thread resolves some of a block's tokens at once (one round of dependent index -> slot /
+  // block-table loads for the whole block), so no token waits on its own index loads.
+  auto meta_at = [&](int64_t jj) {
+    return meta + ((jj / kStagedMetaBlock) & 1) * kStagedMetaBlock + jj % kStagedMetaBlock;
+  };
+  auto fill_meta = [&](int64_t j0) {
+    for (int i = tid; i < kStagedMetaBlock; i += nthreads) {
+      const int64_t jj = j0 + i;
+      if (jj >= my_tokens) break;
+      const int64_t t = blockIdx.x + jj * gridDim.x;
+      const int64_t pos = load_index<Idx>(p.positions, t);
+      const int64_t ri = load_index<Idx>(p.request_indices, t);
+      uint32_t bad = 0u;
+      int64_t slot = 0;
+      const bool table_ok = pos >= 0 && pos < p.table_rows;
+      if (!table_ok) bad |= kStatusPosTable;
+      const bool pos_ok = pos >= 0 && pos < p.S;
+      const bool ri_ok = ri >= 0 && ri < p.B;
+      if (!pos_ok) bad |= kStatusPosCache;
+      if (!ri_ok) bad |= kStatusRequest;
+      bool cache_ok = pos_ok && ri_ok;
+      if constexpr (C == Cache::kStrided) {
+        slot = ri * p.c_bs + pos * p.c_ss;
+      } else if (cache_ok) {
+        const int64_t blk_i = pos / p.block_size;
+        const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
+        if (blk < 0 || blk >= p.num_blocks) {
+          bad |= kStatusBlock;
+          cache_ok = false;
+        }
+        slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
+      }
+      // Warm the address translation of the token's cache slots before the bulk stores.
+      if (cache_ok) {
+        prefetch_l2(p.k_dst + slot * ES);
+        prefetch_l2(p.v_dst + slot * ES);
+      }
+      StagedTokenMeta* m = meta_at(jj);
+      m->pos = pos;
+      m->slot = slot;
+      m->bad = bad;
+      m->ok = (table_ok ? kMetaTableOk : 0u) | (cache_ok ? kMetaCacheOk : 0u);
+    }
+  };
 
   if (tid == 0) {
     for (int st = 0; st < sp.stages; ++st) mbar_init(&bars[st], 1);
@@ -205,11 +275,17 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
       bulk_prefetch_l2(p.v + t * p.v_ts * ES, sp.kv_bytes);
     }
   }
+  // Indices, bounds and slots of the first two blocks of tokens: they are never written by the
+  // preceding kernel, so they are resolved before waiting on it.
+  fill_meta(0);
+  if (my_tokens > kStagedMetaBlock) fill_meta(kStagedMetaBlock);
 
   const uint64_t wait_ns = p.wait_limit_ns > 0 ? static_cast<uint64_t>(p.wait_limit_ns)
                                                : DRK_WAIT_LIMIT_NS;
   int64_t issued = 0;   // tokens whose copies thread 0 has issued
   int64_t skipped = -1; // testing only: the token whose copies were not issued
+  // Thread 0: the token's Q, K and V row blocks and, when they travel with them, its cos and
+  // sin rows (tab_bytes each, after the rows) into its stage.
   auto issue_load = [&](int64_t j) {
     issued = j + 1;
     const int64_t t = blockIdx.x + j * gridDim.x;
@@ -219,96 +295,62 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     }
     const int st = static_cast<int>(j % sp.stages);
     unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
-    mbar_expect_tx(&bars[st], sp.q_bytes + 2 * sp.kv_bytes);
+    const StagedTokenMeta* m = meta_at(j);
+    const bool tab = sp.tab_bytes != 0 && (m->ok & kMetaTableOk);
+    mbar_expect_tx(&bars[st], qkv_bytes + (tab ? 2 * sp.tab_bytes : 0u));
     bulk_load(stage, p.q + t * p.q_ts * ES, sp.q_bytes, &bars[st]);
     bulk_load(stage + sp.q_bytes, p.k + t * p.k_ts * ES, sp.kv_bytes, &bars[st]);
     bulk_load(stage + sp.q_bytes + sp.kv_bytes, p.v + t * p.v_ts * ES, sp.kv_bytes, &bars[st]);
+    if (tab) {
+      // Table rows are read by many tokens: no evict-first hint.
+      const int64_t row = m->pos * p.table_stride;
+      bulk_load_keep(stage + qkv_bytes, p.cos_t + row, sp.tab_bytes, &bars[st]);
+      bulk_load_keep(stage + qkv_bytes + sp.tab_bytes, p.sin_t + row, sp.tab_bytes, &bars[st]);
+    }
   };
 
   const bool lane_rotates = lane < p.nrot;
   const int off1 = lane * VEC * static_cast<int>(ES);
   const int off2 = off1 + (p.R >> 1) * static_cast<int>(ES);
 
-  // Per-token metadata runs ahead of the data: the indices of token j+2 and the bounds, slot
-  // and table slice of token j+1 are fetched while token j is processed, so the dependent
-  // index -> table/slot loads never sit on a token's critical path.
-  struct Meta {
-    int64_t slot;
-    uint32_t bad;
-    bool table_ok, cache_ok;
-  };
-  auto fetch_index = [&](int64_t jj, int64_t& pos, int64_t& ri) {
-    const int64_t t = blockIdx.x + jj * gridDim.x;
-    pos = load_index<Idx>(p.positions, t);
-    ri = load_index<Idx>(p.request_indices, t);
-  };
-  auto resolve = [&](int64_t pos, int64_t ri, float* c, float* s) {
-    Meta m{0, 0u, false, false};
-    m.table_ok = pos >= 0 && pos < p.table_rows;
-    if (!m.table_ok) m.bad |= kStatusPosTable;
-    const bool pos_ok = pos >= 0 && pos < p.S;
-    const bool ri_ok = ri >= 0 && ri < p.B;
-    if (!pos_ok) m.bad |= kStatusPosCache;
-    if (!ri_ok) m.bad |= kStatusRequest;
-    m.cache_ok = pos_ok && ri_ok;
-    if constexpr (C == Cache::kStrided) {
-      m.slot = ri * p.c_bs + pos * p.c_ss;
-    } else if (m.cache_ok) {
-      const int64_t blk_i = pos / p.block_size;
-      const int64_t blk = load_index<Idx>(p.block_table, ri * p.bt_stride + blk_i);
-      if (blk < 0 || blk >= p.num_blocks) {
-        m.bad |= kStatusBlock;
-        m.cache_ok = false;
+  // This lane's cos/sin slice of token jj when the tables do not travel in the stage: computed
+  // in registers (in-register trig) or loaded a token ahead of its use.
+  auto table_slice = [&](int64_t jj, float* c, float* s) {
+    const StagedTokenMeta* m = meta_at(jj);
+    if (!lane_rotates || !(m->ok & kMetaTableOk)) return;
+    const int64_t pos = m->pos;
+    if (p.inreg_trig) {
+      const float pf = static_cast<float>(pos);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + e));
+        sincosf(ang, &s[e], &c[e]);
       }
-      m.slot = blk * p.c_bs + (pos - blk_i * p.block_size) * p.c_ss;
+      return;
     }
-    // Warm the address translation of the token's cache slots before the bulk stores.
-    if (m.cache_ok && tid == 0) {
-      prefetch_l2(p.k_dst + m.slot * ES);
-      prefetch_l2(p.v_dst + m.slot * ES);
-    }
-    if (lane_rotates && m.table_ok) {
-      if (p.inreg_trig) {
-        const float pf = static_cast<float>(pos);
+    const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
+    const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
+    bool vec4 = false;
+    if constexpr (VEC % 4 == 0) vec4 = p.table_vec4 != 0;
+    if (vec4) {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float ang = __fmul_rn(pf, __ldg(p.inv_freq + lane * VEC + e));
-          sincosf(ang, &s[e], &c[e]);
-        }
-      } else {
-        const float* crow = p.cos_t + pos * p.table_stride + lane * VEC;
-        const float* srow = p.sin_t + pos * p.table_stride + lane * VEC;
-        bool vec4 = false;
-        if constexpr (VEC % 4 == 0) vec4 = p.table_vec4 != 0;
-        if (vec4) {
-#pragma unroll
-          for (int e = 0; e < VEC; e += 4) {
-            const float4 cv = __ldg(reinterpret_cast<const float4*>(crow + e));
-            const float4 sv = __ldg(reinterpret_cast<const float4*>(srow + e));
-            c[e] = cv.x; c[e + 1] = cv.y; c[e + 2] = cv.z; c[e + 3] = cv.w;
-            s[e] = sv.x; s[e + 1] = sv.y; s[e + 2] = sv.z; s[e + 3] = sv.w;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) { c[e] = __ldg(crow + e); s[e] = __ldg(srow + e); }
-        }
+      for (int e = 0; e < VEC; e += 4) {
+        const float4 cv = __ldg(reinterpret_cast<const float4*>(crow + e));
+        const float4 sv = __ldg(reinterpret_cast<const float4*>(srow + e));
+        c[e] = cv.x; c[e + 1] = cv.y; c[e + 2] = cv.z; c[e + 3] = cv.w;
+        s[e] = sv.x; s[e + 1] = sv.y; s[e + 2] = sv.z; s[e + 3] = sv.w;
       }
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) { c[e] = __ldg(crow + e); s[e] = __ldg(srow + e); }
     }
-    return m;
   };
 
-  // Indices, bounds, slot and table slice of the first tokens: they are never written by the
-  // preceding kernel, so they are resolved before waiting on it.
   float c_cur[VEC], s_cur[VEC];
-  int64_t pos_next = 0, ri_next = 0;
-  Meta cur{0, 0u, false, false};
-  if (my_tokens > 0) {
-    int64_t pos0, ri0;
-    fetch_index(0, pos0, ri0);
-    if (my_tokens > 1) fetch_index(1, pos_next, ri_next);
-    cur = resolve(pos0, ri0, c_cur, s_cur);
-  }
-  __syncthreads();   // the barriers are initialised
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) c_cur[e] = s_cur[e] = 0.f;
+  __syncthreads();   // the barriers are initialised and the first blocks' metadata written
+  if (sp.tab_bytes == 0 && my_tokens > 0) table_slice(0, c_cur, s_cur);
   pdl_wait();        // q/k/v may be written by the preceding kernel
   if (tid == 0) {
     for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) issue_load(j);
@@ -321,12 +363,21 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     const uint32_t parity = static_cast<uint32_t>((j / sp.stages) & 1);
     unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
 
-    // Metadata of the next tokens, in flight while this one is processed.
-    int64_t pos_after = 0, ri_after = 0;
-    if (j + 2 < my_tokens) fetch_index(j + 2, pos_after, ri_after);
+    // Every block of metadata but the first two is resolved as the walk enters the block
+    // before it (into the array's other half, whose tokens are done): the loads of a whole
+    // block share one round trip, and the barriers below order them before their readers
+    // (the earliest, a refill, comes kStagedMetaBlock - stages + 1 tokens later).
+    if (j >= kStagedMetaBlock && j % kStagedMetaBlock == 0 && j + kStagedMetaBlock < my_tokens)
+      fill_meta(j + kStagedMetaBlock);
+    const StagedTokenMeta* curp = meta_at(j);
+    const uint32_t cur_ok = curp->ok, cur_bad = curp->bad;
+    const int64_t cur_slot = curp->slot;
+    const bool table_ok = (cur_ok & kMetaTableOk) != 0;
+    // The next token's table slice, in flight while this one is processed.
     float c_nxt[VEC], s_nxt[VEC];
-    Meta nxt{0, 0u, false, false};
-    if (j + 1 < my_tokens) nxt = resolve(pos_next, ri_next, c_nxt, s_nxt);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) c_nxt[e] = s_nxt[e] = 0.f;
+    if (sp.tab_bytes == 0 && j + 1 < my_tokens) table_slice(j + 1, c_nxt, s_nxt);
 
     if (!mbar_wait(&bars[st], parity, wait_ns)) {
       atomicOr(&s_abort, 1);
@@ -335,7 +386,16 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     if (s_abort) break;
 
     // Rotate the rotary dims of the Q and K rows in place.
-    if (lane_rotates && cur.table_ok) {
+    if (lane_rotates && table_ok) {
+      if (sp.tab_bytes != 0) {
+        const float* cs = reinterpret_cast<const float*>(stage + qkv_bytes) + lane * VEC;
+        const float* sn = cs + (sp.tab_bytes >> 2);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          c_cur[e] = cs[e];
+          s_cur[e] = sn[e];
+        }
+      }
       for (int r = grp; r < rot_rows; r += blockDim.y) {
         unsigned char* row = stage + static_cast<size_t>(r) * row_bytes;
         Pack<E, VB> x1, x2;
@@ -350,12 +410,12 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     __syncthreads();
 
     if (tid == 0) {
-      if (cur.bad && p.status != nullptr) atomicOr(p.status, cur.bad);
-      if (cur.table_ok)
+      if (cur_bad && p.status != nullptr) atomicOr(p.status, cur_bad);
+      if (table_ok)
         bulk_store(p.q_out + t * static_cast<int64_t>(sp.q_bytes), stage, sp.q_bytes);
-      if (cur.cache_ok) {
-        if (cur.table_ok) bulk_store(p.k_dst + cur.slot * ES, stage + sp.q_bytes, sp.kv_bytes);
-        bulk_store(p.v_dst + cur.slot * ES, stage + sp.q_bytes + sp.kv_bytes, sp.kv_bytes);
+      if (cur_ok & kMetaCacheOk) {
+        if (table_ok) bulk_store(p.k_dst + cur_slot * ES, stage + sp.q_bytes, sp.kv_bytes);
+        bulk_store(p.v_dst + cur_slot * ES, stage + sp.q_bytes + sp.kv_bytes, sp.kv_bytes);
       }
       bulk_commit();
       // Refill the stage read by the previous token's stores once they have read it.
@@ -365,14 +425,13 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
       }
     }
 
-    cur = nxt;
+    if (sp.tab_bytes == 0) {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      c_cur[e] = c_nxt[e];
-      s_cur[e] = s_nxt[e];
+      for (int e = 0; e < VEC; ++e) {
+        c_cur[e] = c_nxt[e];
+        s_cur[e] = s_nxt[e];
+      }
     }
-    pos_next = pos_after;
-    ri_next = ri_after;
   }
 
   if (tid == 0) {

@@ -549,6 +549,50 @@ def test_staged_kernel_token_counts_and_partial_rotary(T):
     assert bits_equal(a.v_cache.cpu(), ref[7])
 
 
+@pytest.mark.parametrize("rotary_dim", [8, 4])
+def test_staged_kernel_walks_many_metadata_blocks(rotary_dim):
+    """One head of 8 fp16 dims per token: small rows give a grid of thousands of CTAs, and
+    160,000 tokens make each CTA walk ~60-70 of them, so the shared metadata array (two blocks
+    of 32 tokens) is refilled during the walk. rotary_dim 8: the cos/sin rows (16 bytes)
+    travel in the stage with the token's rows; rotary_dim 4 (8-byte rows): the lanes load
+    them a token ahead."""
+    T, S = 160_000, 4
+    cfg = case("tiny", 1, 1, 8, T, S, "fp16", pos.RAGGED, rotary_dim=rotary_dim,
+               request_order="shuffled")
+    p = pos.build_position_sets(T, S, pos.RAGGED, SEED, 1, "cuda")[0]
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
+    ref = _oracle_args(a)
+    q_ref = oracle.fused_rope_kv_append(*ref)
+    extra = {} if rotary_dim == 8 else {"rotary_dim": rotary_dim}
+    q = ops().fused_rope_kv_append_ex(*a, path="staged", **extra)
+    assert bits_equal(q.cpu(), q_ref)
+    assert bits_equal(a.k_cache.cpu(), ref[6])
+    assert bits_equal(a.v_cache.cpu(), ref[7])
+
+
+def test_staged_kernel_paged_cache_many_metadata_blocks():
+    """The block-table lookups of later metadata blocks (160,000 tokens, pages of 2 rows)."""
+    T, S, bs = 160_000, 4, 2
+    cfg = case("tiny", 1, 1, 8, T, S, "fp16", pos.RAGGED, request_order="shuffled")
+    p = pos.build_position_sets(T, S, pos.RAGGED, SEED, 1, "cuda")[0]
+    a = make_inputs(cfg, "cuda", SEED, p, cache_fill=SENTINEL)
+    max_blocks = S // bs
+    num_blocks = T * max_blocks + 5
+    perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(4))[
+        : T * max_blocks].view(T, max_blocks).to(a.positions.dtype)
+    k_pages = torch.full((num_blocks, bs, 1, 8), 7.5, dtype=torch.float16, device="cuda")
+    v_pages = torch.full_like(k_pages, 7.5)
+    q = ops().paged_rope_kv_append(a.q, a.k, a.v, a.positions, a.cos, a.sin, k_pages, v_pages,
+                                   perm.cuda(), a.request_indices, path="staged")
+    ref = _oracle_args(a)
+    q_ref = oracle.fused_rope_kv_append(*ref)
+    assert bits_equal(q.cpu(), q_ref)
+    ri, pp = a.request_indices.long().cpu(), a.positions.long().cpu()
+    blk, row = perm.long()[ri, pp // bs], pp % bs
+    assert bits_equal(k_pages.cpu()[blk, row], ref[6][ri, pp])
+    assert bits_equal(v_pages.cpu()[blk, row], ref[7][ri, pp])
+
+
 def test_staged_kernel_paged_cache():
     T, Hq, Hkv, D, S, bs = 400, 32, 8, 128, 256, 16
     cfg = case("gqa", Hq, Hkv, D, T, S, "bf16", pos.RAGGED, request_order="shuffled")
