@@ -51,7 +51,7 @@ from decode_llm_kernel_b200.harness.configs import WORKLOADS, make_positions  # 
 FALLBACK_HBM_GBS = 6650.0
 # ncu captures (profiles/): DRAM bytes read + written per launch
 DECODE32_NCU_DRAM_BYTES = 878848 + 0
-MISTRAL_NCU_DRAM_BYTES = 51449088 + 5161984
+MISTRAL_NCU_DRAM_BYTES = 51543296 + 4917504
 E2E_STEPS_PER_GRAPH = 32
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "achieved HBM GB/s per decode step (algorithmic bytes / device time), with us/call"
@@ -477,7 +477,7 @@ def single_layer_probe(name, world, rank, device, seed, peak, cache_len=0, iters
         out["traffic"] = MISTRAL_NCU_DRAM_BYTES
         out["traffic_note"] = ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
                                "profiles/rope_kv_staged_kernel_mistral_b4096_fp16.md (caches cut "
-                               "to 128 positions): reads 51.4 MB = the algorithmic reads; 5.2 MB "
+                               "to 128 positions): reads 51.5 MB = the algorithmic reads; 4.9 MB "
                                "of the 51.4 MB of writes reach DRAM within the launch, the rest "
                                "drains from L2 afterwards")
     del kc, vc, sets
