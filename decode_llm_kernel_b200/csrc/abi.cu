@@ -319,8 +319,7 @@ struct StagedPlan {
 StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
                        const drk_tensor* q_out, const drk_tensor* k_cache,
                        const drk_tensor* v_cache, int64_t T, int64_t Hq, int64_t Hkv,
-                       int64_t D, int64_t R, int64_t es, int64_t tab_bytes,
-                       int32_t stages_hint = 0) {
+                       int64_t D, int64_t R, int64_t es, int32_t stages_hint = 0) {
   StagedPlan pl;
   auto fail = [&](const char* why) {
     pl.why = why;
@@ -357,7 +356,7 @@ StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tenso
   const int64_t rot_rows = Hq + Hkv;
   pl.groups = static_cast<int>(std::max<int64_t>(
       1, std::min<int64_t>(rot_rows, drk::kStagedThreadsPerBlock / pl.nrot)));
-  const int64_t stage = (q_bytes + 2 * kv_bytes + 2 * tab_bytes + 127) / 128 * 128;
+  const int64_t stage = (q_bytes + 2 * kv_bytes + 127) / 128 * 128;
   if (stages_hint < 0 || stages_hint == 1 || stages_hint > 8)
     invalid("staged_stages must be 0 (chosen by the library) or in [2, 8], got ", stages_hint);
   int stages = static_cast<int>(std::min<int64_t>(stages_hint ? stages_hint : DRK_STAGED_STAGES,
@@ -368,7 +367,6 @@ StagedPlan plan_staged(const drk_tensor* q, const drk_tensor* k, const drk_tenso
   }
   pl.sp.q_bytes = static_cast<uint32_t>(q_bytes);
   pl.sp.kv_bytes = static_cast<uint32_t>(kv_bytes);
-  pl.sp.tab_bytes = static_cast<uint32_t>(tab_bytes);
   pl.sp.stage_bytes = static_cast<uint32_t>(stage);
   pl.sp.stages = stages;
   pl.sp.deepen = stages_hint == 0 ? 1 : 0;
@@ -546,12 +544,8 @@ void fused_impl(const drk_tensor* q, const drk_tensor* k, const drk_tensor* v,
   if (force_staged && force_register)
     invalid("DRK_FLAG_FORCE_STAGED_PATH and DRK_FLAG_FORCE_REGISTER_PATH are exclusive");
   if (!force_register && (force_staged || T >= DRK_STAGED_MIN_TOKENS)) {
-    // A token's cos and sin rows travel with its Q/K/V rows when a bulk copy can take them:
-    // 16-byte aligned rows (table_vec4) whose length R / 2 * 4 bytes is a multiple of 16.
-    const int64_t tab_bytes =
-        (!p.inreg_trig && p.table_vec4 && (R / 2 * 4) % 16 == 0) ? R / 2 * 4 : 0;
     const StagedPlan pl = plan_staged(q, k, v, q_out, k_cache, v_cache, T, Hq, Hkv, D, R, es,
-                                      tab_bytes, o.staged_stages);
+                                      o.staged_stages);
     if (pl.ok) {
       p.nrot = pl.nrot;
       p.G = pl.groups;

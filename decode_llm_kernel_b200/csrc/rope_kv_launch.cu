@@ -206,6 +206,7 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp_in,
   }
   const int64_t slots = static_cast<int64_t>(sm_count(device)) * per_sm;
   const int grid = static_cast<int>(p.T < slots ? p.T : slots);
+  sp.early_issue = shape.pdl ? 0 : 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(shape.lanes, shape.groups, 1);

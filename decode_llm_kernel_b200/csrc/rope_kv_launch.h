@@ -80,11 +80,11 @@ cudaError_t launch_rope_kv(const KernelParams& p, int elem_code, int index_bits,
 struct StagedParams {
   uint32_t q_bytes;      // Hq * D * es: one token's Q rows
   uint32_t kv_bytes;     // Hkv * D * es: one token's K (or V) rows
-  uint32_t tab_bytes;    // R / 2 * 4: one cos (or sin) row copied into the stage; 0: loaded
-                         // by the lanes instead (in-register trig, unaligned tables)
-  uint32_t stage_bytes;  // q_bytes + 2 * kv_bytes + 2 * tab_bytes, rounded up to 128
+  uint32_t stage_bytes;  // q_bytes + 2 * kv_bytes, rounded up to 128
   int32_t stages;        // pipeline depth
   int32_t deepen;        // the launcher may add a stage when CTAs walk many tokens each
+  int32_t early_issue;   // set by the launcher for launches without programmatic dependent
+                         // launch: the first copies go out during the metadata round trip
 };
 // Token metadata a CTA of the bulk-copy kernel keeps in shared memory: two blocks of 32 tokens
 // of 24 bytes (position, cache slot, status bits, flags), after the stages and their barriers.

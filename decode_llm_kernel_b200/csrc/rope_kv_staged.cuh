@@ -7,13 +7,14 @@
 //
 // Per CTA, a persistent loop over tokens t = blockIdx.x, blockIdx.x + gridDim.x, ... with a
 // kStages-deep pipeline in shared memory. Before griddepcontrol.wait (programmatic dependent
-// launch) a CTA resolves the indices, bounds and cache slots of its first 64 tokens into
-// shared memory, all threads at once (later blocks of 32 the same way, a block ahead), and
-// pulls its first tokens' row blocks toward L2 (cp.async.bulk.prefetch.L2); after it:
+// launch) a CTA pulls its first tokens' row blocks toward L2 (cp.async.bulk.prefetch.L2) and
+// resolves the positions, request indices, bounds and cache slots of its first 64 tokens into
+// shared memory, many threads at once (later blocks of 32 the same way, a block ahead), so no
+// token waits on a load of its own index; launched without PDL, its first thread issues the
+// first stage-full of copies during that round trip. Then:
 //   1. one thread issues cp.async.bulk global->shared copies of the token's Q, K and V row
-//      blocks and, when the table rows are 16-byte aligned, its cos and sin rows, all
-//      completing on the stage's mbarrier (expect_tx bytes) -- so no token waits on a load of
-//      its own index or table row (otherwise a lane's table slice is loaded a token ahead);
+//      blocks, completing on the stage's mbarrier (expect_tx bytes); the lanes load their
+//      cos/sin slice of the token a token ahead, from the position in shared memory;
 //   2. every thread waits on the stage's mbarrier (bounded: see below);
 //   3. threads rotate only the rotary dims of the Q and K rows, in place in shared memory
 //      (lane j: elements [j*VEC, +VEC) and [R/2 + j*VEC, +VEC), the rotate_half pair), with
@@ -124,15 +125,6 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
 #endif
 }
 
-// bulk_load without an L2 hint: for rows that many tokens read (the cos/sin tables).
-__device__ __forceinline__ void bulk_load_keep(void* smem_dst, const void* gmem_src,
-                                               uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
 #if DRK_STAGED_L2_HINT & 2
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;"
@@ -214,16 +206,16 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
   const int rot_rows = p.Hq + p.Hkv;
   const int64_t my_tokens = p.T > blockIdx.x ? (p.T - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int row_bytes = p.D * static_cast<int>(ES);
-  const uint32_t qkv_bytes = sp.q_bytes + 2 * sp.kv_bytes;
 
-  // Token j's metadata lives in block (j / kStagedMetaBlock) % 2 of the shared array. Every
-  // thread resolves some of a block's tokens at once (one round of dependent index -> slot /
+  // Token j's metadata lives in block (j / kStagedMetaBlock) % 2 of the shared array. Threads
+  // first.. resolve a block's tokens at once (one round of dependent index -> slot /
   // block-table loads for the whole block), so no token waits on its own index loads.
   auto meta_at = [&](int64_t jj) {
     return meta + ((jj / kStagedMetaBlock) & 1) * kStagedMetaBlock + jj % kStagedMetaBlock;
   };
-  auto fill_meta = [&](int64_t j0) {
-    for (int i = tid; i < kStagedMetaBlock; i += nthreads) {
+  auto fill_meta = [&](int64_t j0, int first) {
+    if (tid < first) return;
+    for (int i = tid - first; i < kStagedMetaBlock; i += nthreads - first) {
       const int64_t jj = j0 + i;
       if (jj >= my_tokens) break;
       const int64_t t = blockIdx.x + jj * gridDim.x;
@@ -262,6 +254,35 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     }
   };
 
+  const uint64_t wait_ns = p.wait_limit_ns > 0 ? static_cast<uint64_t>(p.wait_limit_ns)
+                                               : DRK_WAIT_LIMIT_NS;
+  int64_t issued = 0;   // tokens whose copies thread 0 has issued
+  int64_t skipped = -1; // testing only: the token whose copies were not issued
+  // Thread 0: the token's Q, K and V row blocks into its stage (no metadata needed).
+  auto issue_load = [&](int64_t j) {
+    issued = j + 1;
+    const int64_t t = blockIdx.x + j * gridDim.x;
+    if (t == p.test_skip_token) {
+      skipped = j;        // nothing in flight for it: its stage's wait runs out
+      return;
+    }
+    const int st = static_cast<int>(j % sp.stages);
+    unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
+    mbar_expect_tx(&bars[st], sp.q_bytes + 2 * sp.kv_bytes);
+    bulk_load(stage, p.q + t * p.q_ts * ES, sp.q_bytes, &bars[st]);
+    bulk_load(stage + sp.q_bytes, p.k + t * p.k_ts * ES, sp.kv_bytes, &bars[st]);
+    bulk_load(stage + sp.q_bytes + sp.kv_bytes, p.v + t * p.v_ts * ES, sp.kv_bytes, &bars[st]);
+  };
+
+  // The first two blocks' metadata is never written by the preceding kernel, so it is
+  // resolved before waiting on it. Launched as a programmatic dependent, every thread resolves
+  // it while the preceding kernel finishes, and thread 0 issues the first copies after the
+  // wait. Launched plainly (early_issue), nothing hides that round trip, so thread 0 issues the
+  // first stage-full of copies at once while the threads of the other warps resolve the
+  // metadata (not warp 0's: its lanes would run their loads only after thread 0's path).
+  // Measured on B200 (Mistral-shaped rows, 4096 tokens): either order alone costs 1.4-1.5 us
+  // in the other regime. A CTA of fewer than 64 threads always resolves first.
+  const int meta_first = (sp.early_issue && nthreads >= 64) ? 32 : 0;
   if (tid == 0) {
     for (int st = 0; st < sp.stages; ++st) mbar_init(&bars[st], 1);
     fence_mbar_init();
@@ -274,47 +295,20 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
       bulk_prefetch_l2(p.k + t * p.k_ts * ES, sp.kv_bytes);
       bulk_prefetch_l2(p.v + t * p.v_ts * ES, sp.kv_bytes);
     }
+    if (meta_first != 0) {
+      pdl_wait();    // q/k/v may be written by the preceding kernel
+      for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) issue_load(j);
+    }
   }
-  // Indices, bounds and slots of the first two blocks of tokens: they are never written by the
-  // preceding kernel, so they are resolved before waiting on it.
-  fill_meta(0);
-  if (my_tokens > kStagedMetaBlock) fill_meta(kStagedMetaBlock);
-
-  const uint64_t wait_ns = p.wait_limit_ns > 0 ? static_cast<uint64_t>(p.wait_limit_ns)
-                                               : DRK_WAIT_LIMIT_NS;
-  int64_t issued = 0;   // tokens whose copies thread 0 has issued
-  int64_t skipped = -1; // testing only: the token whose copies were not issued
-  // Thread 0: the token's Q, K and V row blocks and, when they travel with them, its cos and
-  // sin rows (tab_bytes each, after the rows) into its stage.
-  auto issue_load = [&](int64_t j) {
-    issued = j + 1;
-    const int64_t t = blockIdx.x + j * gridDim.x;
-    if (t == p.test_skip_token) {
-      skipped = j;        // nothing in flight for it: its stage's wait runs out
-      return;
-    }
-    const int st = static_cast<int>(j % sp.stages);
-    unsigned char* stage = smem + static_cast<size_t>(st) * sp.stage_bytes;
-    const StagedTokenMeta* m = meta_at(j);
-    const bool tab = sp.tab_bytes != 0 && (m->ok & kMetaTableOk);
-    mbar_expect_tx(&bars[st], qkv_bytes + (tab ? 2 * sp.tab_bytes : 0u));
-    bulk_load(stage, p.q + t * p.q_ts * ES, sp.q_bytes, &bars[st]);
-    bulk_load(stage + sp.q_bytes, p.k + t * p.k_ts * ES, sp.kv_bytes, &bars[st]);
-    bulk_load(stage + sp.q_bytes + sp.kv_bytes, p.v + t * p.v_ts * ES, sp.kv_bytes, &bars[st]);
-    if (tab) {
-      // Table rows are read by many tokens: no evict-first hint.
-      const int64_t row = m->pos * p.table_stride;
-      bulk_load_keep(stage + qkv_bytes, p.cos_t + row, sp.tab_bytes, &bars[st]);
-      bulk_load_keep(stage + qkv_bytes + sp.tab_bytes, p.sin_t + row, sp.tab_bytes, &bars[st]);
-    }
-  };
+  fill_meta(0, meta_first);
+  if (my_tokens > kStagedMetaBlock) fill_meta(kStagedMetaBlock, meta_first);
 
   const bool lane_rotates = lane < p.nrot;
   const int off1 = lane * VEC * static_cast<int>(ES);
   const int off2 = off1 + (p.R >> 1) * static_cast<int>(ES);
 
-  // This lane's cos/sin slice of token jj when the tables do not travel in the stage: computed
-  // in registers (in-register trig) or loaded a token ahead of its use.
+  // This lane's cos/sin slice of token jj: computed in registers (in-register trig) or loaded
+  // a token ahead of its use.
   auto table_slice = [&](int64_t jj, float* c, float* s) {
     const StagedTokenMeta* m = meta_at(jj);
     if (!lane_rotates || !(m->ok & kMetaTableOk)) return;
@@ -350,9 +344,9 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
 #pragma unroll
   for (int e = 0; e < VEC; ++e) c_cur[e] = s_cur[e] = 0.f;
   __syncthreads();   // the barriers are initialised and the first blocks' metadata written
-  if (sp.tab_bytes == 0 && my_tokens > 0) table_slice(0, c_cur, s_cur);
+  if (my_tokens > 0) table_slice(0, c_cur, s_cur);
   pdl_wait();        // q/k/v may be written by the preceding kernel
-  if (tid == 0) {
+  if (tid == 0 && meta_first == 0) {
     for (int64_t j = 0; j < my_tokens && j < sp.stages; ++j) issue_load(j);
   }
 
@@ -365,10 +359,10 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
 
     // Every block of metadata but the first two is resolved as the walk enters the block
     // before it (into the array's other half, whose tokens are done): the loads of a whole
-    // block share one round trip, and the barriers below order them before their readers
-    // (the earliest, a refill, comes kStagedMetaBlock - stages + 1 tokens later).
+    // block share one round trip, and the barriers below order them before their first reader
+    // (the next token's table slice, kStagedMetaBlock - 1 tokens later).
     if (j >= kStagedMetaBlock && j % kStagedMetaBlock == 0 && j + kStagedMetaBlock < my_tokens)
-      fill_meta(j + kStagedMetaBlock);
+      fill_meta(j + kStagedMetaBlock, 0);
     const StagedTokenMeta* curp = meta_at(j);
     const uint32_t cur_ok = curp->ok, cur_bad = curp->bad;
     const int64_t cur_slot = curp->slot;
@@ -377,7 +371,7 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
     float c_nxt[VEC], s_nxt[VEC];
 #pragma unroll
     for (int e = 0; e < VEC; ++e) c_nxt[e] = s_nxt[e] = 0.f;
-    if (sp.tab_bytes == 0 && j + 1 < my_tokens) table_slice(j + 1, c_nxt, s_nxt);
+    if (j + 1 < my_tokens) table_slice(j + 1, c_nxt, s_nxt);
 
     if (!mbar_wait(&bars[st], parity, wait_ns)) {
       atomicOr(&s_abort, 1);
@@ -387,15 +381,6 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
 
     // Rotate the rotary dims of the Q and K rows in place.
     if (lane_rotates && table_ok) {
-      if (sp.tab_bytes != 0) {
-        const float* cs = reinterpret_cast<const float*>(stage + qkv_bytes) + lane * VEC;
-        const float* sn = cs + (sp.tab_bytes >> 2);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          c_cur[e] = cs[e];
-          s_cur[e] = sn[e];
-        }
-      }
       for (int r = grp; r < rot_rows; r += blockDim.y) {
         unsigned char* row = stage + static_cast<size_t>(r) * row_bytes;
         Pack<E, VB> x1, x2;
@@ -425,12 +410,10 @@ rope_kv_staged_kernel(const __grid_constant__ KernelParams p,
       }
     }
 
-    if (sp.tab_bytes == 0) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        c_cur[e] = c_nxt[e];
-        s_cur[e] = s_nxt[e];
-      }
+    for (int e = 0; e < VEC; ++e) {
+      c_cur[e] = c_nxt[e];
+      s_cur[e] = s_nxt[e];
     }
   }
 
