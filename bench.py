@@ -51,7 +51,7 @@ from decode_llm_kernel_b200.harness.configs import WORKLOADS, make_positions  # 
 FALLBACK_HBM_GBS = 6650.0
 # ncu captures (profiles/): DRAM bytes read + written per launch
 DECODE32_NCU_DRAM_BYTES = 878848 + 0
-MISTRAL_NCU_DRAM_BYTES = 51543296 + 4917504
+MISTRAL_NCU_DRAM_BYTES = 51549696 + 4873728
 E2E_STEPS_PER_GRAPH = 32
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "achieved HBM GB/s per decode step (algorithmic bytes / device time), with us/call"
