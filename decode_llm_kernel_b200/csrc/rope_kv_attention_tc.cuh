@@ -437,6 +437,57 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
     const int64_t ws_head = static_cast<int64_t>(a.max_chunks) * row;
     raw* out = reinterpret_cast<raw*>(a.attn_out) + (w.t * p.Hq + h0) * int64_t{DIM};
     constexpr int kPerLane = DIM / 32;   // dims lane + 32 i
+    if (h_step == 1 && nchunks <= 32) {
+      // One warp, up to 8 heads at a time, with every head's loads in flight together: the
+      // (m, l) of chunk `lane` of each head, then chunk by chunk the partial rows of all the
+      // heads. The same arithmetic, in the same order per head, as the loop below (whose first
+      // pass starts from m = -inf, a rescale of 0).
+      constexpr int kG = HR < 8 ? HR : 8;
+      for (int hb = 0; hb < nh; hb += kG) {
+        float mc[kG], lc[kG], wc[kG], Ls[kG], O[kG][kPerLane];
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          const bool on = hb + g < nh && lane < nchunks;
+          const float* hw = ws + (hb + g) * ws_head + static_cast<int64_t>(lane) * row;
+          mc[g] = on ? __ldcg(hw + DIM) : -INFINITY;
+          lc[g] = on ? __ldcg(hw + DIM + 1) : 0.f;
+        }
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          float mg = mc[g];
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1)
+            mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+          wc[g] = (hb + g < nh && lane < nchunks) ? exp2f(mc[g] - mg) : 0.f;
+          float lg = lc[g] * wc[g];
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
+          Ls[g] = lg;
+#pragma unroll
+          for (int i = 0; i < kPerLane; ++i) O[g][i] = 0.f;
+        }
+#pragma unroll 2
+        for (int j = 0; j < nchunks; ++j) {
+#pragma unroll
+          for (int g = 0; g < kG; ++g) {
+            const float wj = __shfl_sync(0xffffffffu, wc[g], j);
+            if (hb + g < nh) {
+              const float* cp = ws + (hb + g) * ws_head + static_cast<int64_t>(j) * row + lane;
+#pragma unroll
+              for (int i = 0; i < kPerLane; ++i) O[g][i] = fmaf(__ldcg(cp + 32 * i), wj, O[g][i]);
+            }
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < kG; ++g)
+          if (hb + g < nh)
+#pragma unroll
+            for (int i = 0; i < kPerLane; ++i)
+              out[(hb + g) * int64_t{DIM} + lane + 32 * i] = E::from_f(O[g][i] / Ls[g]);
+      }
+      if (lane == 0 && h_first == 0) a.counters[(w.t * p.Hkv + w.g) * a.nhb + w.hb] = 0;
+      return;
+    }
     for (int h = h_first; h < nh; h += h_step) {
       const float* hw = ws + h * ws_head;
       float M = -INFINITY, Ls = 0.f, O[kPerLane];
