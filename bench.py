@@ -511,7 +511,8 @@ def reference_gpu(device, seed, peak, ours):
         mine = ours.get(name)
         if mine and "cuda_fused" in row:
             row["ours_us"] = mine["us_per_launch"]
-            row["speedup_vs_reference_fused"] = row["cuda_fused"]["us_per_launch"] / mine["us_per_launch"]
+            row["speedup_vs_reference_fused"] = (row["cuda_fused"]["us_per_launch"]
+                                                 / mine["us_per_launch"])
             row["speedup_vs_reference_separate"] = (row["cuda_separate"]["us_per_launch"]
                                                     / mine["us_per_launch"])
         out[name] = row
@@ -1191,7 +1192,8 @@ def launch_floor(stream, layers, copy_bytes=0, copy_threads=192, sets=10):
             g.replay()
         end.record(stream)
         torch.cuda.synchronize()
-        out[f"graph_us_per_node{'_pdl' if pdl else ''}"] = start.elapsed_time(end) * 1e3 / (500 * layers)
+        key = f"graph_us_per_node{'_pdl' if pdl else ''}"
+        out[key] = start.elapsed_time(end) * 1e3 / (500 * layers)
     if copy_bytes:
         out.update(copy_floor(ext, stream, layers, copy_bytes, copy_threads, sets))
     return out

@@ -225,7 +225,8 @@ cudaError_t launch_staged_one(const KernelParams& p, const StagedParams& sp_in,
 template <typename E, typename Idx, int VB>
 cudaError_t launch_staged_cache(const KernelParams& p, const StagedParams& sp, int cache,
                                 const LaunchShape& shape, cudaStream_t stream) {
-  if (cache == kCachePaged) return launch_staged_one<E, Idx, VB, Cache::kPaged>(p, sp, shape, stream);
+  if (cache == kCachePaged)
+    return launch_staged_one<E, Idx, VB, Cache::kPaged>(p, sp, shape, stream);
   return launch_staged_one<E, Idx, VB, Cache::kStrided>(p, sp, shape, stream);
 }
 
