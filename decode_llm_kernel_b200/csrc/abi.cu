@@ -299,8 +299,9 @@ Shape plan(const Aligner& al, int nrows, bool rotates, int64_t tokens, int32_t s
 // The bulk-copy kernel's plan: eligible only if every row block it copies is one contiguous,
 // 16-byte-aligned run. It takes calls of DRK_STAGED_MIN_TOKENS tokens and up; measured on B200
 // (Mistral-shaped rows, fp16, graph-replayed launches with programmatic dependent launch), the
-// register kernel is faster at 512 tokens (3.04 against 3.78 us) and the bulk-copy kernel from
-// 768 (4.51 against 4.93 us; 1024: 5.89 against 6.09; 4096: 18.9 against 22.1 us).
+// register kernel is faster at 512 tokens (2.96 against 3.84 us at the best depth) and the
+// bulk-copy kernel from 768 (4.70-4.80 against 4.96 us; 2048: 10.0 against 11.1; 4096: 17.7
+// against 21.1 us).
 #ifndef DRK_STAGED_MIN_TOKENS
 #define DRK_STAGED_MIN_TOKENS 768
 #endif
