@@ -44,8 +44,9 @@ def fused_rope_kv_append_ex(q, k, v, positions, cos, sin, k_cache, v_cache, requ
                             staged_stages=0):
     """fused_rope_kv_append with:
     rotary_dim     rotate only the first rotary_dim dims (table [P, rotary_dim]), copy the rest;
-    pdl            programmatic dependent launch (indices and table read before waiting on the
-                   preceding kernel -- the caller guarantees that kernel does not write them);
+    pdl            programmatic dependent launch (indices, block table and table rows read
+                   before waiting on the preceding kernel -- the caller guarantees that kernel
+                   does not write them);
     strided_cache  caches of any strides with a contiguous last dim, e.g. a head-major
                    [B, Hkv, S, D] cache passed as cache.transpose(1, 2);
     inv_freq       fp32 [rotary_dim/2] device tensor: cos/sin from sincosf in registers

@@ -66,10 +66,11 @@ enum {
 
 /* Launch options (drk_options.flags). */
 enum {
-  /* Launch with programmatic dependent launch: the kernel reads positions, request indices
-   * and the cos/sin rows before waiting on the preceding kernel in the stream, then waits
-   * (griddepcontrol.wait) before it reads q/k/v or writes anything. The caller guarantees the
-   * immediately preceding kernel does not write positions, request indices or the tables. */
+  /* Launch with programmatic dependent launch: the kernel reads positions, request indices,
+   * the block table of a paged cache and the cos/sin rows before waiting on the preceding
+   * kernel in the stream, then waits (griddepcontrol.wait) before it reads q/k/v or writes
+   * anything. The caller guarantees the immediately preceding kernel writes none of those
+   * (positions, request indices, block table, tables). */
   DRK_FLAG_PDL = 1u << 0,
   /* Accept caches with any element strides whose last dim is contiguous (e.g. head-major
    * [B, Hkv, S, D] passed as its [B, S, Hkv, D] transposed view). Without it the cache must be
