@@ -656,9 +656,9 @@ AttentionPlan plan_attention(int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int6
     const int64_t tile = D == 64 ? 256 : 128;
     pl.chunk = (chunk + tile - 1) / tile * tile;
     pl.max_chunks = std::max<int64_t>(1, (S + pl.chunk - 1) / pl.chunk);
-    // Arrival counters of the units, then the persistent grid's unit counter and its count
-    // of CTAs that have finished (the last one resets both).
-    pl.counter_bytes = ((T * Hkv * pl.nhb + 2) * 4 + 255) / 256 * 256;
+    // Arrival counters of the units, then the persistent grid's unit counter (reset by the
+    // grid's last take).
+    pl.counter_bytes = ((T * Hkv * pl.nhb + 1) * 4 + 255) / 256 * 256;
     pl.partial_bytes = T * Hq * pl.max_chunks * (D + 2) * 4;
     return pl;
   }

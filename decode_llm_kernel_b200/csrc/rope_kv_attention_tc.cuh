@@ -613,8 +613,16 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
       int64_t tu = -1, tpos = 0, tri = 0;
       if (lane == 0) {
         while (true) {
-          int64_t u = first_take ? static_cast<int64_t>(blockIdx.x)
-                                 : static_cast<int64_t>(gridDim.x) + atomicAdd(next_unit, 1);
+          int64_t u = static_cast<int64_t>(blockIdx.x);
+          if (!first_take) {
+            const int taken = atomicAdd(next_unit, 1);
+            u = static_cast<int64_t>(gridDim.x) + taken;
+            // Units gridDim.x.. are taken here once each and every CTA's walk ends with one
+            // take past the last unit, so the grid adds `units` times in all: the add that
+            // returns units - 1 is the last, and it leaves the counter at zero for the next
+            // call on this workspace (a walk cut short by a timeout leaves it set).
+            if (taken == static_cast<int>(units) - 1) atomicExch(next_unit, 0);
+          }
           first_take = false;
           if (u >= units) break;
           if (sorted) {
@@ -1291,17 +1299,6 @@ rope_kv_attention_tc_kernel(const __grid_constant__ KernelParams p,
   }
   if (sh.fin_merge) merge_unit(tc_unit_at<kTile>(p, a, sh.fin[0], sh.fin[1], sh.fin[2]), warp,
                                kTcBlock / 32);
-  // Leave the unit counter at zero for the next call on this workspace: every CTA has taken
-  // its last unit before the barrier above, so the last CTA to count its exit here resets the
-  // counter and the exit count (the arrival counters are reset by the CTAs that merge).
-  if (threadIdx.x == 0) {
-    int* unit_counter = a.counters + static_cast<int64_t>(p.T) * p.Hkv * a.nhb;
-    __threadfence();
-    if (atomicAdd(unit_counter + 1, 1) == static_cast<int>(gridDim.x) - 1) {
-      atomicExch(unit_counter, 0);
-      atomicExch(unit_counter + 1, 0);
-    }
-  }
 }
 
 }  // namespace drk

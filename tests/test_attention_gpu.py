@@ -378,7 +378,7 @@ def test_a_zeroed_workspace_stays_zeroed_and_can_skip_the_per_call_zeroing(path,
                                              heads_per_cta=hpc, path=path)
     ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     # the counter region comes first: 40 tokens x 4 KV heads x 1 head block arrival counters
-    # (+ the unit counter and exit count of the tensor-core kernel), rounded up to 768 bytes
+    # (+ the unit counter of the tensor-core kernel), rounded up to 768 bytes
     counters = ws[:768].view(torch.int32)
     for step in range(3):
         pos = (p + step).clamp(max=1023)
