@@ -395,6 +395,28 @@ def test_a_zeroed_workspace_stays_zeroed_and_can_skip_the_per_call_zeroing(path,
         assert int(counters.abs().sum()) == 0, step
 
 
+@pytest.mark.parametrize("T,chunk", [(1, 512), (3, 0)])
+def test_tensor_core_counter_is_reset_when_every_cta_has_one_unit(T, chunk):
+    """With no more units than CTAs, no take past a CTA's first unit succeeds: the unit
+    counter is still back at zero after each call (its last take resets it)."""
+    case = make_case(45, T, 16, 4, 128, 1024, torch.bfloat16)
+    q, k, v, p, cos, sin, kc, vc, ri = [t.cuda() for t in case]
+    nbytes = ops().attention_workspace_bytes(T, 16, 4, 128, 1024, torch.bfloat16, chunk=chunk,
+                                             path="tensor_cores")
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    counters = ws[:256].view(torch.int32)
+    for step in range(2):
+        kc_a, vc_a, kc_b, vc_b = kc.clone(), vc.clone(), kc.clone(), vc.clone()
+        want = ops().fused_rope_kv_append_attention(q, k, v, p, cos, sin, kc_a, vc_a, ri,
+                                                    chunk=chunk, path="tensor_cores")
+        got = ops().fused_rope_kv_append_attention(q, k, v, p, cos, sin, kc_b, vc_b, ri,
+                                                   chunk=chunk, path="tensor_cores",
+                                                   workspace=ws, workspace_zeroed=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), step
+        assert int(counters.abs().sum()) == 0, step
+
+
 def test_workspace_zeroed_needs_a_workspace():
     case = make_case(3, 2, 8, 2, 128, 64, torch.bfloat16)
     args = [t.cuda() for t in case]
